@@ -1,0 +1,175 @@
+/*
+ * latent-attn-b200 -- C ABI of the B200 (sm_100a) MLA decode library.
+ *
+ * Every entry point takes plain pointers and sizes, returns an mla_status_t,
+ * never exits or aborts, never synchronises the host, and is asynchronous on
+ * the given stream. Pointers are device pointers unless a name ends in _host.
+ *
+ * Entry points and the reference interface each one replaces
+ * (anishesg/latent-attn, paths relative to that project):
+ *
+ *   mla_launch_fused          launch_fused_mla(const FusedMLAParams&, cudaStream_t)
+ *                             src/fused_mla.cuh:11-34 (params), :51 (function)
+ *   mla_launch_batched_fused  launch_batched_fused_mla(const BatchedFusedMLAParams&, cudaStream_t)
+ *                             src/fused_mla_batched.cuh:7-30 (params), :35 (function)
+ *   mla_decode                no reference counterpart: the general decode
+ *                             (absorption in-op, variable-length batch, split-KV,
+ *                             caller-provided workspace); it generalises the two
+ *                             launchers above and the caller-side absorption of
+ *                             tests/test_python.py:98-99
+ *   mla_decode_partial /      no reference counterpart: the two halves of the
+ *   mla_combine_partials      KV-range-sharded multi-GPU decode (per-head partial
+ *                             (m, l, o_latent) out of one shard; log-sum-exp merge of
+ *                             G shards' partials + the W_UV projection of
+ *                             src/fused_mla.cu:258-267)
+ *   mla_config_validate       MLAConfig::validate() (src/mla_config.cuh:35-40)
+ */
+#ifndef LATENT_ATTN_B200_MLA_H_
+#define LATENT_ATTN_B200_MLA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MLA_API __attribute__((visibility("default")))
+#else
+#define MLA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Opaque stream handle, ABI-identical to cudaStream_t. */
+typedef struct CUstream_st* mla_stream_t;
+
+typedef enum mla_status {
+  MLA_OK = 0,
+  MLA_ERR_INVALID_ARGUMENT = 1,   /* null pointer, bad size, non-positive dim */
+  MLA_ERR_UNSUPPORTED = 2,        /* valid but not implemented (e.g. odd qk_rope_head_dim) */
+  MLA_ERR_WORKSPACE = 3,          /* workspace pointer null / too small / misaligned */
+  MLA_ERR_CUDA = 4,               /* a CUDA runtime call failed; see mla_last_error() */
+  MLA_ERR_NO_DEVICE_CODE = 5,     /* the library was not built for this GPU (needs sm_100a) */
+  MLA_ERR_TIMEOUT = 6             /* a device-side wait gave up (reported by the kernel) */
+} mla_status_t;
+
+typedef enum mla_dtype {
+  MLA_DTYPE_F16 = 0,
+  MLA_DTYPE_BF16 = 1,
+  MLA_DTYPE_F32 = 2
+} mla_dtype_t;
+
+/* Same field order and types as MLAConfig (src/mla_config.cuh:7-13). */
+typedef struct mla_config {
+  int d_model;            /* not used by the decode op */
+  int kv_lora_rank;       /* d_c */
+  int qk_nope_head_dim;   /* dn */
+  int qk_rope_head_dim;   /* d_R, even */
+  int num_heads;          /* H */
+  int v_head_dim;         /* dv */
+} mla_config_t;
+
+/* MLAConfig::validate(): MLA_ERR_INVALID_ARGUMENT when a dimension is not positive. */
+MLA_API mla_status_t mla_config_validate(const mla_config_t* cfg);
+
+/* Field order of FusedMLAParams (src/fused_mla.cuh:11-34). Element type of
+ * kv_cache / W_UV is given by `dtype` (the reference is fp16-only). */
+typedef struct mla_fused_params {
+  const void* kv_cache;      /* (seq_len, d_c + d_R) packed [c_t | k_rope] */
+  int seq_len;
+  const float* q_absorbed;   /* (H, d_c) fp32 */
+  const float* q_rope;       /* (H, d_R) fp32 */
+  const void* W_UV;          /* (H * dv, d_c) */
+  const float* rope_cos;     /* (seq_len, d_R / 2) fp32 */
+  const float* rope_sin;     /* (seq_len, d_R / 2) fp32 */
+  float* output;             /* (H, dv) fp32 */
+  const mla_config_t* cfg;   /* read during the call only */
+} mla_fused_params_t;
+
+/* Field order of BatchedFusedMLAParams (src/fused_mla_batched.cuh:7-30):
+ * batch_size query tokens attend to ONE shared cache. */
+typedef struct mla_batched_fused_params {
+  const void* kv_cache;      /* (seq_len, d_c + d_R) */
+  int seq_len;
+  int batch_size;
+  const float* q_absorbed;   /* (B, H, d_c) fp32 */
+  const float* q_rope;       /* (B, H, d_R) fp32 */
+  const void* W_UV;          /* (H * dv, d_c) */
+  const float* rope_cos;     /* (seq_len, d_R / 2) fp32 */
+  const float* rope_sin;
+  float* output;             /* (B, H, dv) fp32 */
+  const mla_config_t* cfg;
+} mla_batched_fused_params_t;
+
+/* Drop-in for launch_fused_mla. The reference signature has no workspace, so the
+ * split-KV scratch is taken stream-ordered from the device's default memory
+ * pool (cudaMallocAsync / cudaFreeAsync on `stream`). */
+MLA_API mla_status_t mla_launch_fused(const mla_fused_params_t* p, mla_dtype_t dtype, mla_stream_t stream);
+
+/* Drop-in for launch_batched_fused_mla (same scratch policy). */
+MLA_API mla_status_t mla_launch_batched_fused(const mla_batched_fused_params_t* p, mla_dtype_t dtype,
+                                      mla_stream_t stream);
+
+/* General decode. One query token per sequence (or, with shared_cache, `batch`
+ * tokens over sequence 0). */
+typedef struct mla_decode_args {
+  mla_dtype_t dtype;            /* element type of kv_cache, W_UK, W_UV: F16 or BF16 */
+  int batch;                    /* B >= 1 */
+  int shared_cache;             /* nonzero: all B tokens attend to the same rows (reference batched op) */
+  const void* kv_cache;         /* packed rows [c_t | k_rope] */
+  int64_t kv_row_stride;        /* elements between rows; 0 means d_c + d_R */
+  int64_t kv_total_rows;        /* rows addressable from kv_cache (reads never go past them);
+                                   0: max_seq_len if shared_cache or kv_offsets is NULL and B == 1,
+                                   else batch * max_seq_len when kv_offsets is NULL; required with kv_offsets */
+  const int64_t* kv_offsets;    /* device (B,) first row of sequence b; NULL: b * max_seq_len (0 if shared) */
+  const int* seq_lens;          /* device (B,) positions per sequence; NULL: every sequence has max_seq_len */
+  const int* seq_lens_host;     /* optional host copy of seq_lens (lets the planner skip a device scan) */
+  int max_seq_len;              /* upper bound of seq_lens (>= 1) */
+  int kv_pos_offset;            /* RoPE table row of cache row 0 (KV-range shards); usually 0 */
+  /* queries: q_absorbed, or q_nope together with W_UK (absorption runs in-op) */
+  const float* q_absorbed;      /* (B, H, d_c) fp32, or NULL */
+  const float* q_nope;          /* (B, H, dn) fp32, or NULL */
+  const void* W_UK;             /* (H * dn, d_c), required with q_nope */
+  const float* q_rope;          /* (B, H, d_R) fp32, already rotated to the query position */
+  const void* W_UV;             /* (H * dv, d_c) */
+  const float* rope_cos;        /* (kv_pos_offset + max_seq_len, d_R/2) fp32 */
+  const float* rope_sin;
+  float softmax_scale;          /* 0: 1 / sqrt(dn + d_R) */
+  float* output;                /* (B, H, dv) fp32 */
+  int kernel;                   /* MLA_KERNEL_AUTO (0), MLA_KERNEL_TENSOR_CORE (1), MLA_KERNEL_CUDA_CORE (2) */
+} mla_decode_args_t;
+
+enum { MLA_KERNEL_AUTO = 0, MLA_KERNEL_TENSOR_CORE = 1, MLA_KERNEL_CUDA_CORE = 2 };
+
+/* Bytes of workspace mla_decode needs for these arguments (256-byte aligned). */
+MLA_API mla_status_t mla_decode_workspace_size(const mla_config_t* cfg, const mla_decode_args_t* a,
+                                       size_t* bytes);
+
+MLA_API mla_status_t mla_decode(const mla_config_t* cfg, const mla_decode_args_t* a, void* workspace,
+                        size_t workspace_bytes, mla_stream_t stream);
+
+/* KV-range sharding, step 1: decode over this rank's rows only and write one
+ * partial per (b, h): m (natural-log units), l, and the UNnormalised latent sum
+ * o (d_c floats). partial_ml: (B, H, 2) fp32; partial_o: (B, H, d_c) fp32.
+ * Uses the same workspace as mla_decode (mla_decode_workspace_size). */
+MLA_API mla_status_t mla_decode_partial(const mla_config_t* cfg, const mla_decode_args_t* a,
+                                float* partial_ml, float* partial_o, void* workspace,
+                                size_t workspace_bytes, mla_stream_t stream);
+
+/* KV-range sharding, step 2: merge `num_parts` partial sets laid out
+ * (num_parts, B, H, .) and project through W_UV: output (B, H, dv) fp32. */
+MLA_API mla_status_t mla_combine_partials(const mla_config_t* cfg, mla_dtype_t dtype, int batch,
+                                  int num_parts, const float* partial_ml, const float* partial_o,
+                                  const void* W_UV, float* output, mla_stream_t stream);
+
+/* Thread-local message for the last non-OK status returned on this thread. */
+MLA_API const char* mla_last_error(void);
+
+/* Library build/version string. */
+MLA_API const char* mla_version(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* LATENT_ATTN_B200_MLA_H_ */

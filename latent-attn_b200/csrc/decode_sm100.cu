@@ -1,0 +1,511 @@
+// Tensor-core split-KV MLA decode for sm_100a (tcgen05 MMA, TMEM accumulators, TMA).
+//
+// One worker = a cluster of two CTAs (a "pair") that streams a contiguous range of
+// 64-position tiles (see mla_internal.cuh for the stream-K split). All 128 query
+// rows (heads) of a group form the M = 128 tile, so each cache tile is read from
+// HBM once for every head.
+//
+// The pair splits the 576-wide score reduction and the 512-wide latent output:
+//   CTA 0 owns K = c[0:256] + k_rope[0:64] (320) and output latent columns [0, 256)
+//   CTA 1 owns K = c[256:512]              (256) and output latent columns [256, 512)
+// so each CTA's cache slice serves both of its MMAs from the same shared memory:
+//   score  S_r[128 x 64]  = Q_r(TMEM) . KV_r^T         (K-major B)
+//   latent O_r[128 x 256] += P[128 x 64] . C_r[64 x 256] (P K-major, C MN-major)
+// TMEM per CTA: O_r 256 columns | S 64 | Q_r 160 (CTA 0) or 128 (CTA 1).
+// The full score is S_0 + S_1: each CTA rounds its partial to fp16, ships it to
+// the other CTA's shared memory with st.async (completion counted on the
+// receiver's mbarrier), and both add the same two fp16 halves, so both compute a
+// bit-identical softmax and bit-identical P, m and l.
+//
+// Warp roles (256 threads):
+//   warp 0      TMA producer (one lane): cache tile chunks into a 3-stage ring
+//   warp 1      TMEM allocator + MMA issuer (one lane)
+//   warps 2-3   tile transform: zero rows past the sequence end; CTA 0 also
+//               rotates k_rope in place with the caller's fp32 cos/sin tables
+//               (the rotation of src/fused_mla.cu:34-54 of the reference)
+//   warps 4-7   softmax / correction / epilogue: thread t owns query row t
+// Softmax is online in log2 units (Q is pre-scaled by softmax_scale * log2 e) with
+// a lazy rescale: the running max only moves when a tile's max exceeds it by more
+// than 8, which bounds P by 2^8 and makes the O rescale (TMEM ld/scale/st) rare.
+// Every wait is bounded (mbar_wait*); on timeout the kernel records kStatusTimeout
+// in P.status, unwinds, and the combine kernel turns the outputs into NaN.
+#include <cfloat>
+
+#include "mla_internal.cuh"
+#include "sm100_ptx.cuh"
+#include "tma_host.cuh"
+
+namespace mla {
+using namespace sm100;
+
+namespace {
+
+constexpr int kTileN = 64;                       // positions per tile
+constexpr int kStages = 3;
+constexpr int kChunkBytes = 64 * 128;            // 64 rows x 64 elements (128 B), 128-byte swizzle
+constexpr int kStageBytes = 5 * kChunkBytes;     // CTA 0 uses 5 chunks, CTA 1 uses 4
+constexpr int kPBytes = 128 * 128;               // P: 128 rows x 64 positions x 2 B
+constexpr int kXBytes = 128 * 128;               // exchanged partial score: 128 x 64 fp16
+constexpr int kThreads = 256;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 0, kColS = 256, kColQ = 320;
+constexpr float kRescaleThreshold = 8.0f;        // log2 units
+
+// wait-site codes recorded in the status word's upper bits (debugging aid)
+enum : int { kWaitProducer = 1, kWaitTransform = 2, kWaitMmaTile = 3, kWaitMmaSFree = 4, kWaitMmaP = 5,
+             kWaitMmaQ = 6, kWaitSoftS = 7, kWaitSoftX = 8, kWaitSoftPV = 9, kWaitTeardown = 10,
+             kWaitDrain = 11 };
+
+struct __align__(8) Barriers {
+    uint64_t kv_full[kStages];
+    uint64_t kv_empty[kStages];
+    uint64_t tile_ready[kStages];
+    uint64_t s_full, s_free;
+    uint64_t x_full[2];
+    uint64_t p_full[2];
+    uint64_t pv_done[2];
+    uint64_t q_ready, drain, done;
+    uint32_t tmem_base;
+};
+
+constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 2 * kPBytes + 2 * kXBytes +
+                              sizeof(Barriers) + 1024;
+
+__device__ __forceinline__ int code(int site) { return kStatusTimeout | (site << 8); }
+
+// Walks the worker's tiles; every role advances an identical copy.
+struct TileIter {
+    int t, t_begin, t_end;
+    int g, gt0, gt1, len;
+    long long row0;
+
+    __device__ void load_group(const DecodePlan& P) {
+        gt0 = tile_prefix(P, g);
+        gt1 = tile_prefix(P, g + 1);
+        len = group_len(P, g);
+        row0 = group_kv_row0(P, g);
+    }
+    __device__ void init(const DecodePlan& P, int tb, int te) {
+        t = t_begin = tb;
+        t_end = te;
+        g = group_of_tile(P, tb);
+        load_group(P);
+    }
+    __device__ bool valid() const { return t < t_end; }
+    __device__ int pos0() const { return (t - gt0) * kTileN; }
+    __device__ int np() const { int r = len - pos0(); return r < kTileN ? r : kTileN; }
+    __device__ bool seg_first() const { return t == t_begin || t == gt0; }
+    __device__ bool seg_last() const { return t + 1 == t_end || t + 1 == gt1; }
+    __device__ void next(const DecodePlan& P) {
+        ++t;
+        if (t < t_end && t >= gt1) {
+            ++g;
+            while (g < P.G - 1 && tile_prefix(P, g + 1) <= t) ++g;  // skip empty groups
+            load_group(P);
+        }
+    }
+};
+
+template <typename T> struct MmaFmt;
+template <> struct MmaFmt<__half> { static constexpr uint32_t v = 0; };
+template <> struct MmaFmt<__nv_bfloat16> { static constexpr uint32_t v = 1; };
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) { return pack_half2(a, b); }
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t v) {
+    return ElemTraits<T>::to_f2(*reinterpret_cast<const typename ElemTraits<T>::T2*>(&v));
+}
+
+}  // namespace
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P, const T* __restrict__ qpack,
+                    const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
+                    float* __restrict__ rec_ml, float* __restrict__ rec_o) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    unsigned char* stages = smem;
+    unsigned char* pbuf = stages + kStages * kStageBytes;
+    unsigned char* xbuf = pbuf + 2 * kPBytes;
+    Barriers* bars = reinterpret_cast<Barriers*>(xbuf + 2 * kXBytes);
+
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t peer = rank ^ 1u;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int w = blockIdx.x >> 1;
+    volatile int* err = P.status;
+
+    const int ntiles = total_tiles(P);
+    if (ntiles <= 0 || w >= P.W) return;  // identical for both CTAs of the pair
+    const int tb = worker_begin(ntiles, P.W, w), te = worker_begin(ntiles, P.W, w + 1);
+    if (tb >= te) return;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_u32(&bars->kv_full[s]), 1);
+            mbar_init(smem_u32(&bars->kv_empty[s]), 1);
+            mbar_init(smem_u32(&bars->tile_ready[s]), 64);
+        }
+        mbar_init(smem_u32(&bars->s_full), 1);
+        mbar_init(smem_u32(&bars->s_free), 128);
+        for (int j = 0; j < 2; ++j) {
+            mbar_init(smem_u32(&bars->x_full[j]), 1);
+            mbar_init(smem_u32(&bars->p_full[j]), 128);
+            mbar_init(smem_u32(&bars->pv_done[j]), 1);
+        }
+        mbar_init(smem_u32(&bars->q_ready), 128);
+        mbar_init(smem_u32(&bars->drain), 1);
+        mbar_init(smem_u32(&bars->done), 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&bars->tmem_base), kTmemCols);
+        tmem_relinquish();
+    }
+    if (warp == 0 && lane == 0) tma_prefetch_desc(&tmap);
+    tc_fence_before();
+    cluster_sync();  // both CTAs: barriers initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tbase = bars->tmem_base;
+
+    const int nchunks = rank == 0 ? 5 : 4;
+    const int ksteps = rank == 0 ? 20 : 16;   // score K / 16
+    const uint32_t stages_u32 = smem_u32(stages);
+    const uint32_t pbuf_u32 = smem_u32(pbuf);
+    const uint32_t xbuf_u32 = smem_u32(xbuf);
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            TileIter it;
+            it.init(P, tb, te);
+            for (int i = 0; it.valid(); ++i, it.next(P)) {
+                const int st = i % kStages;
+                if (i >= kStages &&
+                    !mbar_wait(smem_u32(&bars->kv_empty[st]), ((i / kStages) - 1) & 1, err, code(kWaitProducer)))
+                    break;
+                const uint32_t full = smem_u32(&bars->kv_full[st]);
+                mbar_arrive_expect_tx(full, nchunks * kChunkBytes);
+                const int y = static_cast<int>(it.row0 + it.pos0());
+                const uint32_t dst = stages_u32 + st * kStageBytes;
+                for (int j = 0; j < nchunks; ++j) {
+                    const int x = rank == 0 ? (j < 4 ? 64 * j : 512) : 256 + 64 * j;
+                    tma_load_2d(dst + j * kChunkBytes, &tmap, full, x, y);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t fmt = MmaFmt<T>::v;
+            constexpr uint32_t idesc_s = idesc_f16(128, kTileN, fmt, false, false);
+            constexpr uint32_t idesc_pv = idesc_f16(128, 256, fmt, false, true);
+            bool ok = true;
+            auto issue_score = [&](int i) {
+                const uint32_t sa = stages_u32 + (i % kStages) * kStageBytes;
+                for (int k = 0; k < ksteps; ++k) {
+                    const uint64_t bd = smem_desc_sw128(sa + (k >> 2) * kChunkBytes + (k & 3) * 32, 16, 1024);
+                    mma_ts(tbase + kColS, tbase + kColQ + 8 * k, bd, idesc_s, k > 0 ? 1u : 0u);
+                }
+                mma_commit(smem_u32(&bars->s_full));
+            };
+            auto issue_pv = [&](int i, bool first) {
+                const uint32_t sa = stages_u32 + (i % kStages) * kStageBytes;
+                const uint32_t pa = pbuf_u32 + (i & 1) * kPBytes;
+                for (int k = 0; k < kTileN / 16; ++k) {
+                    const uint64_t ad = smem_desc_sw128(pa + 32 * k, 16, 1024);
+                    const uint64_t bd = smem_desc_sw128(sa + 2048 * k, 8192, 1024);
+                    mma_ss(tbase + kColO, ad, bd, idesc_pv, (first && k == 0) ? 0u : 1u);
+                }
+                mma_commit(smem_u32(&bars->pv_done[i & 1]));
+                mma_commit(smem_u32(&bars->kv_empty[i % kStages]));
+            };
+            auto wait_tile = [&](int i) {
+                return mbar_wait(smem_u32(&bars->tile_ready[i % kStages]), (i / kStages) & 1, err,
+                                 code(kWaitMmaTile));
+            };
+            TileIter it;
+            it.init(P, tb, te);
+            int seg = 0;
+            ok = mbar_wait(smem_u32(&bars->q_ready), 0, err, code(kWaitMmaQ)) && wait_tile(0);
+            if (ok) {
+                tc_fence_after();
+                issue_score(0);
+            }
+            for (int i = 0; ok && it.valid(); ++i) {
+                TileIter nx = it;
+                nx.next(P);
+                const bool has_next = nx.valid();
+                const bool next_new_seg = has_next && nx.seg_first();
+                if (has_next && !next_new_seg) {
+                    ok = mbar_wait(smem_u32(&bars->s_free), i & 1, err, code(kWaitMmaSFree)) && wait_tile(i + 1);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_score(i + 1);
+                }
+                ok = mbar_wait(smem_u32(&bars->p_full[i & 1]), (i >> 1) & 1, err, code(kWaitMmaP));
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv(i, it.seg_first());
+                if (next_new_seg) {
+                    ++seg;
+                    ok = mbar_wait(smem_u32(&bars->q_ready), seg & 1, err, code(kWaitMmaQ)) &&
+                         mbar_wait(smem_u32(&bars->s_free), i & 1, err, code(kWaitMmaSFree)) && wait_tile(i + 1);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_score(i + 1);
+                }
+                it = nx;
+            }
+            // drain: every MMA this thread issued has completed before teardown
+            mma_commit(smem_u32(&bars->drain));
+            mbar_wait(smem_u32(&bars->drain), 0, err, code(kWaitDrain));
+        }
+    } else if (warp < 4) {
+        // ------------------------------------------------------------ tile transform
+        const int tt = threadIdx.x - 64;  // 0..63
+        TileIter it;
+        it.init(P, tb, te);
+        for (int i = 0; it.valid(); ++i, it.next(P)) {
+            const int st = i % kStages;
+            if (!mbar_wait(smem_u32(&bars->kv_full[st]), (i / kStages) & 1, err, code(kWaitTransform))) break;
+            unsigned char* sp = stages + st * kStageBytes;
+            const int np = it.np();
+            if (np < kTileN) {
+                // zero whole rows past the sequence end (swizzle permutes within a row only)
+                const int rows = kTileN - np;
+                for (int v = tt; v < nchunks * rows * 8; v += 64) {
+                    const int j = v / (rows * 8), rem = v % (rows * 8);
+                    const int r = np + rem / 8, c = rem % 8;
+                    *reinterpret_cast<uint4*>(sp + j * kChunkBytes + r * 128 + c * 16) = make_uint4(0, 0, 0, 0);
+                }
+            }
+            if (rank == 0) {
+                // rotate-half RoPE on the k_rope chunk: pairs (d, d + 32), d = lane
+                unsigned char* rc = sp + 4 * kChunkBytes;
+                const long long pbase = static_cast<long long>(P.kv_pos_offset) + it.pos0();
+                const int d = lane;
+                const int sub = warp - 2;
+#pragma unroll 4
+                for (int p = sub; p < np; p += 2) {
+                    const long long pos = pbase + p;
+                    const float cs = __ldg(rope_cos + pos * 32 + d);
+                    const float sn = __ldg(rope_sin + pos * 32 + d);
+                    T* e0 = reinterpret_cast<T*>(rc + p * 128 + ((((d >> 3)) ^ (p & 7)) << 4) + ((d & 7) << 1));
+                    T* e1 = reinterpret_cast<T*>(rc + p * 128 + ((((d >> 3) + 4) ^ (p & 7)) << 4) + ((d & 7) << 1));
+                    const float k0 = ElemTraits<T>::to_f(*e0), k1 = ElemTraits<T>::to_f(*e1);
+                    *e0 = ElemTraits<T>::from_f(k0 * cs - k1 * sn);
+                    *e1 = ElemTraits<T>::from_f(k0 * sn + k1 * cs);
+                }
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(smem_u32(&bars->tile_ready[st]));
+        }
+    } else {
+        // ------------------------------------------------------------ softmax warpgroup
+        const int t = threadIdx.x - 128;                       // query row
+        const uint32_t lane_off = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+        const uint32_t taddr_row = tbase + lane_off;
+        const int ncol_q = rank == 0 ? 160 : 128;
+        auto load_q = [&](int g) {
+            const uint32_t* src = reinterpret_cast<const uint32_t*>(qpack + (static_cast<long long>(g) * 128 + t) * 576);
+            for (int c = 0; c < ncol_q; c += 32) {
+                const int e0 = rank == 0 ? (c < 128 ? 2 * c : 512 + 2 * (c - 128)) : 256 + 2 * c;
+                uint32_t r[32];
+                const uint4* s4 = reinterpret_cast<const uint4*>(src + e0 / 2);
+#pragma unroll
+                for (int v = 0; v < 8; ++v) {
+                    uint4 x = __ldg(s4 + v);
+                    r[4 * v] = x.x; r[4 * v + 1] = x.y; r[4 * v + 2] = x.z; r[4 * v + 3] = x.w;
+                }
+                tmem_st32(taddr_row + kColQ + c, r);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(smem_u32(&bars->q_ready));
+        };
+
+        TileIter it;
+        it.init(P, tb, te);
+        load_q(it.g);
+        float m_run = 0.f, l_run = 0.f;
+        const uint32_t x_row_local = xbuf_u32 + t * 128;
+        const uint32_t x_row_remote = mapa(x_row_local, peer);
+        const uint32_t p_row = pbuf_u32 + t * 128;
+        const int sw = t & 7;
+        for (int i = 0; it.valid(); ++i, it.next(P)) {
+            const int slot = i & 1;
+            if (t == 0) mbar_arrive_expect_tx(smem_u32(&bars->x_full[slot]), kXBytes);
+            if (!mbar_wait(smem_u32(&bars->s_full), i & 1, err, code(kWaitSoftS))) break;
+            tc_fence_after();
+            uint32_t sr[64];
+            tmem_ld32(taddr_row + kColS, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+            tmem_ld32(taddr_row + kColS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+            tmem_ld_wait();
+            tc_fence_before();
+            mbar_arrive(smem_u32(&bars->s_free));
+
+            // own partial -> fp16, ship to the peer (chunk c holds positions 8c..8c+7)
+            uint32_t h[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) h[j] = pack_half2(__uint_as_float(sr[2 * j]), __uint_as_float(sr[2 * j + 1]));
+            const uint32_t rbar = mapa(smem_u32(&bars->x_full[slot]), peer);
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                st_async_v4(x_row_remote + slot * kXBytes + ((c ^ sw) << 4), h[4 * c], h[4 * c + 1], h[4 * c + 2],
+                            h[4 * c + 3], rbar);
+            if (!mbar_wait_cluster(smem_u32(&bars->x_full[slot]), (i >> 1) & 1, err, code(kWaitSoftX))) break;
+
+            // full score = fp16(own) + fp16(peer), identical in both CTAs
+            float s[64];
+            const int np = it.np();
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint4 v;
+                asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                             : "r"(x_row_local + slot * kXBytes + ((c ^ sw) << 4)));
+                const uint32_t pv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&h[4 * c + q]));
+                    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&pv[q]));
+                    const int j = 8 * c + 2 * q;
+                    s[j] = j < np ? a.x + b.x : -INFINITY;
+                    s[j + 1] = j + 1 < np ? a.y + b.y : -INFINITY;
+                }
+            }
+            float mt = s[0];
+#pragma unroll
+            for (int j = 1; j < 64; ++j) mt = fmaxf(mt, s[j]);
+            float alpha = 1.f;
+            bool need = false;
+            const bool first = it.seg_first();
+            if (first) {
+                m_run = mt;
+                l_run = 0.f;
+            } else if (mt > m_run + kRescaleThreshold) {
+                alpha = exp2f(m_run - mt);
+                m_run = mt;
+                l_run *= alpha;
+                need = true;
+            }
+            uint32_t pp[32];
+            float lsum = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const uint32_t v = pack2<T>(exp2f(s[2 * j] - m_run), exp2f(s[2 * j + 1] - m_run));
+                pp[j] = v;
+                const float2 f = unpack2<T>(v);
+                lsum += f.x + f.y;
+            }
+            l_run += lsum;
+            // P slot is free once PV(i-2) has completed
+            if (i >= 2 && !mbar_wait(smem_u32(&bars->pv_done[slot]), ((i - 2) >> 1) & 1, err, code(kWaitSoftPV)))
+                break;
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(p_row + slot * kPBytes + ((c ^ sw) << 4)),
+                             "r"(pp[4 * c]), "r"(pp[4 * c + 1]), "r"(pp[4 * c + 2]), "r"(pp[4 * c + 3])
+                             : "memory");
+            fence_proxy_async_smem();
+            if (__any_sync(0xffffffffu, need)) {
+                // rescale this warp's O rows once PV(i-1) has completed
+                if (!mbar_wait(smem_u32(&bars->pv_done[(i - 1) & 1]), ((i - 1) >> 1) & 1, err, code(kWaitSoftPV)))
+                    break;
+                tc_fence_after();
+#pragma unroll 1
+                for (int c0 = 0; c0 < 256; c0 += 32) {
+                    uint32_t o[32];
+                    tmem_ld32(taddr_row + kColO + c0, o);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+                    tmem_st32(taddr_row + kColO + c0, o);
+                }
+                tmem_st_wait();
+            }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&bars->p_full[slot]));
+
+            if (it.seg_last()) {
+                if (!mbar_wait(smem_u32(&bars->pv_done[slot]), (i >> 1) & 1, err, code(kWaitSoftPV))) break;
+                tc_fence_after();
+                const int rec = it.g + w;
+                const bool row_ok = t < group_rows(P, it.g);
+                float* orow = rec_o + (static_cast<long long>(rec) * kGroupRows + t) * 512 + 256 * rank;
+#pragma unroll 1
+                for (int c0 = 0; c0 < 256; c0 += 32) {
+                    uint32_t o[32];
+                    tmem_ld32(taddr_row + kColO + c0, o);
+                    tmem_ld_wait();
+                    if (row_ok) {
+#pragma unroll
+                        for (int v = 0; v < 8; ++v)
+                            *reinterpret_cast<float4*>(orow + c0 + 4 * v) =
+                                make_float4(__uint_as_float(o[4 * v]), __uint_as_float(o[4 * v + 1]),
+                                            __uint_as_float(o[4 * v + 2]), __uint_as_float(o[4 * v + 3]));
+                    }
+                }
+                if (rank == 0 && row_ok)
+                    *reinterpret_cast<float2*>(rec_ml + (static_cast<long long>(rec) * kGroupRows + t) * 2) =
+                        make_float2(m_run, l_run);
+                tc_fence_before();
+                if (it.t + 1 < it.t_end) {
+                    TileIter nx = it;
+                    nx.next(P);
+                    load_q(nx.g);
+                }
+            }
+        }
+    }
+
+    // ---------------------------------------------------------------- teardown
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // the pair finishes together: no CTA leaves while the other may still address it
+        mbar_arrive_remote(mapa(smem_u32(&bars->done), peer));
+        mbar_wait_cluster(smem_u32(&bars->done), 0, err, code(kWaitTeardown));
+    }
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tbase, kTmemCols);
+}
+
+bool decode_sm100_available() { return true; }
+
+template <typename T>
+cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
+                                const float* sin, float* rec_ml, float* rec_o, cudaStream_t s) {
+    if (P.dc != 512 || P.dR != 64 || P.tile != kTileN) return cudaErrorInvalidValue;
+    CUtensorMap tmap;
+    if (!make_tmap_2d_16b(&tmap, kv, static_cast<uint64_t>(P.kv_rows), 576, static_cast<uint64_t>(P.row_stride),
+                          64, 64))
+        return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(decode_sm100_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) return e;
+    decode_sm100_kernel<T><<<2 * P.W, kThreads, kSmemBytes, s>>>(tmap, P, qpack, cos, sin, rec_ml, rec_o);
+    return cudaGetLastError();
+}
+
+template cudaError_t launch_decode_sm100<__half>(const DecodePlan&, const __half*, const __half*, const float*,
+                                                 const float*, float*, float*, cudaStream_t);
+template cudaError_t launch_decode_sm100<__nv_bfloat16>(const DecodePlan&, const __nv_bfloat16*,
+                                                        const __nv_bfloat16*, const float*, const float*, float*,
+                                                        float*, cudaStream_t);
+
+}  // namespace mla

@@ -1,0 +1,368 @@
+// C ABI implementation: argument validation, work planning, workspace layout and
+// the launch sequence  pack(Q) -> decode(split-KV partial records) -> combine(+W_UV).
+//
+// Error behaviour mirrors the reference's layers: configuration errors are the
+// conditions of MLAConfig::validate (src/mla_config.cuh:35-40), shape/pointer
+// errors those the torch binding rejects (csrc/bindings.cpp:28-40, 146-152,
+// 208-221); here they become status codes with a thread-local message instead of
+// exceptions, and nothing ever exits, aborts or synchronises the host.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "latent_attn_b200/mla.h"
+#include "mla_internal.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+mla_status_t fail(mla_status_t s, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return s;
+}
+
+mla_status_t cuda_fail(cudaError_t e, const char* what) {
+    return fail(MLA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct DeviceInfo {
+    int sms = 0, major = 0, minor = 0;
+};
+
+bool device_info(DeviceInfo* out) {
+    static std::mutex mu;
+    static std::vector<DeviceInfo> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    std::lock_guard<std::mutex> lk(mu);
+    if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1);
+    DeviceInfo& d = cache[dev];
+    if (d.sms == 0) {
+        if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+            d.sms = 0;
+            return false;
+        }
+    }
+    *out = d;
+    return true;
+}
+
+// LATENT_ATTN_B200_PATH = "simt" | "tc" overrides the automatic kernel choice.
+int env_path_override() {
+    static int v = [] {
+        const char* s = std::getenv("LATENT_ATTN_B200_PATH");
+        if (!s) return 0;
+        if (!std::strcmp(s, "tc")) return 1;
+        if (!std::strcmp(s, "simt")) return 2;
+        return 0;
+    }();
+    return v;
+}
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+struct Plan {
+    mla::DecodePlan dp;
+    bool use_tc = false;
+    size_t off_prefix = 0, off_qpack = 0, off_rec_ml = 0, off_rec_o = 0, off_status = 0, total = 0;
+    float q_scale = 0.f;
+    int nrec = 0;
+};
+
+mla_status_t validate_cfg(const mla_config_t* c) {
+    if (!c) return fail(MLA_ERR_INVALID_ARGUMENT, "cfg is null");
+    if (c->kv_lora_rank <= 0 || c->qk_nope_head_dim <= 0 || c->qk_rope_head_dim <= 0)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "MLA dims must be positive");
+    if (c->num_heads <= 0 || c->v_head_dim <= 0)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "num_heads and v_head_dim must be positive");
+    return MLA_OK;
+}
+
+mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan* p) {
+    mla_status_t st = validate_cfg(cfg);
+    if (st != MLA_OK) return st;
+    if (!a) return fail(MLA_ERR_INVALID_ARGUMENT, "args is null");
+    const int dc = cfg->kv_lora_rank, dR = cfg->qk_rope_head_dim, H = cfg->num_heads;
+    const int dn = cfg->qk_nope_head_dim, dv = cfg->v_head_dim;
+    if (a->dtype != MLA_DTYPE_F16 && a->dtype != MLA_DTYPE_BF16)
+        return fail(MLA_ERR_UNSUPPORTED, "dtype must be F16 or BF16 (got %d)", static_cast<int>(a->dtype));
+    if (dR % 2 != 0) return fail(MLA_ERR_UNSUPPORTED, "qk_rope_head_dim must be even (got %d)", dR);
+    if (dc % 32 != 0 || dc > 1024)
+        return fail(MLA_ERR_UNSUPPORTED, "kv_lora_rank must be a multiple of 32 and <= 1024 (got %d)", dc);
+    if (dR > 256) return fail(MLA_ERR_UNSUPPORTED, "qk_rope_head_dim must be <= 256 (got %d)", dR);
+    if (dv > 256) return fail(MLA_ERR_UNSUPPORTED, "v_head_dim must be <= 256 (got %d)", dv);
+    if (a->batch <= 0) return fail(MLA_ERR_INVALID_ARGUMENT, "batch_size must be positive, got %d", a->batch);
+    if (a->max_seq_len <= 0) return fail(MLA_ERR_INVALID_ARGUMENT, "max_seq_len must be positive, got %d", a->max_seq_len);
+    if (a->kv_pos_offset < 0) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_pos_offset must be >= 0");
+    if (!a->kv_cache) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_cache is null");
+    if (!a->q_rope) return fail(MLA_ERR_INVALID_ARGUMENT, "q_rope is null");
+    if (!a->W_UV) return fail(MLA_ERR_INVALID_ARGUMENT, "W_UV is null");
+    if (!a->rope_cos || !a->rope_sin) return fail(MLA_ERR_INVALID_ARGUMENT, "rope_cos / rope_sin are null");
+    if (!a->q_absorbed && !(a->q_nope && a->W_UK))
+        return fail(MLA_ERR_INVALID_ARGUMENT, "give q_absorbed, or q_nope together with W_UK");
+    const int64_t stride = a->kv_row_stride ? a->kv_row_stride : (dc + dR);
+    if (stride < dc + dR) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_row_stride %lld < d_c + d_R", (long long)stride);
+    if (stride % 8 != 0 || stride > (1 << 30))
+        return fail(MLA_ERR_UNSUPPORTED, "kv_row_stride must be a multiple of 8 elements (got %lld)", (long long)stride);
+    if (reinterpret_cast<uintptr_t>(a->kv_cache) % 16 != 0)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "kv_cache must be 16-byte aligned");
+    if (a->shared_cache && a->kv_offsets)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "kv_offsets must be null with shared_cache");
+
+    mla::DecodePlan& d = p->dp;
+    std::memset(&d, 0, sizeof(d));
+    d.dc = dc; d.dR = dR; d.H = H; d.dn = dn; d.dv = dv;
+    d.row_stride = static_cast<int>(stride);
+    d.B = a->batch;
+    d.shared = a->shared_cache ? 1 : 0;
+    d.head_blocks = mla::ceil_div(H, mla::kGroupRows);
+    if (d.shared) {
+        long long rows = static_cast<long long>(a->batch) * H;
+        d.G = static_cast<int>((rows + mla::kGroupRows - 1) / mla::kGroupRows);
+    } else {
+        d.G = a->batch * d.head_blocks;
+    }
+    d.max_len = a->max_seq_len;
+    d.kv_offsets = a->kv_offsets;
+    d.kv_pos_offset = a->kv_pos_offset;
+    if (a->kv_total_rows < 0) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_total_rows must be >= 0");
+    if (a->kv_total_rows > 0) d.kv_rows = a->kv_total_rows;
+    else if (a->kv_offsets) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_total_rows is required with kv_offsets");
+    else d.kv_rows = d.shared ? a->max_seq_len : static_cast<long long>(a->batch) * a->max_seq_len;
+    const bool uniform = a->seq_lens == nullptr || d.shared;
+    if (d.shared && a->seq_lens)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "seq_lens must be null with shared_cache (one sequence)");
+    d.uniform_len = uniform ? a->max_seq_len : 0;
+    d.seq_lens = a->seq_lens;
+
+    DeviceInfo di;
+    if (!device_info(&di)) return fail(MLA_ERR_CUDA, "no CUDA device");
+    const bool tc_shape = dc == 512 && dR == 64;
+    bool use_tc = tc_shape && di.major == 10 && mla::decode_sm100_available();
+    int ov = a->kernel != MLA_KERNEL_AUTO ? a->kernel : env_path_override();
+    if (ov == 2) use_tc = false;
+    if (ov == 1) {
+        if (!tc_shape || di.major != 10 || !mla::decode_sm100_available())
+            return fail(MLA_ERR_UNSUPPORTED, "tensor-core path forced but unavailable for this shape/device");
+        use_tc = true;
+    }
+    p->use_tc = use_tc;
+    d.tile = use_tc ? 64 : 32;
+
+    // tiles, if known on the host
+    long long T = -1;
+    if (uniform) {
+        T = static_cast<long long>(d.G) * mla::ceil_div(a->max_seq_len, d.tile);
+    } else if (a->seq_lens_host) {
+        T = 0;
+        for (int b = 0; b < a->batch; ++b) {
+            int L = a->seq_lens_host[b];
+            if (L < 0 || L > a->max_seq_len)
+                return fail(MLA_ERR_INVALID_ARGUMENT, "seq_lens[%d]=%d outside [0, max_seq_len=%d]", b, L, a->max_seq_len);
+            T += static_cast<long long>(d.head_blocks) * mla::ceil_div(L, d.tile);
+        }
+    }
+    if (T > (1LL << 30)) return fail(MLA_ERR_UNSUPPORTED, "too many positions");
+    int cap = use_tc ? di.sms / 2 : 64;
+    if (cap < 1) cap = 1;
+    int W = cap;
+    if (T >= 0 && T < W) W = T > 0 ? static_cast<int>(T) : 1;
+    d.W = W;
+    p->nrec = d.G + W - 1;
+
+    size_t off = 0;
+    p->off_status = off; off = align_up(off + sizeof(int) * 4);
+    p->off_prefix = off; off = align_up(off + sizeof(int) * (static_cast<size_t>(d.G) + 1));
+    p->off_qpack = off;
+    off = align_up(off + static_cast<size_t>(d.G) * mla::kGroupRows * (dc + dR) * 2);
+    p->off_rec_ml = off;
+    off = align_up(off + static_cast<size_t>(p->nrec) * mla::kGroupRows * 2 * sizeof(float));
+    p->off_rec_o = off;
+    off = align_up(off + static_cast<size_t>(p->nrec) * mla::kGroupRows * dc * sizeof(float));
+    p->total = off;
+
+    float scale = a->softmax_scale > 0.f ? a->softmax_scale : 1.0f / std::sqrt(static_cast<float>(dn + dR));
+    p->q_scale = scale * 1.4426950408889634f;  // log2(e): scores in log2 units
+    return MLA_OK;
+}
+
+template <typename T>
+mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned char* ws, float* out,
+                        float* part_ml, float* part_o, cudaStream_t s) {
+    mla::DecodePlan d = pl.dp;
+    int* prefix = reinterpret_cast<int*>(ws + pl.off_prefix);
+    d.tile_prefix = d.uniform_len > 0 ? nullptr : prefix;
+    d.status = reinterpret_cast<int*>(ws + pl.off_status);
+    T* qpack = reinterpret_cast<T*>(ws + pl.off_qpack);
+    float* rec_ml = reinterpret_cast<float*>(ws + pl.off_rec_ml);
+    float* rec_o = reinterpret_cast<float*>(ws + pl.off_rec_o);
+    cudaError_t e = cudaMemsetAsync(d.status, 0, sizeof(int), s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
+    e = mla::launch_pack_q<T>(d, a->q_absorbed, a->q_absorbed ? nullptr : a->q_nope,
+                              reinterpret_cast<const T*>(a->W_UK), a->q_rope, pl.q_scale, qpack,
+                              d.uniform_len > 0 ? nullptr : prefix, s);
+    if (e != cudaSuccess) return cuda_fail(e, "pack kernel launch");
+    const T* kv = reinterpret_cast<const T*>(a->kv_cache);
+    if (pl.use_tc)
+        e = mla::launch_decode_sm100<T>(d, kv, qpack, a->rope_cos, a->rope_sin, rec_ml, rec_o, s);
+    else
+        e = mla::launch_decode_simt<T>(d, kv, qpack, a->rope_cos, a->rope_sin, rec_ml, rec_o, s);
+    if (e == cudaErrorNoKernelImageForDevice || e == cudaErrorInvalidDeviceFunction)
+        return fail(MLA_ERR_NO_DEVICE_CODE, "decode kernel: %s (library is built for sm_100a)", cudaGetErrorString(e));
+    if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
+    e = mla::launch_combine<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, part_ml, part_o, s);
+    if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
+    return MLA_OK;
+}
+
+mla_status_t decode_impl(const mla_config_t* cfg, const mla_decode_args_t* a, void* workspace,
+                         size_t ws_bytes, float* out, float* part_ml, float* part_o, cudaStream_t s) {
+    Plan pl;
+    mla_status_t st = make_plan(cfg, a, &pl);
+    if (st != MLA_OK) return st;
+    if (!workspace) return fail(MLA_ERR_WORKSPACE, "workspace is null");
+    if (reinterpret_cast<uintptr_t>(workspace) % kAlign != 0)
+        return fail(MLA_ERR_WORKSPACE, "workspace must be %zu-byte aligned", kAlign);
+    if (ws_bytes < pl.total)
+        return fail(MLA_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", ws_bytes, pl.total);
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    if (a->dtype == MLA_DTYPE_BF16) return run_decode<__nv_bfloat16>(pl, a, ws, out, part_ml, part_o, s);
+    return run_decode<__half>(pl, a, ws, out, part_ml, part_o, s);
+}
+
+// Scratch for the reference-shaped launchers, whose signatures carry no workspace.
+mla_status_t decode_with_pool(const mla_config_t* cfg, const mla_decode_args_t* a, cudaStream_t s) {
+    Plan pl;
+    mla_status_t st = make_plan(cfg, a, &pl);
+    if (st != MLA_OK) return st;
+    void* ws = nullptr;
+    cudaError_t e = cudaMallocAsync(&ws, pl.total, s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(workspace)");
+    st = decode_impl(cfg, a, ws, pl.total, a->output, nullptr, nullptr, s);
+    e = cudaFreeAsync(ws, s);
+    if (st == MLA_OK && e != cudaSuccess) return cuda_fail(e, "cudaFreeAsync(workspace)");
+    return st;
+}
+
+}  // namespace
+
+extern "C" {
+
+mla_status_t mla_config_validate(const mla_config_t* cfg) { return validate_cfg(cfg); }
+
+mla_status_t mla_decode_workspace_size(const mla_config_t* cfg, const mla_decode_args_t* a, size_t* bytes) {
+    if (!bytes) return fail(MLA_ERR_INVALID_ARGUMENT, "bytes is null");
+    Plan pl;
+    mla_status_t st = make_plan(cfg, a, &pl);
+    if (st != MLA_OK) return st;
+    *bytes = pl.total;
+    return MLA_OK;
+}
+
+mla_status_t mla_decode(const mla_config_t* cfg, const mla_decode_args_t* a, void* workspace,
+                        size_t workspace_bytes, mla_stream_t stream) {
+    if (!a) return fail(MLA_ERR_INVALID_ARGUMENT, "args is null");
+    if (!a->output) return fail(MLA_ERR_INVALID_ARGUMENT, "output is null");
+    return decode_impl(cfg, a, workspace, workspace_bytes, a->output, nullptr, nullptr,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+mla_status_t mla_decode_partial(const mla_config_t* cfg, const mla_decode_args_t* a, float* partial_ml,
+                                float* partial_o, void* workspace, size_t workspace_bytes,
+                                mla_stream_t stream) {
+    if (!partial_ml || !partial_o) return fail(MLA_ERR_INVALID_ARGUMENT, "partial outputs are null");
+    return decode_impl(cfg, a, workspace, workspace_bytes, nullptr, partial_ml, partial_o,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+mla_status_t mla_combine_partials(const mla_config_t* cfg, mla_dtype_t dtype, int batch, int num_parts,
+                                  const float* partial_ml, const float* partial_o, const void* W_UV,
+                                  float* output, mla_stream_t stream) {
+    mla_status_t st = validate_cfg(cfg);
+    if (st != MLA_OK) return st;
+    if (batch <= 0 || num_parts <= 0) return fail(MLA_ERR_INVALID_ARGUMENT, "batch and num_parts must be positive");
+    if (!partial_ml || !partial_o || !W_UV || !output) return fail(MLA_ERR_INVALID_ARGUMENT, "null pointer");
+    if (cfg->kv_lora_rank > 1024 || cfg->v_head_dim > 256)
+        return fail(MLA_ERR_UNSUPPORTED, "kv_lora_rank <= 1024 and v_head_dim <= 256 required");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    if (dtype == MLA_DTYPE_BF16)
+        e = mla::launch_combine_parts<__nv_bfloat16>(batch, cfg->num_heads, cfg->kv_lora_rank, cfg->v_head_dim,
+                                                     num_parts, partial_ml, partial_o,
+                                                     static_cast<const __nv_bfloat16*>(W_UV), output, s);
+    else if (dtype == MLA_DTYPE_F16)
+        e = mla::launch_combine_parts<__half>(batch, cfg->num_heads, cfg->kv_lora_rank, cfg->v_head_dim,
+                                              num_parts, partial_ml, partial_o,
+                                              static_cast<const __half*>(W_UV), output, s);
+    else
+        return fail(MLA_ERR_UNSUPPORTED, "dtype must be F16 or BF16");
+    if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
+    return MLA_OK;
+}
+
+mla_status_t mla_launch_fused(const mla_fused_params_t* p, mla_dtype_t dtype, mla_stream_t stream) {
+    if (!p) return fail(MLA_ERR_INVALID_ARGUMENT, "params is null");
+    mla_status_t st = validate_cfg(p->cfg);
+    if (st != MLA_OK) return st;
+    if (!p->output) return fail(MLA_ERR_INVALID_ARGUMENT, "output is null");
+    if (!p->q_absorbed) return fail(MLA_ERR_INVALID_ARGUMENT, "q_absorbed is null");
+    if (p->seq_len <= 0) return fail(MLA_ERR_INVALID_ARGUMENT, "seq_len must be positive, got %d", p->seq_len);
+    mla_decode_args_t a;
+    std::memset(&a, 0, sizeof(a));
+    a.dtype = dtype;
+    a.batch = 1;
+    a.kv_cache = p->kv_cache;
+    a.max_seq_len = p->seq_len;
+    a.q_absorbed = p->q_absorbed;
+    a.q_rope = p->q_rope;
+    a.W_UV = p->W_UV;
+    a.rope_cos = p->rope_cos;
+    a.rope_sin = p->rope_sin;
+    a.output = p->output;
+    return decode_with_pool(p->cfg, &a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+mla_status_t mla_launch_batched_fused(const mla_batched_fused_params_t* p, mla_dtype_t dtype,
+                                      mla_stream_t stream) {
+    if (!p) return fail(MLA_ERR_INVALID_ARGUMENT, "params is null");
+    mla_status_t st = validate_cfg(p->cfg);
+    if (st != MLA_OK) return st;
+    if (!p->output) return fail(MLA_ERR_INVALID_ARGUMENT, "output is null");
+    if (!p->q_absorbed) return fail(MLA_ERR_INVALID_ARGUMENT, "q_absorbed is null");
+    if (p->seq_len <= 0) return fail(MLA_ERR_INVALID_ARGUMENT, "seq_len must be positive, got %d", p->seq_len);
+    if (p->batch_size <= 0) return fail(MLA_ERR_INVALID_ARGUMENT, "batch_size must be positive, got %d", p->batch_size);
+    mla_decode_args_t a;
+    std::memset(&a, 0, sizeof(a));
+    a.dtype = dtype;
+    a.batch = p->batch_size;
+    a.shared_cache = 1;
+    a.kv_cache = p->kv_cache;
+    a.max_seq_len = p->seq_len;
+    a.q_absorbed = p->q_absorbed;
+    a.q_rope = p->q_rope;
+    a.W_UV = p->W_UV;
+    a.rope_cos = p->rope_cos;
+    a.rope_sin = p->rope_sin;
+    a.output = p->output;
+    return decode_with_pool(p->cfg, &a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+const char* mla_last_error(void) { return g_last_error.c_str(); }
+
+const char* mla_version(void) { return "latent-attn-b200 0.1 (sm_100a)"; }
+
+}  // extern "C"

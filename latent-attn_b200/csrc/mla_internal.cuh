@@ -1,0 +1,159 @@
+// Internal definitions shared by the decode, pack and combine kernels.
+//
+// Work decomposition (all decode kernels):
+//   * A "group" is up to 128 query rows that attend to one KV sequence. With one
+//     query token per sequence (single / variable-length batch) a group is the
+//     heads [128k, 128k+128) of sequence b; with a shared cache (the reference's
+//     batched op, src/fused_mla_batched.cuh:5-11) the B*H rows (token, head) are
+//     flattened and cut into groups of 128 that all read sequence 0.
+//   * Each group's positions are cut into tiles of TILE positions. The tiles of
+//     all groups are concatenated (tile_prefix) and split evenly over W workers
+//     ("stream-K"): worker w owns tiles [floor(T*w/W), floor(T*(w+1)/W)).
+//   * A worker writes one partial record per group it touches. Record index
+//     rec(g, w) = g + w is unique because, walking tiles in order, every step to
+//     the next (group, worker) piece advances g or w. The combine kernel finds
+//     group g's records from the workers holding its first and last tile.
+//   * A record holds, per row: m (running max, log2 units), l (sum of 2^(s-m)),
+//     and o (unnormalised sum of 2^(s-m) * c_t, d_c floats).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace mla {
+
+constexpr int kGroupRows = 128;  // query rows per group (the tcgen05 M tile)
+
+struct DecodePlan {
+    // dims
+    int dc, dR, H, dn, dv;
+    int row_stride;          // cache row stride in elements
+    long long kv_rows;       // rows addressable from the cache pointer (bounds the TMA tensor map)
+    // batch geometry
+    int B;
+    int shared;              // 1: all groups read sequence 0 (rows are flattened (token, head))
+    int head_blocks;         // ceil(H / 128) when !shared
+    int G;                   // groups
+    int max_len;             // upper bound of sequence lengths
+    int uniform_len;         // > 0: every sequence has this length; no prefix array
+    const int* seq_lens;     // device (B,) when !uniform
+    const int64_t* kv_offsets;  // device (B,) or null
+    int kv_pos_offset;       // rope table row of cache row 0
+    // work split
+    int tile;                // positions per tile
+    int W;                   // workers
+    const int* tile_prefix;  // device (G + 1,) when !uniform (written by the pack kernel)
+    int* status;             // device error word (0 = ok)
+};
+
+__host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// Sequence index of group g.
+__device__ inline int group_seq(const DecodePlan& P, int g) { return P.shared ? 0 : g / P.head_blocks; }
+
+__device__ inline int group_len(const DecodePlan& P, int g) {
+    if (P.uniform_len > 0) return P.uniform_len;
+    return P.seq_lens[group_seq(P, g)];
+}
+
+__device__ inline int64_t group_kv_row0(const DecodePlan& P, int g) {
+    int b = group_seq(P, g);
+    if (P.kv_offsets) return P.kv_offsets[b];
+    return P.shared ? 0 : static_cast<int64_t>(b) * P.max_len;
+}
+
+// Number of valid rows in group g (rows beyond H, or beyond B*H when shared, are padding).
+__device__ inline int group_rows(const DecodePlan& P, int g) {
+    if (P.shared) {
+        int total = P.B * P.H;
+        int r = total - g * kGroupRows;
+        return r < kGroupRows ? r : kGroupRows;
+    }
+    int r = P.H - (g % P.head_blocks) * kGroupRows;
+    return r < kGroupRows ? r : kGroupRows;
+}
+
+// Output row (b * H + h) of row r of group g, or -1 for a padding row.
+__device__ inline int group_out_row(const DecodePlan& P, int g, int r) {
+    if (P.shared) {
+        int f = g * kGroupRows + r;
+        return f < P.B * P.H ? f : -1;
+    }
+    int b = g / P.head_blocks;
+    int h = (g % P.head_blocks) * kGroupRows + r;
+    return h < P.H ? b * P.H + h : -1;
+}
+
+__device__ inline int tile_prefix(const DecodePlan& P, int g) {
+    if (P.uniform_len > 0) return g * ceil_div(P.uniform_len, P.tile);
+    return P.tile_prefix[g];
+}
+
+__device__ inline int total_tiles(const DecodePlan& P) { return tile_prefix(P, P.G); }
+
+__device__ inline int worker_begin(int T, int W, int w) {
+    return static_cast<int>((static_cast<long long>(T) * w) / W);
+}
+
+// Worker owning global tile t.
+__device__ inline int worker_of_tile(int T, int W, int t) {
+    return static_cast<int>(((static_cast<long long>(t) + 1) * W - 1) / T);
+}
+
+// First group whose tile range contains global tile t (binary search on the prefix).
+__device__ inline int group_of_tile(const DecodePlan& P, int t) {
+    if (P.uniform_len > 0) return t / ceil_div(P.uniform_len, P.tile);
+    int lo = 0, hi = P.G - 1;
+    while (lo < hi) {  // largest g with prefix[g] <= t and prefix[g+1] > t
+        int mid = (lo + hi + 1) >> 1;
+        if (P.tile_prefix[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    // skip empty groups (prefix[g] == prefix[g+1])
+    while (lo < P.G - 1 && P.tile_prefix[lo + 1] <= t) ++lo;
+    return lo;
+}
+
+__device__ inline int num_records(const DecodePlan& P) { return P.G + P.W - 1; }
+
+template <typename T> struct ElemTraits;
+template <> struct ElemTraits<__half> {
+    static __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+    static __device__ __forceinline__ __half from_f(float x) { return __float2half_rn(x); }
+    static __device__ __forceinline__ float2 to_f2(__half2 x) { return __half22float2(x); }
+    using T2 = __half2;
+};
+template <> struct ElemTraits<__nv_bfloat16> {
+    static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+    static __device__ __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+    static __device__ __forceinline__ float2 to_f2(__nv_bfloat162 x) { return __bfloat1622float2(x); }
+    using T2 = __nv_bfloat162;
+};
+
+// Device error codes written to DecodePlan::status.
+enum : int { kStatusOk = 0, kStatusTimeout = 1, kStatusBadPlan = 2 };
+
+// ---- kernel launchers (defined in the .cu files; return cudaGetLastError()) ----
+// pack.cu
+template <typename T>
+cudaError_t launch_pack_q(const DecodePlan& P, const float* q_absorbed, const float* q_nope,
+                          const T* W_UK, const float* q_rope, float q_scale, T* qpack,
+                          int* tile_prefix_out, cudaStream_t s);
+// decode_simt.cu
+template <typename T>
+cudaError_t launch_decode_simt(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
+                               const float* sin, float* rec_ml, float* rec_o, cudaStream_t s);
+// decode_sm100.cu
+template <typename T>
+cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
+                                const float* sin, float* rec_ml, float* rec_o, cudaStream_t s);
+bool decode_sm100_available();
+// combine.cu
+template <typename T>
+cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const float* rec_o,
+                           const T* W_UV, float* out, float* part_ml, float* part_o, cudaStream_t s);
+template <typename T>
+cudaError_t launch_combine_parts(int B, int H, int dc, int dv, int parts, const float* part_ml,
+                                 const float* part_o, const T* W_UV, float* out, cudaStream_t s);
+
+}  // namespace mla

@@ -1,0 +1,164 @@
+// Query packing: builds the decode kernels' Q operand
+//   qpack[g * 128 + r] = q_scale * [ q_abs(b, h) (d_c) | q_rope(b, h) (d_R) ]   (element type T)
+// where q_scale = softmax_scale * log2(e), so scores come out in log2 units.
+// q_abs is either given (the reference ops take it precomputed, src/fused_mla.cuh:18)
+// or absorbed here: q_abs[b,h,c] = sum_i q_nope[b,h,i] * W_UK[h*dn + i, c]
+// (tests/test_python.py:98-99 / tests/test_correctness.cu:29-46 of the reference).
+// Padding rows of a group are written as zeros.
+//
+// Block (0, 0) of the absorb launch -- or of the copy launch -- also writes the
+// tile prefix over groups for variable-length batches.
+#include "mla_internal.cuh"
+
+namespace mla {
+
+__device__ void write_tile_prefix(const DecodePlan& P, int* prefix) {
+    // one block; G is small (batch * head_blocks)
+    __shared__ int carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (int base = 0; base < P.G; base += blockDim.x) {
+        int g = base + threadIdx.x;
+        int v = 0;
+        if (g < P.G) {
+            int L = P.seq_lens[group_seq(P, g)];
+            L = L < 0 ? 0 : (L > P.max_len ? P.max_len : L);
+            v = ceil_div(L, P.tile);
+        }
+        // inclusive scan across the block (simple Hillis-Steele in shared memory)
+        __shared__ int buf[1024];
+        buf[threadIdx.x] = v;
+        __syncthreads();
+        for (int off = 1; off < blockDim.x; off <<= 1) {
+            int add = threadIdx.x >= off ? buf[threadIdx.x - off] : 0;
+            __syncthreads();
+            buf[threadIdx.x] += add;
+            __syncthreads();
+        }
+        if (g < P.G) prefix[g + 1] = carry + buf[threadIdx.x];
+        __syncthreads();
+        if (threadIdx.x == blockDim.x - 1) carry += buf[threadIdx.x];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) prefix[0] = 0;
+}
+
+// Rows given as q_absorbed: one thread per element.
+template <typename T>
+__global__ void pack_q_copy_kernel(DecodePlan P, const float* __restrict__ q_abs,
+                                   const float* __restrict__ q_rope, float q_scale,
+                                   T* __restrict__ qpack, int* tile_prefix_out) {
+    if (tile_prefix_out && blockIdx.x == 0) write_tile_prefix(P, tile_prefix_out);
+    const int K = P.dc + P.dR;
+    const long long total = static_cast<long long>(P.G) * kGroupRows * K;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        int k = static_cast<int>(i % K);
+        long long row = i / K;
+        int g = static_cast<int>(row / kGroupRows), r = static_cast<int>(row % kGroupRows);
+        int orow = group_out_row(P, g, r);
+        float v = 0.f;
+        if (orow >= 0) {
+            v = k < P.dc ? q_abs[static_cast<long long>(orow) * P.dc + k]
+                         : q_rope[static_cast<long long>(orow) * P.dR + (k - P.dc)];
+            v *= q_scale;
+        }
+        qpack[i] = ElemTraits<T>::from_f(v);
+    }
+}
+
+// Absorption: block (h, token chunk). W_UK[h] is (dn, dc) row-major; every thread
+// owns output columns c = threadIdx.x + k * blockDim.x and streams over i, so a
+// warp reads 32 consecutive W_UK elements per step. kTok tokens share each load.
+template <typename T, int kTok>
+__global__ void pack_q_absorb_kernel(DecodePlan P, const float* __restrict__ q_nope,
+                                     const T* __restrict__ W_UK, const float* __restrict__ q_rope,
+                                     float q_scale, T* __restrict__ qpack, int* tile_prefix_out) {
+    if (tile_prefix_out && blockIdx.x == 0 && blockIdx.y == 0) write_tile_prefix(P, tile_prefix_out);
+    extern __shared__ float qn_s[];  // (kTok, dn)
+    const int h = blockIdx.x;
+    const int b0 = blockIdx.y * kTok;
+    const int dn = P.dn, dc = P.dc, K = P.dc + P.dR;
+    for (int i = threadIdx.x; i < kTok * dn; i += blockDim.x) {
+        int t = i / dn, d = i % dn;
+        int b = b0 + t;
+        qn_s[i] = b < P.B ? q_nope[(static_cast<long long>(b) * P.H + h) * dn + d] : 0.f;
+    }
+    __syncthreads();
+    const T* W = W_UK + static_cast<long long>(h) * dn * dc;
+    for (int c = threadIdx.x; c < dc; c += blockDim.x) {
+        float acc[kTok];
+#pragma unroll
+        for (int t = 0; t < kTok; ++t) acc[t] = 0.f;
+        for (int i = 0; i < dn; ++i) {
+            float w = ElemTraits<T>::to_f(W[static_cast<long long>(i) * dc + c]);
+#pragma unroll
+            for (int t = 0; t < kTok; ++t) acc[t] = fmaf(qn_s[t * dn + i], w, acc[t]);
+        }
+#pragma unroll
+        for (int t = 0; t < kTok; ++t) {
+            int b = b0 + t;
+            if (b >= P.B) break;
+            int flat = b * P.H + h;  // output row
+            long long qrow;
+            if (P.shared) qrow = flat;  // groups of 128 flattened rows
+            else qrow = static_cast<long long>(b) * P.head_blocks * kGroupRows + h;
+            qpack[qrow * K + c] = ElemTraits<T>::from_f(acc[t] * q_scale);
+        }
+    }
+    // rope part
+    for (int i = threadIdx.x; i < kTok * P.dR; i += blockDim.x) {
+        int t = i / P.dR, j = i % P.dR;
+        int b = b0 + t;
+        if (b >= P.B) continue;
+        int flat = b * P.H + h;
+        long long qrow = P.shared ? flat : static_cast<long long>(b) * P.head_blocks * kGroupRows + h;
+        qpack[qrow * K + dc + j] =
+            ElemTraits<T>::from_f(q_rope[static_cast<long long>(flat) * P.dR + j] * q_scale);
+    }
+}
+
+// Zero the padding rows of every group (rows whose output row is -1).
+template <typename T>
+__global__ void pack_q_zero_pad_kernel(DecodePlan P, T* __restrict__ qpack) {
+    const int K = P.dc + P.dR;
+    const long long total = static_cast<long long>(P.G) * kGroupRows * K;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        long long row = i / K;
+        int g = static_cast<int>(row / kGroupRows), r = static_cast<int>(row % kGroupRows);
+        if (group_out_row(P, g, r) < 0) qpack[i] = ElemTraits<T>::from_f(0.f);
+    }
+}
+
+template <typename T>
+cudaError_t launch_pack_q(const DecodePlan& P, const float* q_absorbed, const float* q_nope,
+                          const T* W_UK, const float* q_rope, float q_scale, T* qpack,
+                          int* tile_prefix_out, cudaStream_t s) {
+    const long long total = static_cast<long long>(P.G) * kGroupRows * (P.dc + P.dR);
+    int blocks = static_cast<int>((total + 255) / 256);
+    if (blocks > 4096) blocks = 4096;
+    if (q_absorbed) {
+        pack_q_copy_kernel<T><<<blocks, 256, 0, s>>>(P, q_absorbed, q_rope, q_scale, qpack,
+                                                     tile_prefix_out);
+        return cudaGetLastError();
+    }
+    bool has_pad = P.shared ? (P.B * P.H) % kGroupRows != 0 : P.H % kGroupRows != 0;
+    if (has_pad) {
+        pack_q_zero_pad_kernel<T><<<blocks, 256, 0, s>>>(P, qpack);
+    }
+    constexpr int kTok = 4;
+    dim3 grid(P.H, ceil_div(P.B, kTok));
+    size_t smem = static_cast<size_t>(kTok) * P.dn * sizeof(float);
+    pack_q_absorb_kernel<T, kTok><<<grid, 256, smem, s>>>(P, q_nope, W_UK, q_rope, q_scale, qpack,
+                                                          tile_prefix_out);
+    return cudaGetLastError();
+}
+
+template cudaError_t launch_pack_q<__half>(const DecodePlan&, const float*, const float*, const __half*,
+                                           const float*, float, __half*, int*, cudaStream_t);
+template cudaError_t launch_pack_q<__nv_bfloat16>(const DecodePlan&, const float*, const float*,
+                                                  const __nv_bfloat16*, const float*, float,
+                                                  __nv_bfloat16*, int*, cudaStream_t);
+
+}  // namespace mla

@@ -1,0 +1,356 @@
+"""Torch-facing operators, mirroring the reference's ``latent_attn._C`` module
+(csrc/bindings.cpp:1-256 of anishesg/latent-attn): same op names, same argument
+order and meaning, output allocated by the op on the current CUDA stream, and
+``RuntimeError`` on a wrong dtype, layout, device or shape.
+
+Differences from the reference, all additive:
+* the cache / weight tensors may be float16 (the reference's only type) or
+  bfloat16;
+* the computation runs through the C ABI (``libmla_b200.so``): query packing,
+  the tensor-core split-KV decode (or the CUDA-core kernel for shapes it does not
+  cover) and the log-sum-exp combine with the W_UV projection;
+* ``mla_decode`` / ``mla_decode_partial`` / ``mla_combine_partials`` expose the
+  general decode (in-op absorption, variable-length batches, KV-range shards).
+
+PyTorch is used only for tensors, streams and workspace memory.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16}
+
+
+def _check_half(t: torch.Tensor, name: str) -> None:
+    if t.dtype not in _DT:
+        raise RuntimeError(f"{name} must be float16 or bfloat16, got {t.dtype}")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be on CUDA")
+
+
+def _check_f32(t: torch.Tensor, name: str) -> None:
+    if t.dtype != torch.float32:
+        raise RuntimeError(f"{name} must be float32, got {t.dtype}")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be on CUDA")
+
+
+def _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim):
+    c = _lib.MlaConfig(int(d_model), int(kv_lora_rank), int(qk_nope_head_dim), int(qk_rope_head_dim),
+                       int(num_heads), int(v_head_dim))
+    # MLAConfig::validate (src/mla_config.cuh:35-40) raises std::invalid_argument -> ValueError
+    if kv_lora_rank <= 0 or qk_nope_head_dim <= 0 or qk_rope_head_dim <= 0:
+        raise ValueError("MLA dims must be positive")
+    if num_heads <= 0 or v_head_dim <= 0:
+        raise ValueError("num_heads and v_head_dim must be positive")
+    return c
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _decode_args(dtype, batch, shared, kv_cache, max_seq_len, q_rope, W_UV, rope_cos, rope_sin, out,
+                 q_absorbed=None, q_nope=None, W_UK=None, seq_lens=None, kv_offsets=None,
+                 seq_lens_host=None, kv_pos_offset=0, softmax_scale=0.0, kv_row_stride=0, kernel=0):
+    a = _lib.MlaDecodeArgs()
+    a.dtype = _DT[dtype]
+    a.batch = int(batch)
+    a.shared_cache = 1 if shared else 0
+    a.kv_cache = kv_cache.data_ptr()
+    a.kv_row_stride = int(kv_row_stride)
+    a.kv_total_rows = int(kv_cache.size(0))
+    a.kv_offsets = _ptr(kv_offsets)
+    a.seq_lens = _ptr(seq_lens)
+    a.seq_lens_host = C.cast(seq_lens_host, C.c_void_p) if seq_lens_host is not None else None
+    a.max_seq_len = int(max_seq_len)
+    a.kv_pos_offset = int(kv_pos_offset)
+    a.q_absorbed = _ptr(q_absorbed)
+    a.q_nope = _ptr(q_nope)
+    a.W_UK = _ptr(W_UK)
+    a.q_rope = q_rope.data_ptr()
+    a.W_UV = W_UV.data_ptr()
+    a.rope_cos = rope_cos.data_ptr()
+    a.rope_sin = rope_sin.data_ptr()
+    a.softmax_scale = float(softmax_scale)
+    a.output = _ptr(out)
+    a.kernel = int(kernel)
+    return a
+
+
+def _workspace(cfg, args, device, workspace: Optional[torch.Tensor]) -> torch.Tensor:
+    lib = _lib.load()
+    n = C.c_size_t(0)
+    _lib.check(lib.mla_decode_workspace_size(C.byref(cfg), C.byref(args), C.byref(n)))
+    if workspace is not None and workspace.numel() * workspace.element_size() >= n.value \
+            and workspace.data_ptr() % 256 == 0:
+        return workspace
+    return torch.empty(max(int(n.value), 1), dtype=torch.uint8, device=device)
+
+
+def workspace_size(cfg, args) -> int:
+    n = C.c_size_t(0)
+    _lib.check(_lib.load().mla_decode_workspace_size(C.byref(cfg), C.byref(args), C.byref(n)))
+    return int(n.value)
+
+
+# ---------------------------------------------------------------------------
+# reference ops
+# ---------------------------------------------------------------------------
+
+def fused_mla_forward(kv_cache, q_absorbed, q_rope, W_UV, rope_cos, rope_sin,
+                      d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim):
+    """Single-token fused absorbed decode (csrc/bindings.cpp:126-176). Returns (H, dv) fp32."""
+    _check_half(kv_cache, "kv_cache")
+    _check_f32(q_absorbed, "q_absorbed")
+    _check_f32(q_rope, "q_rope")
+    _check_half(W_UV, "W_UV")
+    _check_f32(rope_cos, "rope_cos")
+    _check_f32(rope_sin, "rope_sin")
+    cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    seq_len = kv_cache.size(0)
+    if kv_cache.dim() != 2 or kv_cache.size(1) != kv_lora_rank + qk_rope_head_dim:
+        raise RuntimeError("kv_cache dim1 mismatch")
+    if q_absorbed.dim() != 2 or q_absorbed.size(0) != num_heads or q_absorbed.size(1) != kv_lora_rank:
+        raise RuntimeError("q_absorbed shape mismatch")
+    if q_rope.dim() != 2 or q_rope.size(0) != num_heads or q_rope.size(1) != qk_rope_head_dim:
+        raise RuntimeError("q_rope shape mismatch")
+    _check_common(kv_cache, W_UV, rope_cos, rope_sin, seq_len, num_heads, v_head_dim, kv_lora_rank,
+                  qk_rope_head_dim)
+    out = torch.empty(num_heads, v_head_dim, dtype=torch.float32, device=kv_cache.device)
+    if seq_len == 0:
+        return out.zero_()
+    _run_decode(cfg, kv_cache.dtype, 1, False, kv_cache, seq_len, q_rope, W_UV, rope_cos, rope_sin, out,
+                q_absorbed=q_absorbed)
+    return out
+
+
+def batched_fused_mla_forward(kv_cache, q_absorbed, q_rope, W_UV, rope_cos, rope_sin,
+                              d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads,
+                              v_head_dim):
+    """B query tokens over one shared cache (csrc/bindings.cpp:188-244). Returns (B, H, dv) fp32."""
+    _check_half(kv_cache, "kv_cache")
+    _check_f32(q_absorbed, "q_absorbed")
+    _check_f32(q_rope, "q_rope")
+    _check_half(W_UV, "W_UV")
+    _check_f32(rope_cos, "rope_cos")
+    _check_f32(rope_sin, "rope_sin")
+    cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    if q_absorbed.dim() != 3:
+        raise RuntimeError("q_absorbed must be 3D (batch, num_heads, kv_lora_rank)")
+    if q_rope.dim() != 3:
+        raise RuntimeError("q_rope must be 3D (batch, num_heads, qk_rope_head_dim)")
+    batch = q_absorbed.size(0)
+    seq_len = kv_cache.size(0)
+    if batch <= 0:
+        raise RuntimeError(f"batch_size must be positive, got {batch}")
+    if q_rope.size(0) != batch:
+        raise RuntimeError(f"q_rope batch dim must match q_absorbed batch dim: {q_rope.size(0)} vs {batch}")
+    if q_absorbed.size(1) != num_heads or q_absorbed.size(2) != kv_lora_rank:
+        raise RuntimeError(
+            f"q_absorbed shape mismatch: expected ({batch}, {num_heads}, {kv_lora_rank}) got "
+            f"({q_absorbed.size(0)}, {q_absorbed.size(1)}, {q_absorbed.size(2)})")
+    if q_rope.size(1) != num_heads or q_rope.size(2) != qk_rope_head_dim:
+        raise RuntimeError("q_rope shape mismatch")
+    if kv_cache.dim() != 2 or kv_cache.size(1) != kv_lora_rank + qk_rope_head_dim:
+        raise RuntimeError("kv_cache dim1 mismatch")
+    _check_common(kv_cache, W_UV, rope_cos, rope_sin, seq_len, num_heads, v_head_dim, kv_lora_rank,
+                  qk_rope_head_dim)
+    out = torch.empty(batch, num_heads, v_head_dim, dtype=torch.float32, device=kv_cache.device)
+    if seq_len == 0:
+        return out.zero_()
+    _run_decode(cfg, kv_cache.dtype, batch, True, kv_cache, seq_len, q_rope, W_UV, rope_cos, rope_sin,
+                out, q_absorbed=q_absorbed)
+    return out
+
+
+def naive_mla_forward(kv_cache, W_UK, W_UV, q_nope, q_rope, rope_cos, rope_sin,
+                      d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim):
+    """Decompress-then-attend baseline (csrc/bindings.cpp:53-114, src/naive_mla.cu:58-246).
+
+    This is the comparison baseline the fused path exists to beat, not part of the
+    accelerated path: it materialises K_nope = c @ W_UK^T and V = c @ W_UV^T with
+    plain library GEMMs and attends with fp32 torch ops, with the reference's
+    output-layout error (its cuBLAS outputs are read transposed) corrected.
+    Returns (H, dv) fp32.
+    """
+    _check_half(kv_cache, "kv_cache")
+    _check_half(W_UK, "W_UK")
+    _check_half(W_UV, "W_UV")
+    _check_f32(q_nope, "q_nope")
+    _check_f32(q_rope, "q_rope")
+    _check_f32(rope_cos, "rope_cos")
+    _check_f32(rope_sin, "rope_sin")
+    _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    S = kv_cache.size(0)
+    dc, dR, H, dn, dv = kv_lora_rank, qk_rope_head_dim, num_heads, qk_nope_head_dim, v_head_dim
+    if kv_cache.size(1) != dc + dR:
+        raise RuntimeError(f"kv_cache dim1 must be {dc + dR}")
+    if q_nope.size(0) != H or q_nope.size(1) != dn:
+        raise RuntimeError("q_nope shape mismatch")
+    if q_rope.size(0) != H or q_rope.size(1) != dR:
+        raise RuntimeError("q_rope shape mismatch")
+    c = kv_cache[:, :dc]
+    K_nope = torch.matmul(c, W_UK.t()).float().view(S, H, dn)
+    V = torch.matmul(c, W_UV.t()).float().view(S, H, dv)
+    kr = kv_cache[:, dc:].float()
+    half = dR // 2
+    k0, k1 = kr[:, :half], kr[:, half:]
+    K_rope = torch.cat([k0 * rope_cos[:S] - k1 * rope_sin[:S], k0 * rope_sin[:S] + k1 * rope_cos[:S]], dim=-1)
+    scale = 1.0 / math.sqrt(dn + dR)
+    s = torch.einsum("hd,shd->hs", q_nope, K_nope) * scale + (q_rope @ K_rope.t()) * scale
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("hs,shv->hv", p, V).contiguous()
+
+
+def _check_common(kv_cache, W_UV, rope_cos, rope_sin, seq_len, H, dv, dc, dR):
+    if W_UV.dtype != kv_cache.dtype:
+        raise RuntimeError(f"W_UV dtype {W_UV.dtype} must match kv_cache dtype {kv_cache.dtype}")
+    if W_UV.dim() != 2 or W_UV.size(0) != H * dv or W_UV.size(1) != dc:
+        raise RuntimeError("W_UV shape mismatch")
+    for t, n in ((rope_cos, "rope_cos"), (rope_sin, "rope_sin")):
+        if t.dim() != 2 or t.size(1) != dR // 2 or t.size(0) < seq_len:
+            raise RuntimeError(f"{n} shape mismatch: expected (>= {seq_len}, {dR // 2})")
+    if kv_cache.data_ptr() % 16 != 0:
+        raise RuntimeError("kv_cache must be 16-byte aligned")
+
+
+def _run_decode(cfg, dtype, batch, shared, kv_cache, max_seq_len, q_rope, W_UV, rope_cos, rope_sin, out,
+                workspace=None, **kw):
+    args = _decode_args(dtype, batch, shared, kv_cache, max_seq_len, q_rope, W_UV, rope_cos, rope_sin, out,
+                        **kw)
+    ws = _workspace(cfg, args, kv_cache.device, workspace)
+    lib = _lib.load()
+    _lib.check(lib.mla_decode(C.byref(cfg), C.byref(args), C.c_void_p(ws.data_ptr()),
+                              C.c_size_t(ws.numel()), C.c_void_p(_stream(kv_cache.device))))
+    return ws
+
+
+# ---------------------------------------------------------------------------
+# general decode (no reference counterpart)
+# ---------------------------------------------------------------------------
+
+def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor, rope_cos: torch.Tensor,
+               rope_sin: torch.Tensor, d_model: int, kv_lora_rank: int, qk_nope_head_dim: int,
+               qk_rope_head_dim: int, num_heads: int, v_head_dim: int, *,
+               q_absorbed: Optional[torch.Tensor] = None, q_nope: Optional[torch.Tensor] = None,
+               W_UK: Optional[torch.Tensor] = None, seq_lens: Optional[torch.Tensor] = None,
+               kv_offsets: Optional[torch.Tensor] = None, max_seq_len: Optional[int] = None,
+               seq_lens_host: Optional[Sequence[int]] = None, shared_cache: bool = False,
+               kv_pos_offset: int = 0, softmax_scale: float = 0.0, kv_row_stride: int = 0,
+               kernel: int = 0, out: Optional[torch.Tensor] = None,
+               workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """General decode: (B, H, dv) fp32 for B sequences (or B tokens over one shared cache).
+
+    Give ``q_absorbed`` (B, H, d_c) fp32, or ``q_nope`` (B, H, dn) fp32 with ``W_UK``
+    (H*dn, d_c) for in-op absorption. ``seq_lens`` (B,) int32 and ``kv_offsets`` (B,)
+    int64 (device) describe a variable-length batch packed in ``kv_cache``; without
+    them every sequence has ``max_seq_len`` rows at ``b * max_seq_len``.
+    """
+    if kv_row_stride:
+        if kv_cache.dtype not in _DT or not kv_cache.is_cuda or kv_cache.stride(-1) != 1:
+            raise RuntimeError("kv_cache must be a CUDA fp16/bf16 tensor with unit inner stride")
+    else:
+        _check_half(kv_cache, "kv_cache")
+    _check_half(W_UV, "W_UV")
+    _check_f32(q_rope, "q_rope")
+    _check_f32(rope_cos, "rope_cos")
+    _check_f32(rope_sin, "rope_sin")
+    cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    if q_absorbed is not None:
+        _check_f32(q_absorbed, "q_absorbed")
+        q_nope = None
+        W_UK = None
+    else:
+        if q_nope is None or W_UK is None:
+            raise RuntimeError("give q_absorbed, or q_nope together with W_UK")
+        _check_f32(q_nope, "q_nope")
+        _check_half(W_UK, "W_UK")
+        if W_UK.dtype != kv_cache.dtype:
+            raise RuntimeError("W_UK dtype must match kv_cache dtype")
+    if q_rope.dim() != 3:
+        raise RuntimeError("q_rope must be 3D (batch, num_heads, qk_rope_head_dim)")
+    B = q_rope.size(0)
+    if max_seq_len is None:
+        if seq_lens_host is not None:
+            max_seq_len = max(int(x) for x in seq_lens_host)
+        elif seq_lens is None:
+            max_seq_len = kv_cache.size(0) if shared_cache else kv_cache.size(0) // B
+        else:
+            raise RuntimeError("max_seq_len is required with device seq_lens")
+    if seq_lens is not None:
+        if seq_lens.dtype != torch.int32 or not seq_lens.is_cuda or seq_lens.numel() != B:
+            raise RuntimeError("seq_lens must be a CUDA int32 tensor of shape (batch,)")
+    if kv_offsets is not None:
+        if kv_offsets.dtype != torch.int64 or not kv_offsets.is_cuda or kv_offsets.numel() != B:
+            raise RuntimeError("kv_offsets must be a CUDA int64 tensor of shape (batch,)")
+    host_arr = None
+    if seq_lens_host is not None:
+        host_arr = (C.c_int * B)(*[int(x) for x in seq_lens_host])
+    if out is None:
+        out = torch.empty(B, num_heads, v_head_dim, dtype=torch.float32, device=kv_cache.device)
+    _run_decode(cfg, kv_cache.dtype, B, shared_cache, kv_cache, max_seq_len, q_rope, W_UV, rope_cos,
+                rope_sin, out, workspace=workspace, q_absorbed=q_absorbed, q_nope=q_nope, W_UK=W_UK,
+                seq_lens=seq_lens, kv_offsets=kv_offsets, seq_lens_host=host_arr,
+                kv_pos_offset=kv_pos_offset, softmax_scale=softmax_scale, kv_row_stride=kv_row_stride,
+                kernel=kernel)
+    return out
+
+
+def mla_decode_partial(kv_cache, q_rope, W_UV, rope_cos, rope_sin, d_model, kv_lora_rank,
+                       qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim, *,
+                       q_absorbed=None, q_nope=None, W_UK=None, kv_pos_offset: int = 0,
+                       softmax_scale: float = 0.0, workspace=None):
+    """One KV-range shard of a single-token-per-sequence decode over all rows of
+    ``kv_cache`` (B sequences of ``kv_cache.size(0) // B`` rows). Returns
+    (ml (B, H, 2), o (B, H, d_c)): natural-log max, sum of exponentials, and the
+    unnormalised latent sum, ready for ``mla_combine_partials``."""
+    _check_half(kv_cache, "kv_cache")
+    cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    B = q_rope.size(0)
+    L = kv_cache.size(0) // B
+    ml = torch.empty(B, num_heads, 2, dtype=torch.float32, device=kv_cache.device)
+    o = torch.empty(B, num_heads, kv_lora_rank, dtype=torch.float32, device=kv_cache.device)
+    args = _decode_args(kv_cache.dtype, B, False, kv_cache, L, q_rope, W_UV, rope_cos, rope_sin, None,
+                        q_absorbed=q_absorbed, q_nope=None if q_absorbed is not None else q_nope,
+                        W_UK=None if q_absorbed is not None else W_UK, kv_pos_offset=kv_pos_offset,
+                        softmax_scale=softmax_scale)
+    ws = _workspace(cfg, args, kv_cache.device, workspace)
+    lib = _lib.load()
+    _lib.check(lib.mla_decode_partial(C.byref(cfg), C.byref(args), C.c_void_p(ml.data_ptr()),
+                                      C.c_void_p(o.data_ptr()), C.c_void_p(ws.data_ptr()),
+                                      C.c_size_t(ws.numel()), C.c_void_p(_stream(kv_cache.device))))
+    return ml, o
+
+
+def mla_combine_partials(part_ml: torch.Tensor, part_o: torch.Tensor, W_UV: torch.Tensor, d_model,
+                         kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim,
+                         out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Merge ``P`` shards' partials (P, B, H, 2) / (P, B, H, d_c) and project with W_UV -> (B, H, dv)."""
+    _check_f32(part_ml, "part_ml")
+    _check_f32(part_o, "part_o")
+    _check_half(W_UV, "W_UV")
+    cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    P, B = part_ml.size(0), part_ml.size(1)
+    if out is None:
+        out = torch.empty(B, num_heads, v_head_dim, dtype=torch.float32, device=part_ml.device)
+    lib = _lib.load()
+    _lib.check(lib.mla_combine_partials(C.byref(cfg), _DT[W_UV.dtype], B, P, C.c_void_p(part_ml.data_ptr()),
+                                        C.c_void_p(part_o.data_ptr()), C.c_void_p(W_UV.data_ptr()),
+                                        C.c_void_p(out.data_ptr()), C.c_void_p(_stream(part_ml.device))))
+    return out

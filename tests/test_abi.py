@@ -1,0 +1,126 @@
+"""The C ABI surface, checked without a GPU: every declared entry point is
+exported, the ctypes mirrors have the header's layout, argument validation
+returns status codes (never aborts), and the C++ drop-in headers compile."""
+
+import ctypes as C
+import os
+import re
+import subprocess
+import tempfile
+
+import pytest
+
+from latent_attn import _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+INC = os.path.join(REPO, "include")
+HEADER = os.path.join(INC, "latent_attn_b200", "mla.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"MLA_API\s+[\w\s\*]+?\b(mla_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_symbols()
+    assert len(names) >= 9, names
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True).stdout
+    exported = set(re.findall(r" T (mla_\w+)", out))
+    for n in names:
+        assert n in exported, f"{n} declared in mla.h but not exported"
+        assert hasattr(lib, n)
+    assert set(_lib.SIGNATURES) == set(names), "ctypes signatures out of sync with mla.h"
+
+
+def test_struct_layouts_match_header():
+    src = r'''
+#include <stdio.h>
+#include <stddef.h>
+#include "latent_attn_b200/mla.h"
+#define P(T, f) printf(#T "." #f " %zu\n", offsetof(T, f));
+int main(void) {
+  printf("mla_config_t %zu\n", sizeof(mla_config_t));
+  printf("mla_fused_params_t %zu\n", sizeof(mla_fused_params_t));
+  printf("mla_batched_fused_params_t %zu\n", sizeof(mla_batched_fused_params_t));
+  printf("mla_decode_args_t %zu\n", sizeof(mla_decode_args_t));
+  P(mla_decode_args_t, kv_total_rows) P(mla_decode_args_t, seq_lens_host) P(mla_decode_args_t, softmax_scale)
+  P(mla_decode_args_t, output) P(mla_decode_args_t, kernel) P(mla_fused_params_t, cfg)
+  P(mla_batched_fused_params_t, output)
+  return 0;
+}
+'''
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "layout.c")
+        exe = os.path.join(d, "layout")
+        open(c, "w").write(src)
+        subprocess.run(["gcc", "-std=c99", "-I", INC, c, "-o", exe], check=True)
+        out = subprocess.run([exe], capture_output=True, text=True, check=True).stdout
+    got = dict(line.rsplit(" ", 1) for line in out.strip().splitlines())
+    want = {
+        "mla_config_t": C.sizeof(_lib.MlaConfig),
+        "mla_fused_params_t": C.sizeof(_lib.MlaFusedParams),
+        "mla_batched_fused_params_t": C.sizeof(_lib.MlaBatchedFusedParams),
+        "mla_decode_args_t": C.sizeof(_lib.MlaDecodeArgs),
+        "mla_decode_args_t.kv_total_rows": _lib.MlaDecodeArgs.kv_total_rows.offset,
+        "mla_decode_args_t.seq_lens_host": _lib.MlaDecodeArgs.seq_lens_host.offset,
+        "mla_decode_args_t.softmax_scale": _lib.MlaDecodeArgs.softmax_scale.offset,
+        "mla_decode_args_t.output": _lib.MlaDecodeArgs.output.offset,
+        "mla_decode_args_t.kernel": _lib.MlaDecodeArgs.kernel.offset,
+        "mla_fused_params_t.cfg": _lib.MlaFusedParams.cfg.offset,
+        "mla_batched_fused_params_t.output": _lib.MlaBatchedFusedParams.output.offset,
+    }
+    for k, v in want.items():
+        assert int(got[k]) == v, (k, got[k], v)
+
+
+def test_validation_without_gpu():
+    lib = _lib.load()
+    ok = _lib.MlaConfig(5120, 512, 128, 64, 128, 128)
+    assert lib.mla_config_validate(C.byref(ok)) == _lib.MLA_OK
+    for bad in (_lib.MlaConfig(0, 0, 128, 64, 128, 128), _lib.MlaConfig(0, 512, 128, 64, 0, 128),
+                _lib.MlaConfig(0, 512, 128, 64, 128, -1)):
+        assert lib.mla_config_validate(C.byref(bad)) == _lib.MLA_ERR_INVALID_ARGUMENT
+        assert b"positive" in lib.mla_last_error()
+    assert lib.mla_config_validate(None) == _lib.MLA_ERR_INVALID_ARGUMENT
+    # argument errors are reported before any device work
+    a = _lib.MlaDecodeArgs()
+    a.dtype, a.batch, a.max_seq_len = _lib.DTYPE_BF16, 1, 16
+    n = C.c_size_t(0)
+    st = lib.mla_decode_workspace_size(C.byref(ok), C.byref(a), C.byref(n))
+    assert st == _lib.MLA_ERR_INVALID_ARGUMENT and b"null" in lib.mla_last_error()
+    a.dtype = _lib.DTYPE_F32
+    assert lib.mla_decode_workspace_size(C.byref(ok), C.byref(a), C.byref(n)) == _lib.MLA_ERR_UNSUPPORTED
+    assert lib.mla_decode(C.byref(ok), None, None, 0, None) == _lib.MLA_ERR_INVALID_ARGUMENT
+    p = _lib.MlaFusedParams()
+    p.cfg = C.pointer(ok)
+    assert lib.mla_launch_fused(C.byref(p), _lib.DTYPE_F16, None) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert lib.mla_version().startswith(b"latent-attn-b200")
+
+
+def test_cpp_drop_in_headers_compile():
+    """A caller written against the reference's C++ API (tests/test_correctness.cu:186-198 style)
+    compiles unchanged against include/latent_attn_b200/*.cuh."""
+    src = r'''
+#include "latent_attn_b200/fused_mla_batched.cuh"
+cudaError_t call(const __half* kv, int S, const float* qa, const float* qr, const __half* wuv,
+                 const float* c, const float* s, float* out, cudaStream_t st) {
+    MLAConfig cfg = MLAConfig::deepseek_v2();
+    cfg.validate();
+    FusedMLAParams p;
+    p.kv_cache = kv; p.seq_len = S; p.q_absorbed = qa; p.q_rope = qr; p.W_UV = wuv;
+    p.rope_cos = c; p.rope_sin = s; p.output = out; p.cfg = &cfg;
+    cudaError_t e = launch_fused_mla(p, st);
+    BatchedFusedMLAParams b;
+    b.kv_cache = kv; b.seq_len = S; b.batch_size = 2; b.q_absorbed = qa; b.q_rope = qr; b.W_UV = wuv;
+    b.rope_cos = c; b.rope_sin = s; b.output = out; b.cfg = &cfg;
+    return e != cudaSuccess ? e : launch_batched_fused_mla(b, st);
+}
+'''
+    with tempfile.TemporaryDirectory() as d:
+        f = os.path.join(d, "caller.cu")
+        open(f, "w").write(src)
+        r = subprocess.run(["nvcc", "-std=c++17", "-I", INC, "-I", os.path.join(INC, "latent_attn_b200"),
+                            "-c", f, "-o", os.path.join(d, "caller.o")], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
