@@ -43,6 +43,9 @@ extern "C" {
 /* Opaque stream handle, ABI-identical to cudaStream_t. */
 typedef struct CUstream_st* mla_stream_t;
 
+/* Opaque kernel timer (see mla_timer_create). */
+typedef struct mla_timer_st* mla_timer_t;
+
 typedef enum mla_status {
   MLA_OK = 0,
   MLA_ERR_INVALID_ARGUMENT = 1,   /* null pointer, bad size, non-positive dim */
@@ -137,6 +140,7 @@ typedef struct mla_decode_args {
   float softmax_scale;          /* 0: 1 / sqrt(dn + d_R) */
   float* output;                /* (B, H, dv) fp32 */
   int kernel;                   /* MLA_KERNEL_AUTO (0), MLA_KERNEL_TENSOR_CORE (1), MLA_KERNEL_CUDA_CORE (2) */
+  mla_timer_t timer;            /* optional: CUDA events are recorded around the decode kernel */
 } mla_decode_args_t;
 
 enum { MLA_KERNEL_AUTO = 0, MLA_KERNEL_TENSOR_CORE = 1, MLA_KERNEL_CUDA_CORE = 2 };
@@ -161,6 +165,17 @@ MLA_API mla_status_t mla_decode_partial(const mla_config_t* cfg, const mla_decod
 MLA_API mla_status_t mla_combine_partials(const mla_config_t* cfg, mla_dtype_t dtype, int batch,
                                   int num_parts, const float* partial_ml, const float* partial_o,
                                   const void* W_UV, float* output, mla_stream_t stream);
+
+/* Kernel timing for benchmarks: a timer passed in mla_decode_args_t.timer gets
+ * CUDA events recorded on the call's stream immediately before and after the
+ * split-KV decode kernel. mla_timer_decode_ms waits for the second event and
+ * returns the elapsed milliseconds of the most recent such call. */
+MLA_API mla_status_t mla_timer_create(mla_timer_t* timer);
+MLA_API mla_status_t mla_timer_destroy(mla_timer_t timer);
+MLA_API mla_status_t mla_timer_decode_ms(mla_timer_t timer, float* ms);
+
+/* Number of CUDA kernels this library has launched in this process so far. */
+MLA_API uint64_t mla_kernel_launch_count(void);
 
 /* Thread-local message for the last non-OK status returned on this thread. */
 MLA_API const char* mla_last_error(void);

@@ -5,8 +5,13 @@
 //     M = max_k m_k,  L = sum_k l_k 2^(m_k - M),  o_lat = sum_k 2^(m_k - M) o_k / L
 // and projected through W_UV: out[b, h, j] = sum_i o_lat[i] * W_UV[h*dv + j, i]
 // (the projection of src/fused_mla.cu:258-267 / src/fused_mla_batched.cu:97-105).
-// Block = (head h, chunk of kTok tokens), so each W_UV[h] slice is read from
-// HBM once per chunk and reused for every token of the chunk.
+//
+// Block = (head h, chunk of up to kTok tokens), 256 threads:
+//   1. warp t computes token t's record list and normalised weights (shared memory);
+//   2. all threads merge the records column by column (coalesced over d_c);
+//   3. warp w projects rows j = w, w + 8, ...: the W_UV[h] row is read once into
+//      registers and dotted with every token's o_lat, so W_UV[h] is read once per
+//      chunk of tokens.
 #include <cfloat>
 
 #include "mla_internal.cuh"
@@ -16,53 +21,22 @@ namespace mla {
 namespace {
 constexpr int kTok = 8;
 constexpr int kThreads = 256;
-constexpr int kChunk = 64;  // latent columns of W_UV staged per step
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxRec = 128;  // records per (b, h): at most the worker count (planner caps W at 128)
 constexpr float kLn2 = 0.6931471805599453f;
+
+struct MergeList {
+    int count[kTok];
+    int row[kTok];                 // record row (r) of the token
+    int rec[kTok][kMaxRec];
+    float wgt[kTok][kMaxRec];
+    float m[kTok], l[kTok];        // merged max (log2) and sum
+};
 }  // namespace
 
-// out[b, h, :] for the kTok tokens whose normalised o_lat rows are in o_s (kTok x dc).
-template <typename T>
-__device__ void project_wuv(int h, int b0, int B, int H, int dc, int dv, const float* o_s,
-                            float* w_s, const T* __restrict__ W_UV, float* __restrict__ out) {
-    // thread -> (token t, column j): t = idx % kTok, j = idx / kTok (several j per thread)
-    const int nout = kTok * dv;
-    float acc[(kTok * 256 + kThreads - 1) / kThreads];  // dv <= 256
-    const int per = (nout + kThreads - 1) / kThreads;
-    for (int k = 0; k < per; ++k) acc[k] = 0.f;
-    const T* W = W_UV + static_cast<long long>(h) * dv * dc;
-    for (int c0 = 0; c0 < dc; c0 += kChunk) {
-        const int cw = (dc - c0) < kChunk ? (dc - c0) : kChunk;
-        __syncthreads();
-        for (int i = threadIdx.x; i < dv * kChunk; i += kThreads) {
-            int j = i / kChunk, c = i % kChunk;
-            w_s[j * (kChunk + 1) + c] = c < cw ? ElemTraits<T>::to_f(W[static_cast<long long>(j) * dc + c0 + c]) : 0.f;
-        }
-        __syncthreads();
-        for (int k = 0; k < per; ++k) {
-            int idx = threadIdx.x + k * kThreads;
-            if (idx >= nout) break;
-            int t = idx % kTok, j = idx / kTok;
-            const float* o = o_s + t * dc + c0;
-            const float* wr = w_s + j * (kChunk + 1);
-            float a = acc[k];
-            for (int c = 0; c < cw; ++c) a = fmaf(o[c], wr[c], a);
-            acc[k] = a;
-        }
-    }
-    for (int k = 0; k < per; ++k) {
-        int idx = threadIdx.x + k * kThreads;
-        if (idx >= nout) break;
-        int t = idx % kTok, j = idx / kTok;
-        int b = b0 + t;
-        if (b < B) out[(static_cast<long long>(b) * H + h) * dv + j] = acc[k];
-    }
-}
-
-// Merge the records of (b, h). Writes normalised o_lat to o_dst (dc floats) and,
-// when part_ml/part_o are given, the unnormalised partial (natural-log m).
-__device__ void merge_records(const DecodePlan& P, int b, int h, const float* __restrict__ rec_ml,
-                              const float* __restrict__ rec_o, float* o_dst, float* part_ml,
-                              float* part_o) {
+// Record list and weights of (b, h) -> slot t (executed by one warp).
+__device__ void build_merge_list(const DecodePlan& P, int b, int h, const float* __restrict__ rec_ml,
+                                 MergeList& ml, int t, bool normalise) {
     const int lane = threadIdx.x & 31;
     int g, r;
     if (P.shared) {
@@ -75,37 +49,131 @@ __device__ void merge_records(const DecodePlan& P, int b, int h, const float* __
     }
     const int T = total_tiles(P);
     const int gt0 = tile_prefix(P, g), gt1 = tile_prefix(P, g + 1);
-    float M = -INFINITY;
     int w0 = 0, w1 = -1;
     if (gt1 > gt0 && T > 0) {
         w0 = worker_of_tile(T, P.W, gt0);
         w1 = worker_of_tile(T, P.W, gt1 - 1);
     }
-    for (int w = w0; w <= w1; ++w) {
-        if (worker_begin(T, P.W, w) == worker_begin(T, P.W, w + 1)) continue;
-        M = fmaxf(M, rec_ml[(static_cast<long long>(g + w) * kGroupRows + r) * 2]);
+    const int n = w1 - w0 + 1;  // <= W <= kMaxRec
+    // pass 1: per-record m (lane k handles records k, k + 32, ...), warp max
+    float M = -INFINITY;
+    for (int k = lane; k < n; k += 32) {
+        const int w = w0 + k;
+        const bool valid = worker_begin(T, P.W, w) != worker_begin(T, P.W, w + 1);
+        const int rec = g + w;
+        float m = valid ? rec_ml[(static_cast<long long>(rec) * kGroupRows + r) * 2] : -INFINITY;
+        ml.rec[t][k] = valid ? rec : -1;
+        ml.wgt[t][k] = m;  // stash m
+        M = fmaxf(M, m);
     }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
     float L = 0.f;
-    for (int w = w0; w <= w1; ++w) {
-        if (worker_begin(T, P.W, w) == worker_begin(T, P.W, w + 1)) continue;
-        const float* ml = rec_ml + (static_cast<long long>(g + w) * kGroupRows + r) * 2;
-        L += ml[1] * exp2f(ml[0] - M);
-    }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    for (int c = lane; c < P.dc; c += 32) {
+    for (int k = lane; k < n; k += 32) {
+        const int rec = ml.rec[t][k];
         float a = 0.f;
-        for (int w = w0; w <= w1; ++w) {
-            if (worker_begin(T, P.W, w) == worker_begin(T, P.W, w + 1)) continue;
-            long long rr = static_cast<long long>(g + w) * kGroupRows + r;
-            a += exp2f(rec_ml[rr * 2] - M) * rec_o[rr * P.dc + c];
+        if (rec >= 0) {
+            a = exp2f(ml.wgt[t][k] - M);
+            L += a * rec_ml[(static_cast<long long>(rec) * kGroupRows + r) * 2 + 1];
         }
-        if (o_dst) o_dst[c] = a * inv;
-        if (part_o) part_o[(static_cast<long long>(b) * P.H + h) * P.dc + c] = a;
+        ml.wgt[t][k] = a;
     }
-    if (part_ml && lane == 0) {
-        float* pm = part_ml + (static_cast<long long>(b) * P.H + h) * 2;
-        pm[0] = L > 0.f ? M * kLn2 : -INFINITY;
-        pm[1] = L;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    if (normalise) {
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        for (int k = lane; k < n; k += 32) ml.wgt[t][k] *= inv;
+    }
+    if (lane == 0) {
+        ml.count[t] = n < 0 ? 0 : n;
+        ml.row[t] = r;
+        ml.m[t] = M;
+        ml.l[t] = L;
+    }
+}
+
+// out[b, h, :] for the tokens of the chunk whose o_lat rows are in o_s (ntok x dc).
+// Warp w handles rows j = w, w + 8, ..., four rows at a time; with d_c a multiple
+// of 256 each lane reads 16-byte vectors (8 elements), so a warp keeps 4 * d_c / 256
+// independent W_UV loads in flight.
+template <typename T>
+__device__ void project_rows(int h, int b0, int ntok, int H, int dc, int dv, const float* o_s,
+                             const T* __restrict__ W_UV, float* __restrict__ out) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const T* W = W_UV + static_cast<long long>(h) * dv * dc;
+    constexpr int kRows = 4;
+    if (dc % 256 == 0 && dc <= 1024) {
+        const int nv = dc / 256;  // 16-byte vectors per lane per row
+        for (int j0 = warp * kRows; j0 < dv; j0 += kWarps * kRows) {
+            uint4 wv[kRows][4];
+#pragma unroll
+            for (int q = 0; q < kRows; ++q)
+#pragma unroll
+                for (int v = 0; v < 4; ++v)
+                    if (v < nv && j0 + q < dv)
+                        wv[q][v] = __ldg(reinterpret_cast<const uint4*>(W + static_cast<long long>(j0 + q) * dc +
+                                                                         256 * v + 8 * lane));
+            float acc[kRows][kTok];
+#pragma unroll
+            for (int q = 0; q < kRows; ++q)
+#pragma unroll
+                for (int t = 0; t < kTok; ++t) acc[q][t] = 0.f;
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                if (v >= nv) break;
+#pragma unroll
+                for (int t = 0; t < kTok; ++t) {
+                    if (t >= ntok) break;
+                    const float4 o0 = *reinterpret_cast<const float4*>(o_s + t * dc + 256 * v + 8 * lane);
+                    const float4 o1 = *reinterpret_cast<const float4*>(o_s + t * dc + 256 * v + 8 * lane + 4);
+#pragma unroll
+                    for (int q = 0; q < kRows; ++q) {
+                        const uint32_t* u = reinterpret_cast<const uint32_t*>(&wv[q][v]);
+                        const float2 w0 = ElemTraits<T>::to_f2(*reinterpret_cast<const typename ElemTraits<T>::T2*>(&u[0]));
+                        const float2 w1 = ElemTraits<T>::to_f2(*reinterpret_cast<const typename ElemTraits<T>::T2*>(&u[1]));
+                        const float2 w2 = ElemTraits<T>::to_f2(*reinterpret_cast<const typename ElemTraits<T>::T2*>(&u[2]));
+                        const float2 w3 = ElemTraits<T>::to_f2(*reinterpret_cast<const typename ElemTraits<T>::T2*>(&u[3]));
+                        float a = acc[q][t];
+                        a = fmaf(w0.x, o0.x, a); a = fmaf(w0.y, o0.y, a); a = fmaf(w1.x, o0.z, a); a = fmaf(w1.y, o0.w, a);
+                        a = fmaf(w2.x, o1.x, a); a = fmaf(w2.y, o1.y, a); a = fmaf(w3.x, o1.z, a); a = fmaf(w3.y, o1.w, a);
+                        acc[q][t] = a;
+                    }
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < kRows; ++q) {
+                if (j0 + q >= dv) break;
+#pragma unroll
+                for (int t = 0; t < kTok; ++t) {
+                    if (t >= ntok) break;
+                    float a = acc[q][t];
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+                    if (lane == 0) out[(static_cast<long long>(b0 + t) * H + h) * dv + j0 + q] = a;
+                }
+            }
+        }
+        return;
+    }
+    for (int j = warp; j < dv; j += kWarps) {
+        const T* wr = W + static_cast<long long>(j) * dc;
+        float acc[kTok];
+#pragma unroll
+        for (int t = 0; t < kTok; ++t) acc[t] = 0.f;
+        for (int c = lane; c < dc; c += 32) {
+            const float wv = ElemTraits<T>::to_f(wr[c]);
+#pragma unroll
+            for (int t = 0; t < kTok; ++t)
+                if (t < ntok) acc[t] = fmaf(wv, o_s[t * dc + c], acc[t]);
+        }
+#pragma unroll
+        for (int t = 0; t < kTok; ++t) {
+            if (t >= ntok) break;
+            float a = acc[t];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+            if (lane == 0) out[(static_cast<long long>(b0 + t) * H + h) * dv + j] = a;
+        }
     }
 }
 
@@ -113,94 +181,117 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads)
 combine_kernel(DecodePlan P, const float* __restrict__ rec_ml, const float* __restrict__ rec_o,
                const T* __restrict__ W_UV, float* __restrict__ out, float* part_ml, float* part_o) {
-    extern __shared__ float smem[];
-    float* o_s = smem;                       // kTok * dc
-    float* w_s = o_s + kTok * P.dc;          // dv * (kChunk + 1)
+    extern __shared__ float o_s[];  // kTok * dc
+    __shared__ MergeList ml;
     const int h = blockIdx.x, b0 = blockIdx.y * kTok;
+    const int ntok = (P.B - b0) < kTok ? (P.B - b0) : kTok;
     const int warp = threadIdx.x >> 5;
     if (P.status && *reinterpret_cast<volatile int*>(P.status) != kStatusOk) {
         // the decode kernel gave up on a wait: make the failure visible in the output
-        for (int i = threadIdx.x; i < kTok * P.dv; i += kThreads) {
-            int b = b0 + i / P.dv;
-            if (b < P.B && out) out[(static_cast<long long>(b) * P.H + h) * P.dv + i % P.dv] = __int_as_float(0x7fc00000);
-        }
-        if (part_ml && threadIdx.x < kTok && b0 + static_cast<int>(threadIdx.x) < P.B)
-            part_ml[(static_cast<long long>(b0 + threadIdx.x) * P.H + h) * 2 + 1] = __int_as_float(0x7fc00000);
+        const float nan = __int_as_float(0x7fc00000);
+        for (int i = threadIdx.x; i < ntok * P.dv; i += kThreads)
+            if (out) out[(static_cast<long long>(b0 + i / P.dv) * P.H + h) * P.dv + i % P.dv] = nan;
+        if (part_ml && static_cast<int>(threadIdx.x) < ntok)
+            part_ml[(static_cast<long long>(b0 + threadIdx.x) * P.H + h) * 2 + 1] = nan;
         return;
     }
-    for (int t = warp; t < kTok; t += kThreads / 32) {
-        int b = b0 + t;
-        if (b < P.B) merge_records(P, b, h, rec_ml, rec_o, o_s + t * P.dc, part_ml, part_o);
-        else for (int c = threadIdx.x & 31; c < P.dc; c += 32) o_s[t * P.dc + c] = 0.f;
+    const bool partial = out == nullptr;
+    if (warp < ntok) build_merge_list(P, b0 + warp, h, rec_ml, ml, warp, !partial);
+    __syncthreads();
+    // merge: thread -> (token, column)
+    for (int i = threadIdx.x; i < ntok * P.dc; i += kThreads) {
+        const int t = i / P.dc, c = i % P.dc;
+        const int r = ml.row[t];
+        float a = 0.f;
+        for (int k = 0; k < ml.count[t]; ++k) {
+            const int rec = ml.rec[t][k];
+            if (rec >= 0) a = fmaf(ml.wgt[t][k], rec_o[(static_cast<long long>(rec) * kGroupRows + r) * P.dc + c], a);
+        }
+        if (partial) part_o[(static_cast<long long>(b0 + t) * P.H + h) * P.dc + c] = a;
+        else o_s[t * P.dc + c] = a;
     }
-    if (out == nullptr) return;  // partial-only mode
-    project_wuv<T>(h, b0, P.B, P.H, P.dc, P.dv, o_s, w_s, W_UV, out);
+    if (partial) {
+        if (static_cast<int>(threadIdx.x) < ntok) {
+            const int t = threadIdx.x;
+            float* pm = part_ml + (static_cast<long long>(b0 + t) * P.H + h) * 2;
+            pm[0] = ml.l[t] > 0.f ? ml.m[t] * kLn2 : -INFINITY;  // natural-log units for the caller
+            pm[1] = ml.l[t];
+        }
+        return;
+    }
+    __syncthreads();
+    project_rows<T>(h, b0, ntok, P.H, P.dc, P.dv, o_s, W_UV, out);
 }
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
 combine_parts_kernel(int B, int H, int dc, int dv, int parts, const float* __restrict__ part_ml,
-                     const float* __restrict__ part_o, const T* __restrict__ W_UV,
-                     float* __restrict__ out) {
-    extern __shared__ float smem[];
-    float* o_s = smem;
-    float* w_s = o_s + kTok * dc;
+                     const float* __restrict__ part_o, const T* __restrict__ W_UV, float* __restrict__ out) {
+    extern __shared__ float o_s[];
+    __shared__ float wgt[kTok][64];
     const int h = blockIdx.x, b0 = blockIdx.y * kTok;
+    const int ntok = (B - b0) < kTok ? (B - b0) : kTok;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long stride = static_cast<long long>(B) * H;
-    for (int t = warp; t < kTok; t += kThreads / 32) {
-        int b = b0 + t;
-        float* dst = o_s + t * dc;
-        if (b >= B) {
-            for (int c = lane; c < dc; c += 32) dst[c] = 0.f;
-            continue;
-        }
-        long long bh = static_cast<long long>(b) * H + h;
+    if (warp < ntok) {
+        const long long bh = static_cast<long long>(b0 + warp) * H + h;
         float M = -INFINITY;
-        for (int p = 0; p < parts; ++p) M = fmaxf(M, part_ml[(p * stride + bh) * 2]);
+        for (int p = lane; p < parts; p += 32) {
+            const float* pm = part_ml + (p * stride + bh) * 2;
+            if (pm[1] > 0.f) M = fmaxf(M, pm[0]);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
         float L = 0.f;
-        for (int p = 0; p < parts; ++p) {
-            const float* ml = part_ml + (p * stride + bh) * 2;
-            if (ml[1] > 0.f) L += ml[1] * expf(ml[0] - M);
+        for (int p = lane; p < parts; p += 32) {
+            const float* pm = part_ml + (p * stride + bh) * 2;
+            const float a = pm[1] > 0.f ? expf(pm[0] - M) : 0.f;
+            wgt[warp][p] = a;
+            L += a * pm[1];
         }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
         const float inv = L > 0.f ? 1.f / L : 0.f;
-        for (int c = lane; c < dc; c += 32) {
-            float a = 0.f;
-            for (int p = 0; p < parts; ++p) {
-                const float* ml = part_ml + (p * stride + bh) * 2;
-                if (ml[1] > 0.f) a += expf(ml[0] - M) * part_o[(p * stride + bh) * dc + c];
-            }
-            dst[c] = a * inv;
-        }
+        __syncwarp();
+        for (int p = lane; p < parts; p += 32) wgt[warp][p] *= inv;
     }
-    project_wuv<T>(h, b0, B, H, dc, dv, o_s, w_s, W_UV, out);
-}
-
-static size_t combine_smem(int dc, int dv) {
-    return (static_cast<size_t>(kTok) * dc + static_cast<size_t>(dv) * (kChunk + 1)) * sizeof(float);
+    __syncthreads();
+    for (int i = threadIdx.x; i < ntok * dc; i += kThreads) {
+        const int t = i / dc, c = i % dc;
+        const long long bh = static_cast<long long>(b0 + t) * H + h;
+        float a = 0.f;
+        for (int p = 0; p < parts; ++p) a = fmaf(wgt[t][p], part_o[(p * stride + bh) * dc + c], a);
+        o_s[t * dc + c] = a;
+    }
+    __syncthreads();
+    project_rows<T>(h, b0, ntok, H, dc, dv, o_s, W_UV, out);
 }
 
 template <typename T>
 cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
                            float* out, float* part_ml, float* part_o, cudaStream_t s) {
-    size_t smem = combine_smem(P.dc, P.dv);
+    if (P.W > kMaxRec) return cudaErrorInvalidValue;
+    const size_t smem = static_cast<size_t>(kTok) * P.dc * sizeof(float);
     cudaError_t e = cudaFuncSetAttribute(combine_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     dim3 grid(P.H, ceil_div(P.B, kTok));
     combine_kernel<T><<<grid, kThreads, smem, s>>>(P, rec_ml, rec_o, W_UV, out, part_ml, part_o);
+    count_launches(1);
     return cudaGetLastError();
 }
 
 template <typename T>
 cudaError_t launch_combine_parts(int B, int H, int dc, int dv, int parts, const float* part_ml,
                                  const float* part_o, const T* W_UV, float* out, cudaStream_t s) {
-    size_t smem = combine_smem(dc, dv);
+    if (parts > 64) return cudaErrorInvalidValue;
+    const size_t smem = static_cast<size_t>(kTok) * dc * sizeof(float);
     cudaError_t e = cudaFuncSetAttribute(combine_parts_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     dim3 grid(H, ceil_div(B, kTok));
     combine_parts_kernel<T><<<grid, kThreads, smem, s>>>(B, H, dc, dv, parts, part_ml, part_o, W_UV, out);
+    count_launches(1);
     return cudaGetLastError();
 }
 

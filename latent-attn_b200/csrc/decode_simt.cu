@@ -166,6 +166,7 @@ cudaError_t launch_decode_simt(const DecodePlan& P, const T* kv, const T* qpack,
     if (e != cudaSuccess) return e;
     dim3 grid(P.W, kGroupRows / kWarps);
     decode_simt_kernel<T><<<grid, kWarps * 32, smem, s>>>(P, kv, qpack, cos, sin, rec_ml, rec_o);
+    count_launches(1);
     return cudaGetLastError();
 }
 

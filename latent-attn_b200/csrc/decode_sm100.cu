@@ -22,7 +22,10 @@
 //   warp 1      TMEM allocator + MMA issuer (one lane)
 //   warps 2-3   tile transform: zero rows past the sequence end; CTA 0 also
 //               rotates k_rope in place with the caller's fp32 cos/sin tables
-//               (the rotation of src/fused_mla.cu:34-54 of the reference)
+//               (the rotation of src/fused_mla.cu:34-54 of the reference). The
+//               producer streams each tile's 64 table rows (2 x 8 KB) with TMA into
+//               a 2-slot ring next to the cache chunks, so the rotation never waits
+//               on a global-memory round trip.
 //   warps 4-7   softmax / correction / epilogue: thread t owns query row t
 // Softmax is online in log2 units (Q is pre-scaled by softmax_scale * log2 e) with
 // a lazy rescale: the running max only moves when a tile's max exceeds it by more
@@ -44,6 +47,8 @@ constexpr int kTileN = 64;                       // positions per tile
 constexpr int kStages = 3;
 constexpr int kChunkBytes = 64 * 128;            // 64 rows x 64 elements (128 B), 128-byte swizzle
 constexpr int kStageBytes = 5 * kChunkBytes;     // CTA 0 uses 5 chunks, CTA 1 uses 4
+constexpr int kTabBytes = 64 * 32 * 4;           // cos (or sin) rows of one tile, fp32
+constexpr int kTabSlotBytes = 2 * kTabBytes;     // cos | sin
 constexpr int kPBytes = 128 * 128;               // P: 128 rows x 64 positions x 2 B
 constexpr int kXBytes = 128 * 128;               // exchanged partial score: 128 x 64 fp16
 constexpr int kThreads = 256;
@@ -64,14 +69,25 @@ struct __align__(8) Barriers {
     uint64_t x_full[2];
     uint64_t p_full[2];
     uint64_t pv_done[2];
+    uint64_t tab_empty[2];
     uint64_t q_ready, drain, done;
     uint32_t tmem_base;
 };
 
-constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 2 * kPBytes + 2 * kXBytes +
-                              sizeof(Barriers) + 1024;
+constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 2 * kTabSlotBytes + 2 * kPBytes +
+                              2 * kXBytes + sizeof(Barriers) + 1024;
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 __device__ __forceinline__ int code(int site) { return kStatusTimeout | (site << 8); }
+
+// Diagnostics after a wait gave up: status[1] counts failures, status[2] holds
+// the first failing (block + 1) << 16 | tile, status[3] ORs the failing sites.
+__device__ __forceinline__ void note_fail(volatile int* err, int site, int tile) {
+    int* e = const_cast<int*>(err);
+    atomicAdd(e + 1, 1);
+    atomicCAS(e + 2, 0, ((static_cast<int>(blockIdx.x) + 1) << 16) | (tile & 0xFFFF));
+    atomicOr(e + 3, 1 << site);
+}
 
 // Walks the worker's tiles; every role advances an identical copy.
 struct TileIter {
@@ -132,13 +148,14 @@ __device__ __forceinline__ float2 unpack2(uint32_t v) {
 
 template <typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P, const T* __restrict__ qpack,
-                    const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
+decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_cos,
+                    const __grid_constant__ CUtensorMap tmap_sin, const DecodePlan P, const T* __restrict__ qpack,
                     float* __restrict__ rec_ml, float* __restrict__ rec_o) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     unsigned char* stages = smem;
-    unsigned char* pbuf = stages + kStages * kStageBytes;
+    unsigned char* tabs = stages + kStages * kStageBytes;
+    unsigned char* pbuf = tabs + 2 * kTabSlotBytes;
     unsigned char* xbuf = pbuf + 2 * kPBytes;
     Barriers* bars = reinterpret_cast<Barriers*>(xbuf + 2 * kXBytes);
 
@@ -166,6 +183,8 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P
             mbar_init(smem_u32(&bars->p_full[j]), 128);
             mbar_init(smem_u32(&bars->pv_done[j]), 1);
         }
+        mbar_init(smem_u32(&bars->tab_empty[0]), 64);
+        mbar_init(smem_u32(&bars->tab_empty[1]), 64);
         mbar_init(smem_u32(&bars->q_ready), 128);
         mbar_init(smem_u32(&bars->drain), 1);
         mbar_init(smem_u32(&bars->done), 1);
@@ -175,7 +194,13 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P
         tmem_alloc(smem_u32(&bars->tmem_base), kTmemCols);
         tmem_relinquish();
     }
-    if (warp == 0 && lane == 0) tma_prefetch_desc(&tmap);
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmap);
+        if (rank == 0) {
+            tma_prefetch_desc(&tmap_cos);
+            tma_prefetch_desc(&tmap_sin);
+        }
+    }
     tc_fence_before();
     cluster_sync();  // both CTAs: barriers initialised, TMEM allocated
     tc_fence_after();
@@ -184,6 +209,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P
     const int nchunks = rank == 0 ? 5 : 4;
     const int ksteps = rank == 0 ? 20 : 16;   // score K / 16
     const uint32_t stages_u32 = smem_u32(stages);
+    const uint32_t tabs_u32 = smem_u32(tabs);
     const uint32_t pbuf_u32 = smem_u32(pbuf);
     const uint32_t xbuf_u32 = smem_u32(xbuf);
 
@@ -195,15 +221,28 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P
             for (int i = 0; it.valid(); ++i, it.next(P)) {
                 const int st = i % kStages;
                 if (i >= kStages &&
-                    !mbar_wait(smem_u32(&bars->kv_empty[st]), ((i / kStages) - 1) & 1, err, code(kWaitProducer)))
+                    !mbar_wait(smem_u32(&bars->kv_empty[st]), ((i / kStages) - 1) & 1, err, code(kWaitProducer))) {
+                    note_fail(err, kWaitProducer, i);
                     break;
+                }
+                if (rank == 0 && i >= 2 &&
+                    !mbar_wait(smem_u32(&bars->tab_empty[i & 1]), ((i - 2) >> 1) & 1, err, code(kWaitProducer))) {
+                    note_fail(err, kWaitProducer, i);
+                    break;
+                }
                 const uint32_t full = smem_u32(&bars->kv_full[st]);
-                mbar_arrive_expect_tx(full, nchunks * kChunkBytes);
+                mbar_arrive_expect_tx(full, nchunks * kChunkBytes + (rank == 0 ? kTabSlotBytes : 0));
                 const int y = static_cast<int>(it.row0 + it.pos0());
                 const uint32_t dst = stages_u32 + st * kStageBytes;
                 for (int j = 0; j < nchunks; ++j) {
                     const int x = rank == 0 ? (j < 4 ? 64 * j : 512) : 256 + 64 * j;
                     tma_load_2d(dst + j * kChunkBytes, &tmap, full, x, y);
+                }
+                if (rank == 0) {
+                    const int yt = P.kv_pos_offset + it.pos0();
+                    const uint32_t tdst = tabs_u32 + (i & 1) * kTabSlotBytes;
+                    tma_load_2d(tdst, &tmap_cos, full, 0, yt);
+                    tma_load_2d(tdst + kTabBytes, &tmap_sin, full, 0, yt);
                 }
             }
         }
@@ -245,7 +284,9 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P
                 tc_fence_after();
                 issue_score(0);
             }
+            int fail_i = 0;
             for (int i = 0; ok && it.valid(); ++i) {
+                fail_i = i;
                 TileIter nx = it;
                 nx.next(P);
                 const bool has_next = nx.valid();
@@ -270,6 +311,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P
                 }
                 it = nx;
             }
+            if (!ok) note_fail(err, kWaitMmaP, fail_i);
             // drain: every MMA this thread issued has completed before teardown
             mma_commit(smem_u32(&bars->drain));
             mbar_wait(smem_u32(&bars->drain), 0, err, code(kWaitDrain));
@@ -281,7 +323,10 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P
         it.init(P, tb, te);
         for (int i = 0; it.valid(); ++i, it.next(P)) {
             const int st = i % kStages;
-            if (!mbar_wait(smem_u32(&bars->kv_full[st]), (i / kStages) & 1, err, code(kWaitTransform))) break;
+            if (!mbar_wait(smem_u32(&bars->kv_full[st]), (i / kStages) & 1, err, code(kWaitTransform))) {
+                note_fail(err, kWaitTransform, i);
+                break;
+            }
             unsigned char* sp = stages + st * kStageBytes;
             const int np = it.np();
             if (np < kTileN) {
@@ -296,14 +341,14 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P
             if (rank == 0) {
                 // rotate-half RoPE on the k_rope chunk: pairs (d, d + 32), d = lane
                 unsigned char* rc = sp + 4 * kChunkBytes;
-                const long long pbase = static_cast<long long>(P.kv_pos_offset) + it.pos0();
+                const float* tc = reinterpret_cast<const float*>(tabs + (i & 1) * kTabSlotBytes);
+                const float* ts = tc + kTabBytes / 4;
                 const int d = lane;
                 const int sub = warp - 2;
 #pragma unroll 4
                 for (int p = sub; p < np; p += 2) {
-                    const long long pos = pbase + p;
-                    const float cs = __ldg(rope_cos + pos * 32 + d);
-                    const float sn = __ldg(rope_sin + pos * 32 + d);
+                    const float cs = tc[p * 32 + d];
+                    const float sn = ts[p * 32 + d];
                     T* e0 = reinterpret_cast<T*>(rc + p * 128 + ((((d >> 3)) ^ (p & 7)) << 4) + ((d & 7) << 1));
                     T* e1 = reinterpret_cast<T*>(rc + p * 128 + ((((d >> 3) + 4) ^ (p & 7)) << 4) + ((d & 7) << 1));
                     const float k0 = ElemTraits<T>::to_f(*e0), k1 = ElemTraits<T>::to_f(*e1);
@@ -313,6 +358,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P
             }
             fence_proxy_async_smem();
             mbar_arrive(smem_u32(&bars->tile_ready[st]));
+            if (rank == 0) mbar_arrive(smem_u32(&bars->tab_empty[i & 1]));
         }
     } else {
         // ------------------------------------------------------------ softmax warpgroup
@@ -349,7 +395,10 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P
         for (int i = 0; it.valid(); ++i, it.next(P)) {
             const int slot = i & 1;
             if (t == 0) mbar_arrive_expect_tx(smem_u32(&bars->x_full[slot]), kXBytes);
-            if (!mbar_wait(smem_u32(&bars->s_full), i & 1, err, code(kWaitSoftS))) break;
+            if (!mbar_wait(smem_u32(&bars->s_full), i & 1, err, code(kWaitSoftS))) {
+                note_fail(err, kWaitSoftS, i);
+                break;
+            }
             tc_fence_after();
             uint32_t sr[64];
             tmem_ld32(taddr_row + kColS, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
@@ -367,7 +416,10 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P
             for (int c = 0; c < 8; ++c)
                 st_async_v4(x_row_remote + slot * kXBytes + ((c ^ sw) << 4), h[4 * c], h[4 * c + 1], h[4 * c + 2],
                             h[4 * c + 3], rbar);
-            if (!mbar_wait_cluster(smem_u32(&bars->x_full[slot]), (i >> 1) & 1, err, code(kWaitSoftX))) break;
+            if (!mbar_wait_cluster(smem_u32(&bars->x_full[slot]), (i >> 1) & 1, err, code(kWaitSoftX))) {
+                note_fail(err, kWaitSoftX, i);
+                break;
+            }
 
             // full score = fp16(own) + fp16(peer), identical in both CTAs
             float s[64];
@@ -414,8 +466,10 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P
             }
             l_run += lsum;
             // P slot is free once PV(i-2) has completed
-            if (i >= 2 && !mbar_wait(smem_u32(&bars->pv_done[slot]), ((i - 2) >> 1) & 1, err, code(kWaitSoftPV)))
+            if (i >= 2 && !mbar_wait(smem_u32(&bars->pv_done[slot]), ((i - 2) >> 1) & 1, err, code(kWaitSoftPV))) {
+                note_fail(err, kWaitSoftPV, i);
                 break;
+            }
 #pragma unroll
             for (int c = 0; c < 8; ++c)
                 asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(p_row + slot * kPBytes + ((c ^ sw) << 4)),
@@ -478,7 +532,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const DecodePlan P
     if (threadIdx.x == 0) {
         // the pair finishes together: no CTA leaves while the other may still address it
         mbar_arrive_remote(mapa(smem_u32(&bars->done), peer));
-        mbar_wait_cluster(smem_u32(&bars->done), 0, err, code(kWaitTeardown));
+        if (!mbar_wait_cluster(smem_u32(&bars->done), 0, err, code(kWaitTeardown))) note_fail(err, kWaitTeardown, 0);
     }
     __syncthreads();
     tc_fence_after();
@@ -491,14 +545,18 @@ template <typename T>
 cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
                                 const float* sin, float* rec_ml, float* rec_o, cudaStream_t s) {
     if (P.dc != 512 || P.dR != 64 || P.tile != kTileN) return cudaErrorInvalidValue;
-    CUtensorMap tmap;
+    CUtensorMap tmap, tcos, tsin;
+    // tables hold kv_pos_offset + max_len rows of d_R / 2 = 32 floats
+    const uint64_t trows = static_cast<uint64_t>(P.kv_pos_offset) + static_cast<uint64_t>(P.max_len);
     if (!make_tmap_2d_16b(&tmap, kv, static_cast<uint64_t>(P.kv_rows), 576, static_cast<uint64_t>(P.row_stride),
-                          64, 64))
+                          64, 64) ||
+        !make_tmap_2d_f32(&tcos, cos, trows, 32, 32, 64, 32) || !make_tmap_2d_f32(&tsin, sin, trows, 32, 32, 64, 32))
         return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(decode_sm100_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
-    decode_sm100_kernel<T><<<2 * P.W, kThreads, kSmemBytes, s>>>(tmap, P, qpack, cos, sin, rec_ml, rec_o);
+    decode_sm100_kernel<T><<<2 * P.W, kThreads, kSmemBytes, s>>>(tmap, tcos, tsin, P, qpack, rec_ml, rec_o);
+    count_launches(1);
     return cudaGetLastError();
 }
 

@@ -6,6 +6,7 @@
 // errors those the torch binding rejects (csrc/bindings.cpp:28-40, 146-152,
 // 208-221); here they become status codes with a thread-local message instead of
 // exceptions, and nothing ever exits, aborts or synchronises the host.
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -17,6 +18,16 @@
 
 #include "latent_attn_b200/mla.h"
 #include "mla_internal.cuh"
+
+struct mla_timer_st {
+    cudaEvent_t begin = nullptr, end = nullptr;
+    bool recorded = false;
+};
+
+namespace mla {
+static std::atomic<uint64_t> g_launches{0};
+void count_launches(int n) { g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed); }
+}  // namespace mla
 
 namespace {
 
@@ -120,6 +131,8 @@ mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan
         return fail(MLA_ERR_UNSUPPORTED, "kv_row_stride must be a multiple of 8 elements (got %lld)", (long long)stride);
     if (reinterpret_cast<uintptr_t>(a->kv_cache) % 16 != 0)
         return fail(MLA_ERR_INVALID_ARGUMENT, "kv_cache must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(a->W_UV) % 16 != 0 || (a->W_UK && reinterpret_cast<uintptr_t>(a->W_UK) % 16 != 0))
+        return fail(MLA_ERR_INVALID_ARGUMENT, "W_UV / W_UK must be 16-byte aligned");
     if (a->shared_cache && a->kv_offsets)
         return fail(MLA_ERR_INVALID_ARGUMENT, "kv_offsets must be null with shared_cache");
 
@@ -178,6 +191,7 @@ mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan
     }
     if (T > (1LL << 30)) return fail(MLA_ERR_UNSUPPORTED, "too many positions");
     int cap = use_tc ? di.sms / 2 : 64;
+    if (cap > 128) cap = 128;  // the combine kernel merges at most 128 records per row
     if (cap < 1) cap = 1;
     int W = cap;
     if (T >= 0 && T < W) W = T > 0 ? static_cast<int>(T) : 1;
@@ -217,6 +231,10 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
                               d.uniform_len > 0 ? nullptr : prefix, s);
     if (e != cudaSuccess) return cuda_fail(e, "pack kernel launch");
     const T* kv = reinterpret_cast<const T*>(a->kv_cache);
+    if (a->timer) {
+        e = cudaEventRecord(a->timer->begin, s);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(timer)");
+    }
     if (pl.use_tc)
         e = mla::launch_decode_sm100<T>(d, kv, qpack, a->rope_cos, a->rope_sin, rec_ml, rec_o, s);
     else
@@ -224,6 +242,11 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
     if (e == cudaErrorNoKernelImageForDevice || e == cudaErrorInvalidDeviceFunction)
         return fail(MLA_ERR_NO_DEVICE_CODE, "decode kernel: %s (library is built for sm_100a)", cudaGetErrorString(e));
     if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
+    if (a->timer) {
+        e = cudaEventRecord(a->timer->end, s);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(timer)");
+        a->timer->recorded = true;
+    }
     e = mla::launch_combine<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, part_ml, part_o, s);
     if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
     return MLA_OK;
@@ -360,6 +383,39 @@ mla_status_t mla_launch_batched_fused(const mla_batched_fused_params_t* p, mla_d
     a.output = p->output;
     return decode_with_pool(p->cfg, &a, reinterpret_cast<cudaStream_t>(stream));
 }
+
+mla_status_t mla_timer_create(mla_timer_t* timer) {
+    if (!timer) return fail(MLA_ERR_INVALID_ARGUMENT, "timer is null");
+    auto* t = new mla_timer_st();
+    cudaError_t e = cudaEventCreate(&t->begin);
+    if (e == cudaSuccess) e = cudaEventCreate(&t->end);
+    if (e != cudaSuccess) {
+        if (t->begin) cudaEventDestroy(t->begin);
+        delete t;
+        return cuda_fail(e, "cudaEventCreate");
+    }
+    *timer = t;
+    return MLA_OK;
+}
+
+mla_status_t mla_timer_destroy(mla_timer_t timer) {
+    if (!timer) return MLA_OK;
+    cudaEventDestroy(timer->begin);
+    cudaEventDestroy(timer->end);
+    delete timer;
+    return MLA_OK;
+}
+
+mla_status_t mla_timer_decode_ms(mla_timer_t timer, float* ms) {
+    if (!timer || !ms) return fail(MLA_ERR_INVALID_ARGUMENT, "null argument");
+    if (!timer->recorded) return fail(MLA_ERR_INVALID_ARGUMENT, "timer has not been used by a decode call");
+    cudaError_t e = cudaEventSynchronize(timer->end);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(ms, timer->begin, timer->end);
+    if (e != cudaSuccess) return cuda_fail(e, "timer");
+    return MLA_OK;
+}
+
+uint64_t mla_kernel_launch_count(void) { return mla::g_launches.load(std::memory_order_relaxed); }
 
 const char* mla_last_error(void) { return g_last_error.c_str(); }
 

@@ -133,6 +133,9 @@ template <> struct ElemTraits<__nv_bfloat16> {
 // Device error codes written to DecodePlan::status.
 enum : int { kStatusOk = 0, kStatusTimeout = 1, kStatusBadPlan = 2 };
 
+// Process-wide count of kernels launched by this library (mla_kernel_launch_count).
+void count_launches(int n);
+
 // ---- kernel launchers (defined in the .cu files; return cudaGetLastError()) ----
 // pack.cu
 template <typename T>

@@ -67,53 +67,82 @@ __global__ void pack_q_copy_kernel(DecodePlan P, const float* __restrict__ q_abs
     }
 }
 
-// Absorption: block (h, token chunk). W_UK[h] is (dn, dc) row-major; every thread
-// owns output columns c = threadIdx.x + k * blockDim.x and streams over i, so a
-// warp reads 32 consecutive W_UK elements per step. kTok tokens share each load.
+// Absorption: block (h, chunk of kTok tokens), 256 threads. W_UK[h] is (dn, dc)
+// row-major. Thread (rg, cg) owns the 8 output columns [8 cg, 8 cg + 8) and the
+// rows i = rg, rg + RG, ... (RG = 256 / (dc / 8) row groups): it streams 16-byte
+// vectors of W_UK, so the block keeps 256 independent loads in flight and reads
+// W_UK[h] exactly once per token chunk. Row-group partial sums are reduced
+// through shared memory.
 template <typename T, int kTok>
-__global__ void pack_q_absorb_kernel(DecodePlan P, const float* __restrict__ q_nope,
-                                     const T* __restrict__ W_UK, const float* __restrict__ q_rope,
-                                     float q_scale, T* __restrict__ qpack, int* tile_prefix_out) {
+__global__ void __launch_bounds__(256)
+pack_q_absorb_kernel(DecodePlan P, const float* __restrict__ q_nope, const T* __restrict__ W_UK,
+                     const float* __restrict__ q_rope, float q_scale, T* __restrict__ qpack,
+                     int* tile_prefix_out) {
     if (tile_prefix_out && blockIdx.x == 0 && blockIdx.y == 0) write_tile_prefix(P, tile_prefix_out);
-    extern __shared__ float qn_s[];  // (kTok, dn)
+    extern __shared__ float smem[];
     const int h = blockIdx.x;
     const int b0 = blockIdx.y * kTok;
     const int dn = P.dn, dc = P.dc, K = P.dc + P.dR;
+    const int ntok = (P.B - b0) < kTok ? (P.B - b0) : kTok;
+    float* qn_s = smem;                    // kTok * dn
+    float* red = smem + kTok * dn;         // RG * kTok * dc partial sums
     for (int i = threadIdx.x; i < kTok * dn; i += blockDim.x) {
         int t = i / dn, d = i % dn;
-        int b = b0 + t;
-        qn_s[i] = b < P.B ? q_nope[(static_cast<long long>(b) * P.H + h) * dn + d] : 0.f;
+        qn_s[i] = t < ntok ? q_nope[(static_cast<long long>(b0 + t) * P.H + h) * dn + d] : 0.f;
     }
     __syncthreads();
+    const int ncg = dc / 8;                       // column groups (dc is a multiple of 32)
+    const int RG = blockDim.x / ncg > 0 ? blockDim.x / ncg : 1;
     const T* W = W_UK + static_cast<long long>(h) * dn * dc;
-    for (int c = threadIdx.x; c < dc; c += blockDim.x) {
-        float acc[kTok];
+    for (int cg0 = 0; cg0 < ncg; cg0 += blockDim.x / RG) {
+        const int cg = cg0 + static_cast<int>(threadIdx.x) % (blockDim.x / RG);
+        const int rg = static_cast<int>(threadIdx.x) / (blockDim.x / RG);
+        float acc[kTok][8];
 #pragma unroll
-        for (int t = 0; t < kTok; ++t) acc[t] = 0.f;
-        for (int i = 0; i < dn; ++i) {
-            float w = ElemTraits<T>::to_f(W[static_cast<long long>(i) * dc + c]);
+        for (int t = 0; t < kTok; ++t)
 #pragma unroll
-            for (int t = 0; t < kTok; ++t) acc[t] = fmaf(qn_s[t * dn + i], w, acc[t]);
-        }
+            for (int e = 0; e < 8; ++e) acc[t][e] = 0.f;
+        if (cg < ncg && rg < RG) {
+#pragma unroll 4
+            for (int i = rg; i < dn; i += RG) {
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(W + static_cast<long long>(i) * dc + 8 * cg));
+                const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+                float w[8];
 #pragma unroll
-        for (int t = 0; t < kTok; ++t) {
-            int b = b0 + t;
-            if (b >= P.B) break;
-            int flat = b * P.H + h;  // output row
-            long long qrow;
-            if (P.shared) qrow = flat;  // groups of 128 flattened rows
-            else qrow = static_cast<long long>(b) * P.head_blocks * kGroupRows + h;
-            qpack[qrow * K + c] = ElemTraits<T>::from_f(acc[t] * q_scale);
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = ElemTraits<T>::to_f2(*reinterpret_cast<const typename ElemTraits<T>::T2*>(&u[e]));
+                    w[2 * e] = f.x;
+                    w[2 * e + 1] = f.y;
+                }
+#pragma unroll
+                for (int t = 0; t < kTok; ++t) {
+                    const float q = qn_s[t * dn + i];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[t][e] = fmaf(q, w[e], acc[t][e]);
+                }
+            }
+            for (int t = 0; t < ntok; ++t)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) red[(rg * kTok + t) * dc + 8 * cg + e] = acc[t][e];
         }
     }
+    __syncthreads();
+    for (int i = threadIdx.x; i < ntok * dc; i += blockDim.x) {
+        const int t = i / dc, c = i % dc;
+        float a = 0.f;
+        for (int rg = 0; rg < RG; ++rg) a += red[(rg * kTok + t) * dc + c];
+        const int b = b0 + t;
+        const long long qrow = P.shared ? static_cast<long long>(b) * P.H + h
+                                        : static_cast<long long>(b) * P.head_blocks * kGroupRows + h;
+        qpack[qrow * K + c] = ElemTraits<T>::from_f(a * q_scale);
+    }
     // rope part
-    for (int i = threadIdx.x; i < kTok * P.dR; i += blockDim.x) {
-        int t = i / P.dR, j = i % P.dR;
-        int b = b0 + t;
-        if (b >= P.B) continue;
-        int flat = b * P.H + h;
-        long long qrow = P.shared ? flat : static_cast<long long>(b) * P.head_blocks * kGroupRows + h;
-        qpack[qrow * K + dc + j] =
+    for (int i = threadIdx.x; i < ntok * P.dR; i += blockDim.x) {
+        const int t = i / P.dR, j = i % P.dR;
+        const int b = b0 + t;
+        const int flat = b * P.H + h;
+        const long long qrow = P.shared ? flat : static_cast<long long>(b) * P.head_blocks * kGroupRows + h;
+        qpack[qrow * K + P.dc + j] =
             ElemTraits<T>::from_f(q_rope[static_cast<long long>(flat) * P.dR + j] * q_scale);
     }
 }
@@ -141,17 +170,27 @@ cudaError_t launch_pack_q(const DecodePlan& P, const float* q_absorbed, const fl
     if (q_absorbed) {
         pack_q_copy_kernel<T><<<blocks, 256, 0, s>>>(P, q_absorbed, q_rope, q_scale, qpack,
                                                      tile_prefix_out);
+        count_launches(1);
         return cudaGetLastError();
     }
     bool has_pad = P.shared ? (P.B * P.H) % kGroupRows != 0 : P.H % kGroupRows != 0;
     if (has_pad) {
         pack_q_zero_pad_kernel<T><<<blocks, 256, 0, s>>>(P, qpack);
+        count_launches(1);
     }
     constexpr int kTok = 4;
     dim3 grid(P.H, ceil_div(P.B, kTok));
-    size_t smem = static_cast<size_t>(kTok) * P.dn * sizeof(float);
+    const int ncg = P.dc / 8;
+    const int RG = 256 / ncg > 0 ? 256 / ncg : 1;
+    size_t smem = (static_cast<size_t>(kTok) * P.dn + static_cast<size_t>(RG) * kTok * P.dc) * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(pack_q_absorb_kernel<T, kTok>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
     pack_q_absorb_kernel<T, kTok><<<grid, 256, smem, s>>>(P, q_nope, W_UK, q_rope, q_scale, qpack,
                                                           tile_prefix_out);
+    count_launches(1);
     return cudaGetLastError();
 }
 

@@ -67,7 +67,8 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 
 def _decode_args(dtype, batch, shared, kv_cache, max_seq_len, q_rope, W_UV, rope_cos, rope_sin, out,
                  q_absorbed=None, q_nope=None, W_UK=None, seq_lens=None, kv_offsets=None,
-                 seq_lens_host=None, kv_pos_offset=0, softmax_scale=0.0, kv_row_stride=0, kernel=0):
+                 seq_lens_host=None, kv_pos_offset=0, softmax_scale=0.0, kv_row_stride=0, kernel=0,
+                 timer=None):
     a = _lib.MlaDecodeArgs()
     a.dtype = _DT[dtype]
     a.batch = int(batch)
@@ -90,6 +91,7 @@ def _decode_args(dtype, batch, shared, kv_cache, max_seq_len, q_rope, W_UV, rope
     a.softmax_scale = float(softmax_scale)
     a.output = _ptr(out)
     a.kernel = int(kernel)
+    a.timer = timer.handle if timer is not None else None
     return a
 
 
@@ -254,7 +256,7 @@ def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
                seq_lens_host: Optional[Sequence[int]] = None, shared_cache: bool = False,
                kv_pos_offset: int = 0, softmax_scale: float = 0.0, kv_row_stride: int = 0,
                kernel: int = 0, out: Optional[torch.Tensor] = None,
-               workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+               workspace: Optional[torch.Tensor] = None, timer=None) -> torch.Tensor:
     """General decode: (B, H, dv) fp32 for B sequences (or B tokens over one shared cache).
 
     Give ``q_absorbed`` (B, H, d_c) fp32, or ``q_nope`` (B, H, dn) fp32 with ``W_UK``
@@ -308,14 +310,14 @@ def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
                 rope_sin, out, workspace=workspace, q_absorbed=q_absorbed, q_nope=q_nope, W_UK=W_UK,
                 seq_lens=seq_lens, kv_offsets=kv_offsets, seq_lens_host=host_arr,
                 kv_pos_offset=kv_pos_offset, softmax_scale=softmax_scale, kv_row_stride=kv_row_stride,
-                kernel=kernel)
+                kernel=kernel, timer=timer)
     return out
 
 
 def mla_decode_partial(kv_cache, q_rope, W_UV, rope_cos, rope_sin, d_model, kv_lora_rank,
                        qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim, *,
                        q_absorbed=None, q_nope=None, W_UK=None, kv_pos_offset: int = 0,
-                       softmax_scale: float = 0.0, workspace=None):
+                       softmax_scale: float = 0.0, workspace=None, kernel: int = 0, timer=None):
     """One KV-range shard of a single-token-per-sequence decode over all rows of
     ``kv_cache`` (B sequences of ``kv_cache.size(0) // B`` rows). Returns
     (ml (B, H, 2), o (B, H, d_c)): natural-log max, sum of exponentials, and the
@@ -329,7 +331,7 @@ def mla_decode_partial(kv_cache, q_rope, W_UV, rope_cos, rope_sin, d_model, kv_l
     args = _decode_args(kv_cache.dtype, B, False, kv_cache, L, q_rope, W_UV, rope_cos, rope_sin, None,
                         q_absorbed=q_absorbed, q_nope=None if q_absorbed is not None else q_nope,
                         W_UK=None if q_absorbed is not None else W_UK, kv_pos_offset=kv_pos_offset,
-                        softmax_scale=softmax_scale)
+                        softmax_scale=softmax_scale, kernel=kernel, timer=timer)
     ws = _workspace(cfg, args, kv_cache.device, workspace)
     lib = _lib.load()
     _lib.check(lib.mla_decode_partial(C.byref(cfg), C.byref(args), C.c_void_p(ml.data_ptr()),

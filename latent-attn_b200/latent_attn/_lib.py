@@ -57,7 +57,7 @@ class MlaDecodeArgs(C.Structure):
                 ("kv_pos_offset", C.c_int), ("q_absorbed", C.c_void_p), ("q_nope", C.c_void_p),
                 ("W_UK", C.c_void_p), ("q_rope", C.c_void_p), ("W_UV", C.c_void_p),
                 ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p), ("softmax_scale", C.c_float),
-                ("output", C.c_void_p), ("kernel", C.c_int)]
+                ("output", C.c_void_p), ("kernel", C.c_int), ("timer", C.c_void_p)]
 
 KERNEL_AUTO = 0
 KERNEL_TENSOR_CORE = 1
@@ -77,6 +77,10 @@ SIGNATURES = {
                                      C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "mla_combine_partials": (C.c_int, [C.POINTER(MlaConfig), C.c_int, C.c_int, C.c_int, C.c_void_p,
                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "mla_timer_create": (C.c_int, [C.POINTER(C.c_void_p)]),
+    "mla_timer_destroy": (C.c_int, [C.c_void_p]),
+    "mla_timer_decode_ms": (C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
+    "mla_kernel_launch_count": (C.c_uint64, []),
     "mla_last_error": (C.c_char_p, []),
     "mla_version": (C.c_char_p, []),
 }
@@ -117,3 +121,34 @@ def check(status: int) -> None:
     if status != MLA_OK:
         msg = load().mla_last_error()
         raise MlaError(status, msg.decode() if msg else "")
+
+
+class DecodeTimer:
+    """Owns an mla_timer_t; pass ``.handle`` as ``timer=`` to a decode call, then
+    read ``decode_ms()`` (waits for the decode kernel of that call)."""
+
+    def __init__(self):
+        lib = load()
+        h = C.c_void_p()
+        check(lib.mla_timer_create(C.byref(h)))
+        self.handle = h.value
+
+    def decode_ms(self) -> float:
+        ms = C.c_float(0.0)
+        check(load().mla_timer_decode_ms(C.c_void_p(self.handle), C.byref(ms)))
+        return float(ms.value)
+
+    def close(self):
+        if self.handle:
+            load().mla_timer_destroy(C.c_void_p(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def kernel_launch_count() -> int:
+    return int(load().mla_kernel_launch_count())
