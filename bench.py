@@ -339,6 +339,7 @@ def main():
     ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     dec_ms = []
+    status_errors = 0
     launches0 = _lib.kernel_launch_count()
     barrier()
     clocks.mark(True)
@@ -348,6 +349,8 @@ def main():
         step(t=timer)
         ev1[k].record(stream)
         dec_ms.append(timer.decode_ms())
+        if int(ws[:4].view(torch.int32)[0]) != 0:  # device status word of the decode kernel
+            status_errors += 1
     barrier()
     clocks.mark(False)
     launches = _lib.kernel_launch_count() - launches0
@@ -425,6 +428,8 @@ def main():
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_max / args.steps, 5),
                     "api": "latent_attn.functional.mla_decode (q_nope/q_rope pinned host -> device, output -> host)"},
             "gpu_launches": int(launches),
+            "decode_status_errors": status_errors,
+            "output_finite": bool(torch.isfinite(out).all()),
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)

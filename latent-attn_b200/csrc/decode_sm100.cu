@@ -61,6 +61,10 @@ enum : int { kWaitProducer = 1, kWaitTransform = 2, kWaitMmaTile = 3, kWaitMmaSF
              kWaitMmaQ = 6, kWaitSoftS = 7, kWaitSoftX = 8, kWaitSoftPV = 9, kWaitTeardown = 10,
              kWaitDrain = 11 };
 
+// Warp-uniform success: every early exit of a warp that runs warp-collective
+// instructions (tcgen05.ld/st, vote) happens with all 32 lanes together.
+__device__ __forceinline__ bool warp_ok(bool ok) { return __all_sync(0xffffffffu, ok); }
+
 struct __align__(8) Barriers {
     uint64_t kv_full[kStages];
     uint64_t kv_empty[kStages];
@@ -125,6 +129,12 @@ struct TileIter {
 template <typename T> struct MmaFmt;
 template <> struct MmaFmt<__half> { static constexpr uint32_t v = 0; };
 template <> struct MmaFmt<__nv_bfloat16> { static constexpr uint32_t v = 1; };
+
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
@@ -339,21 +349,41 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                 }
             }
             if (rank == 0) {
-                // rotate-half RoPE on the k_rope chunk: pairs (d, d + 32), d = lane
+                // rotate-half RoPE on the k_rope chunk: pairs (d, d + 32). Thread (q0, m)
+                // rotates the element pairs d = 2m, 2m + 1 of rows q0, q0 + 4, ...; four rows
+                // are loaded into registers before any store, so the loads of a batch
+                // overlap instead of queueing behind the previous row's stores.
                 unsigned char* rc = sp + 4 * kChunkBytes;
                 const float* tc = reinterpret_cast<const float*>(tabs + (i & 1) * kTabSlotBytes);
                 const float* ts = tc + kTabBytes / 4;
-                const int d = lane;
-                const int sub = warp - 2;
-#pragma unroll 4
-                for (int p = sub; p < np; p += 2) {
-                    const float cs = tc[p * 32 + d];
-                    const float sn = ts[p * 32 + d];
-                    T* e0 = reinterpret_cast<T*>(rc + p * 128 + ((((d >> 3)) ^ (p & 7)) << 4) + ((d & 7) << 1));
-                    T* e1 = reinterpret_cast<T*>(rc + p * 128 + ((((d >> 3) + 4) ^ (p & 7)) << 4) + ((d & 7) << 1));
-                    const float k0 = ElemTraits<T>::to_f(*e0), k1 = ElemTraits<T>::to_f(*e1);
-                    *e0 = ElemTraits<T>::from_f(k0 * cs - k1 * sn);
-                    *e1 = ElemTraits<T>::from_f(k0 * sn + k1 * cs);
+                const int m = tt & 15;
+                const int q0 = tt >> 4;  // 0..3
+#pragma unroll 1
+                for (int pb = 0; pb < np; pb += 16) {
+                    float2 cs[4], sn[4];
+                    uint32_t k0[4], k1[4];
+                    uint32_t* a0[4];
+                    uint32_t* a1[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int p = pb + q0 + 4 * u;
+                        const int sw = p & 7;
+                        a0[u] = reinterpret_cast<uint32_t*>(rc + p * 128 + (((m >> 2) ^ sw) << 4) + ((m & 3) << 2));
+                        a1[u] = reinterpret_cast<uint32_t*>(rc + p * 128 + ((((m >> 2) + 4) ^ sw) << 4) + ((m & 3) << 2));
+                        cs[u] = *reinterpret_cast<const float2*>(tc + p * 32 + 2 * m);
+                        sn[u] = *reinterpret_cast<const float2*>(ts + p * 32 + 2 * m);
+                        k0[u] = *a0[u];
+                        k1[u] = *a1[u];
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int p = pb + q0 + 4 * u;
+                        if (p < np) {
+                            const float2 x0 = unpack2<T>(k0[u]), x1 = unpack2<T>(k1[u]);
+                            *a0[u] = pack2<T>(x0.x * cs[u].x - x1.x * sn[u].x, x0.y * cs[u].y - x1.y * sn[u].y);
+                            *a1[u] = pack2<T>(x0.x * sn[u].x + x1.x * cs[u].x, x0.y * sn[u].y + x1.y * cs[u].y);
+                        }
+                    }
                 }
             }
             fence_proxy_async_smem();
@@ -362,41 +392,53 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
         }
     } else {
         // ------------------------------------------------------------ softmax warpgroup
+        // Tile i: load S_r(i) from TMEM and release it (the score MMA of tile i+1 can
+        // start), round it to fp16 and send it to the peer's X[i & 1] with st.async
+        // (16 KB counted on the peer's x_full[i & 1]). Slot reuse needs no handshake:
+        // the peer writes X[i & 1] again only for tile i + 2, which it reaches only
+        // after receiving this CTA's tile i + 1, sent after tile i was read here.
         const int t = threadIdx.x - 128;                       // query row
         const uint32_t lane_off = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         const uint32_t taddr_row = tbase + lane_off;
         const int ncol_q = rank == 0 ? 160 : 128;
         auto load_q = [&](int g) {
             const uint32_t* src = reinterpret_cast<const uint32_t*>(qpack + (static_cast<long long>(g) * 128 + t) * 576);
-            for (int c = 0; c < ncol_q; c += 32) {
+            for (int c = 0; c < ncol_q; c += 64) {
+                uint32_t r0[32], r1[32];
                 const int e0 = rank == 0 ? (c < 128 ? 2 * c : 512 + 2 * (c - 128)) : 256 + 2 * c;
-                uint32_t r[32];
-                const uint4* s4 = reinterpret_cast<const uint4*>(src + e0 / 2);
+                const bool two = c + 32 < ncol_q;
+                const int e1 = rank == 0 ? (c + 32 < 128 ? 2 * (c + 32) : 512 + 2 * (c + 32 - 128)) : 256 + 2 * (c + 32);
+                const uint4* s0 = reinterpret_cast<const uint4*>(src + e0 / 2);
+                const uint4* s1 = reinterpret_cast<const uint4*>(src + e1 / 2);
 #pragma unroll
                 for (int v = 0; v < 8; ++v) {
-                    uint4 x = __ldg(s4 + v);
-                    r[4 * v] = x.x; r[4 * v + 1] = x.y; r[4 * v + 2] = x.z; r[4 * v + 3] = x.w;
+                    uint4 x = __ldg(s0 + v);
+                    r0[4 * v] = x.x; r0[4 * v + 1] = x.y; r0[4 * v + 2] = x.z; r0[4 * v + 3] = x.w;
+                    uint4 y = two ? __ldg(s1 + v) : make_uint4(0, 0, 0, 0);
+                    r1[4 * v] = y.x; r1[4 * v + 1] = y.y; r1[4 * v + 2] = y.z; r1[4 * v + 3] = y.w;
                 }
-                tmem_st32(taddr_row + kColQ + c, r);
+                tmem_st32(taddr_row + kColQ + c, r0);
+                if (two) tmem_st32(taddr_row + kColQ + c + 32, r1);
             }
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(smem_u32(&bars->q_ready));
         };
 
-        TileIter it;
-        it.init(P, tb, te);
-        load_q(it.g);
-        float m_run = 0.f, l_run = 0.f;
         const uint32_t x_row_local = xbuf_u32 + t * 128;
         const uint32_t x_row_remote = mapa(x_row_local, peer);
         const uint32_t p_row = pbuf_u32 + t * 128;
         const int sw = t & 7;
+        TileIter it;
+        it.init(P, tb, te);
+        load_q(it.g);
+        float m_run = 0.f, l_run = 0.f;
         for (int i = 0; it.valid(); ++i, it.next(P)) {
             const int slot = i & 1;
             if (t == 0) mbar_arrive_expect_tx(smem_u32(&bars->x_full[slot]), kXBytes);
-            if (!mbar_wait(smem_u32(&bars->s_full), i & 1, err, code(kWaitSoftS))) {
-                note_fail(err, kWaitSoftS, i);
+            bool got = mbar_wait(smem_u32(&bars->s_full), i & 1, err, code(kWaitSoftS));
+            if (!warp_ok(got)) {
+                if (!got) note_fail(err, kWaitSoftS, i);
                 break;
             }
             tc_fence_after();
@@ -406,21 +448,21 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             tmem_ld_wait();
             tc_fence_before();
             mbar_arrive(smem_u32(&bars->s_free));
-
-            // own partial -> fp16, ship to the peer (chunk c holds positions 8c..8c+7)
             uint32_t h[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) h[j] = pack_half2(__uint_as_float(sr[2 * j]), __uint_as_float(sr[2 * j + 1]));
-            const uint32_t rbar = mapa(smem_u32(&bars->x_full[slot]), peer);
+            for (int q = 0; q < 32; ++q) h[q] = pack_half2(__uint_as_float(sr[2 * q]), __uint_as_float(sr[2 * q + 1]));
+            {
+                const uint32_t rbar = mapa(smem_u32(&bars->x_full[slot]), peer);
+                const uint32_t dst = x_row_remote + slot * kXBytes;
 #pragma unroll
-            for (int c = 0; c < 8; ++c)
-                st_async_v4(x_row_remote + slot * kXBytes + ((c ^ sw) << 4), h[4 * c], h[4 * c + 1], h[4 * c + 2],
-                            h[4 * c + 3], rbar);
-            if (!mbar_wait_cluster(smem_u32(&bars->x_full[slot]), (i >> 1) & 1, err, code(kWaitSoftX))) {
-                note_fail(err, kWaitSoftX, i);
+                for (int c = 0; c < 8; ++c)
+                    st_async_v4(dst + ((c ^ sw) << 4), h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3], rbar);
+            }
+            got = mbar_wait_cluster(smem_u32(&bars->x_full[slot]), (i >> 1) & 1, err, code(kWaitSoftX));
+            if (!warp_ok(got)) {
+                if (!got) note_fail(err, kWaitSoftX, i);
                 break;
             }
-
             // full score = fp16(own) + fp16(peer), identical in both CTAs
             float s[64];
             const int np = it.np();
@@ -440,34 +482,45 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                     s[j + 1] = j + 1 < np ? a.y + b.y : -INFINITY;
                 }
             }
-            float mt = s[0];
+            // tile max: tree reduction
+            float mx[32];
 #pragma unroll
-            for (int j = 1; j < 64; ++j) mt = fmaxf(mt, s[j]);
+            for (int j = 0; j < 32; ++j) mx[j] = fmaxf(s[j], s[j + 32]);
+#pragma unroll
+            for (int w2 = 16; w2 > 0; w2 >>= 1)
+#pragma unroll
+                for (int j = 0; j < w2; ++j) mx[j] = fmaxf(mx[j], mx[j + w2]);
+            const float mt = mx[0];
             float alpha = 1.f;
             bool need = false;
-            const bool first = it.seg_first();
-            if (first) {
+            if (it.seg_first()) {
                 m_run = mt;
                 l_run = 0.f;
             } else if (mt > m_run + kRescaleThreshold) {
-                alpha = exp2f(m_run - mt);
+                alpha = ex2_approx(m_run - mt);
                 m_run = mt;
                 l_run *= alpha;
                 need = true;
             }
             uint32_t pp[32];
-            float lsum = 0.f;
+            float ls[16];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-                const uint32_t v = pack2<T>(exp2f(s[2 * j] - m_run), exp2f(s[2 * j + 1] - m_run));
+                const uint32_t v = pack2<T>(ex2_approx(s[2 * j] - m_run), ex2_approx(s[2 * j + 1] - m_run));
                 pp[j] = v;
                 const float2 f = unpack2<T>(v);
-                lsum += f.x + f.y;
+                if (j < 16) ls[j] = f.x + f.y;
+                else ls[j - 16] += f.x + f.y;
             }
-            l_run += lsum;
+#pragma unroll
+            for (int w2 = 8; w2 > 0; w2 >>= 1)
+#pragma unroll
+                for (int j = 0; j < w2; ++j) ls[j] += ls[j + w2];
+            l_run += ls[0];
             // P slot is free once PV(i-2) has completed
-            if (i >= 2 && !mbar_wait(smem_u32(&bars->pv_done[slot]), ((i - 2) >> 1) & 1, err, code(kWaitSoftPV))) {
-                note_fail(err, kWaitSoftPV, i);
+            got = i < 2 || mbar_wait(smem_u32(&bars->pv_done[slot]), ((i - 2) >> 1) & 1, err, code(kWaitSoftPV));
+            if (!warp_ok(got)) {
+                if (!got) note_fail(err, kWaitSoftPV, i);
                 break;
             }
 #pragma unroll
@@ -478,8 +531,11 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             fence_proxy_async_smem();
             if (__any_sync(0xffffffffu, need)) {
                 // rescale this warp's O rows once PV(i-1) has completed
-                if (!mbar_wait(smem_u32(&bars->pv_done[(i - 1) & 1]), ((i - 1) >> 1) & 1, err, code(kWaitSoftPV)))
+                got = mbar_wait(smem_u32(&bars->pv_done[(i - 1) & 1]), ((i - 1) >> 1) & 1, err, code(kWaitSoftPV));
+                if (!warp_ok(got)) {
+                    if (!got) note_fail(err, kWaitSoftPV, i);
                     break;
+                }
                 tc_fence_after();
 #pragma unroll 1
                 for (int c0 = 0; c0 < 256; c0 += 32) {
@@ -496,7 +552,11 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             mbar_arrive(smem_u32(&bars->p_full[slot]));
 
             if (it.seg_last()) {
-                if (!mbar_wait(smem_u32(&bars->pv_done[slot]), (i >> 1) & 1, err, code(kWaitSoftPV))) break;
+                got = mbar_wait(smem_u32(&bars->pv_done[slot]), (i >> 1) & 1, err, code(kWaitSoftPV));
+                if (!warp_ok(got)) {
+                    if (!got) note_fail(err, kWaitSoftPV, i);
+                    break;
+                }
                 tc_fence_after();
                 const int rec = it.g + w;
                 const bool row_ok = t < group_rows(P, it.g);
