@@ -113,6 +113,30 @@ MLA_API mla_status_t mla_launch_fused(const mla_fused_params_t* p, mla_dtype_t d
 MLA_API mla_status_t mla_launch_batched_fused(const mla_batched_fused_params_t* p, mla_dtype_t dtype,
                                       mla_stream_t stream);
 
+/* Allocation-free variant of mla_launch_fused. No counterpart in the reference.
+ *
+ * Some callers may not allocate device memory at all: hosts that own every
+ * device allocation themselves (plugin and inference-server runtimes with a
+ * pre-reserved arena), and latency-critical loops where an allocator call (and
+ * the synchronisation it can imply) is not acceptable. mla_launch_fused takes
+ * its split-KV scratch from the stream-ordered pool; this entry point instead
+ * uses one fixed array of MLA_NOALLOC_SCRATCH_BYTES that the library keeps in
+ * device memory on every GPU that loads it, until the process exits. It calls no
+ * cudaMalloc, cudaMallocAsync, cudaFree or other allocating routine.
+ *
+ * - The caller still provides all inputs and the output, as for mla_launch_fused.
+ * - Problems whose scratch does not fit (many heads or a large d_c) are
+ *   rejected with MLA_ERR_UNSUPPORTED before anything runs; the split-KV worker
+ *   count is reduced until the partial records fit.
+ * - The first call on a device looks up the array's device address
+ *   (cudaGetSymbolAddress) with that device current; make that first call
+ *   before capturing any stream.
+ * - Every call uses the same array: calls that can overlap on the GPU (other
+ *   streams, other host threads) race and corrupt each other's results; order
+ *   them on one stream. */
+#define MLA_NOALLOC_SCRATCH_BYTES (8u << 20)
+MLA_API mla_status_t mla_launch_fused_noalloc(const mla_fused_params_t* p, mla_dtype_t dtype, mla_stream_t stream);
+
 /* General decode. One query token per sequence (or, with shared_cache, `batch`
  * tokens over sequence 0). */
 typedef struct mla_decode_args {

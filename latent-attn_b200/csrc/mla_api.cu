@@ -103,7 +103,9 @@ mla_status_t validate_cfg(const mla_config_t* c) {
     return MLA_OK;
 }
 
-mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan* p) {
+// max_workers > 0 caps the split-KV worker count (the allocation-free entry point
+// uses it to fit its fixed scratch array); 0 keeps the planner's own choice.
+mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan* p, int max_workers = 0) {
     mla_status_t st = validate_cfg(cfg);
     if (st != MLA_OK) return st;
     if (!a) return fail(MLA_ERR_INVALID_ARGUMENT, "args is null");
@@ -192,6 +194,7 @@ mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan
     if (T > (1LL << 30)) return fail(MLA_ERR_UNSUPPORTED, "too many positions");
     int cap = use_tc ? di.sms / 2 : 64;
     if (cap > 128) cap = 128;  // the combine kernel merges at most 128 records per row
+    if (max_workers > 0 && cap > max_workers) cap = max_workers;
     if (cap < 1) cap = 1;
     int W = cap;
     if (T >= 0 && T < W) W = T > 0 ? static_cast<int>(T) : 1;
@@ -253,9 +256,10 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
 }
 
 mla_status_t decode_impl(const mla_config_t* cfg, const mla_decode_args_t* a, void* workspace,
-                         size_t ws_bytes, float* out, float* part_ml, float* part_o, cudaStream_t s) {
+                         size_t ws_bytes, float* out, float* part_ml, float* part_o, cudaStream_t s,
+                         int max_workers = 0) {
     Plan pl;
-    mla_status_t st = make_plan(cfg, a, &pl);
+    mla_status_t st = make_plan(cfg, a, &pl, max_workers);
     if (st != MLA_OK) return st;
     if (!workspace) return fail(MLA_ERR_WORKSPACE, "workspace is null");
     if (reinterpret_cast<uintptr_t>(workspace) % kAlign != 0)
@@ -279,6 +283,36 @@ mla_status_t decode_with_pool(const mla_config_t* cfg, const mla_decode_args_t* 
     e = cudaFreeAsync(ws, s);
     if (st == MLA_OK && e != cudaSuccess) return cuda_fail(e, "cudaFreeAsync(workspace)");
     return st;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the single-token launcher.
+//
+// Its split-KV scratch (status word, packed query, partial records) lives in one
+// file-scope device array instead of memory from cudaMalloc / cudaMallocAsync.
+// In host code the array's name is only a stand-in for the device symbol, so the
+// real device address is looked up with cudaGetSymbolAddress, once per device,
+// with that device current, and passed to the kernels.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MLA_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch on the current device (looked up once per device).
+mla_status_t noalloc_scratch(void** out) {
+    static std::mutex mu;
+    static std::vector<void*> addr;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    std::lock_guard<std::mutex> lk(mu);
+    if (static_cast<int>(addr.size()) <= dev) addr.resize(dev + 1, nullptr);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return MLA_OK;
 }
 
 }  // namespace
@@ -416,6 +450,48 @@ mla_status_t mla_timer_decode_ms(mla_timer_t timer, float* ms) {
 }
 
 uint64_t mla_kernel_launch_count(void) { return mla::g_launches.load(std::memory_order_relaxed); }
+
+mla_status_t mla_launch_fused_noalloc(const mla_fused_params_t* p, mla_dtype_t dtype, mla_stream_t stream) {
+    if (!p) return fail(MLA_ERR_INVALID_ARGUMENT, "params is null");
+    mla_status_t st = validate_cfg(p->cfg);
+    if (st != MLA_OK) return st;
+    if (!p->output) return fail(MLA_ERR_INVALID_ARGUMENT, "output is null");
+    if (!p->q_absorbed) return fail(MLA_ERR_INVALID_ARGUMENT, "q_absorbed is null");
+    if (p->seq_len <= 0) return fail(MLA_ERR_INVALID_ARGUMENT, "seq_len must be positive, got %d", p->seq_len);
+    mla_decode_args_t a;
+    std::memset(&a, 0, sizeof(a));
+    a.dtype = dtype;
+    a.batch = 1;
+    a.kv_cache = p->kv_cache;
+    a.max_seq_len = p->seq_len;
+    a.q_absorbed = p->q_absorbed;
+    a.q_rope = p->q_rope;
+    a.W_UV = p->W_UV;
+    a.rope_cos = p->rope_cos;
+    a.rope_sin = p->rope_sin;
+    a.output = p->output;
+    // Largest worker count whose workspace fits the static array (fewer workers,
+    // fewer partial records); a problem that does not fit even with one worker is
+    // rejected before anything is launched.
+    Plan pl;
+    st = make_plan(p->cfg, &a, &pl);
+    if (st != MLA_OK) return st;
+    int workers = pl.dp.W;
+    while (workers > 1 && pl.total > MLA_NOALLOC_SCRATCH_BYTES) {
+        --workers;
+        st = make_plan(p->cfg, &a, &pl, workers);
+        if (st != MLA_OK) return st;
+    }
+    if (pl.total > MLA_NOALLOC_SCRATCH_BYTES)
+        return fail(MLA_ERR_UNSUPPORTED,
+                    "problem needs %zu bytes of scratch; the static scratch of mla_launch_fused_noalloc holds %u",
+                    pl.total, static_cast<unsigned>(MLA_NOALLOC_SCRATCH_BYTES));
+    void* scratch = nullptr;
+    st = noalloc_scratch(&scratch);
+    if (st != MLA_OK) return st;
+    return decode_impl(p->cfg, &a, scratch, MLA_NOALLOC_SCRATCH_BYTES, a.output, nullptr, nullptr,
+                       reinterpret_cast<cudaStream_t>(stream), workers);
+}
 
 const char* mla_last_error(void) { return g_last_error.c_str(); }
 

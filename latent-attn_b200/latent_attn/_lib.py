@@ -26,6 +26,8 @@ STATUS_NAMES = {
     4: "MLA_ERR_CUDA", 5: "MLA_ERR_NO_DEVICE_CODE", 6: "MLA_ERR_TIMEOUT",
 }
 
+NOALLOC_SCRATCH_BYTES = 8 << 20
+
 DTYPE_F16 = 0
 DTYPE_BF16 = 1
 DTYPE_F32 = 2
@@ -69,6 +71,7 @@ SIGNATURES = {
     "mla_config_validate": (C.c_int, [C.POINTER(MlaConfig)]),
     "mla_launch_fused": (C.c_int, [C.POINTER(MlaFusedParams), C.c_int, C.c_void_p]),
     "mla_launch_batched_fused": (C.c_int, [C.POINTER(MlaBatchedFusedParams), C.c_int, C.c_void_p]),
+    "mla_launch_fused_noalloc": (C.c_int, [C.POINTER(MlaFusedParams), C.c_int, C.c_void_p]),
     "mla_decode_workspace_size": (C.c_int, [C.POINTER(MlaConfig), C.POINTER(MlaDecodeArgs),
                                             C.POINTER(C.c_size_t)]),
     "mla_decode": (C.c_int, [C.POINTER(MlaConfig), C.POINTER(MlaDecodeArgs), C.c_void_p, C.c_size_t,

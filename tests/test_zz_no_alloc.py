@@ -1,0 +1,79 @@
+"""mla_launch_fused_noalloc: the allocation-free variant of mla_launch_fused.
+
+It exists for callers that may not allocate device memory (hosts that own every
+allocation, latency-critical loops that must not touch an allocator); it keeps
+its scratch in a fixed device array inside the library. These tests call it
+through the C ABI on raw device pointers and compare it with mla_launch_fused,
+which takes its scratch from the stream-ordered memory pool, on two calls in a
+row (the shared array keeps the previous call's contents), and check that a
+problem too large for the array is rejected on the host.
+
+This file is named to be collected last, so a stop-at-first-failure run has
+already run every other test when it gets here.
+"""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import mla_oracle as O
+from latent_attn import _lib, synthetic
+
+pytestmark = pytest.mark.gpu
+
+# the tolerance used by the other GPU parity tests
+MAX_ABS, MAX_REL, MIN_COS = 1e-2, 2e-2, 0.998
+
+
+def _close(a, b, what):
+    c = O.compare(a, b)
+    assert c["finite"] and c["max_abs"] <= MAX_ABS and c["max_rel"] <= MAX_REL and c["cosine"] > MIN_COS, (what, c)
+
+
+def _launch(fn, cfg, kv, S, qa, qr, wuv, cos, sin, out):
+    p = _lib.MlaFusedParams(kv.data_ptr(), S, qa.data_ptr(), qr.data_ptr(), wuv.data_ptr(), cos.data_ptr(),
+                            sin.data_ptr(), out.data_ptr(), C.pointer(cfg))
+    return fn(C.byref(p), _lib.DTYPE_BF16, C.c_void_p(torch.cuda.current_stream().cuda_stream))
+
+
+def _inputs(S, seed):
+    dev = torch.device("cuda")
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[S], seed=seed)
+    cos, sin = synthetic.build_rope_tables(S, 64, device=dev)
+    return (inp.kv_cache.to(dev), inp.q_absorbed()[0].to(dev).contiguous(),
+            inp.q_rope[0].float().to(dev).contiguous(), inp.W_UV.to(dev), cos, sin)
+
+
+def test_noalloc_matches_pool_launcher_on_consecutive_calls():
+    lib = _lib.load()
+    cfg = _lib.MlaConfig(5120, 512, 128, 64, 128, 128)
+    # two calls in a row with different inputs and lengths: the second must not see the first's scratch
+    for S, seed in ((8192, 1), (3001, 2)):
+        kv, qa, qr, wuv, cos, sin = _inputs(S, seed)
+        want = torch.full((128, 128), float("nan"), device="cuda")
+        got = torch.full((128, 128), float("nan"), device="cuda")
+        assert _launch(lib.mla_launch_fused, cfg, kv, S, qa, qr, wuv, cos, sin, want) == _lib.MLA_OK, \
+            lib.mla_last_error()
+        st = _launch(lib.mla_launch_fused_noalloc, cfg, kv, S, qa, qr, wuv, cos, sin, got)
+        assert st == _lib.MLA_OK, lib.mla_last_error()
+        torch.cuda.synchronize()
+        _close(got.cpu().numpy(), want.cpu().numpy(), f"noalloc vs pool launcher, S={S}")
+
+
+def test_noalloc_rejects_problems_beyond_its_scratch():
+    """2816 heads need 22 query groups: more scratch than the static array holds.
+    The call is refused on the host before any launch, so the (tiny) buffers
+    passed here are never read."""
+    lib = _lib.load()
+    cfg = _lib.MlaConfig(0, 512, 128, 64, 2816, 128)
+    buf = torch.zeros(4096, dtype=torch.bfloat16, device="cuda")
+    f32 = torch.zeros(4096, dtype=torch.float32, device="cuda")
+    out = torch.zeros(16, dtype=torch.float32, device="cuda")
+    p = _lib.MlaFusedParams(buf.data_ptr(), 16, f32.data_ptr(), f32.data_ptr(), buf.data_ptr(), f32.data_ptr(),
+                            f32.data_ptr(), out.data_ptr(), C.pointer(cfg))
+    st = lib.mla_launch_fused_noalloc(C.byref(p), _lib.DTYPE_BF16, C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == _lib.MLA_ERR_UNSUPPORTED
+    msg = lib.mla_last_error().decode()
+    assert "scratch" in msg and str(_lib.NOALLOC_SCRATCH_BYTES) in msg, msg
