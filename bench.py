@@ -89,18 +89,6 @@ def workload_spec(name):
                 desc="config 4: B=256, L=4096, H=128 (DeepSeek-V3 MLA dims), bf16")
 
 
-def lpt_shard(lens, world):
-    """Longest-processing-time assignment of sequences to ranks (balanced sum of lengths)."""
-    order = sorted(range(len(lens)), key=lambda i: -lens[i])
-    loads = [0] * world
-    parts = [[] for _ in range(world)]
-    for i in order:
-        r = min(range(world), key=lambda k: loads[k])
-        parts[r].append(i)
-        loads[r] += lens[i]
-    return [sorted(p) for p in parts]
-
-
 # ----------------------------------------------------------------------------- clocks
 
 class ClockSampler:
@@ -247,6 +235,7 @@ def main():
     from latent_attn import MLAConfig, synthetic, _lib
     from latent_attn.functional import mla_decode
     from latent_attn import _C
+    from latent_attn.distributed import KVRangeDecoder, kv_range, lpt_shard
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -266,7 +255,7 @@ def main():
         seed = 2000 + rank
     else:  # kv-range: contiguous slice of the single sequence
         L = lens_all[0]
-        lo, hi = L * rank // world, L * (rank + 1) // world
+        lo, hi = kv_range(L, world, rank)
         my_lens = [hi - lo]
         seed = 0
     if spec["sharding"] == "kv-range":
@@ -297,16 +286,14 @@ def main():
     bytes_per_step = sum(my_lens) * CACHE_ROW_BYTES
 
     if spec["sharding"] == "kv-range":
-        gathered_ml = torch.empty(world, 1, 128, 2, dtype=torch.float32, device=dev)
-        gathered_o = torch.empty(world, 1, 128, 512, dtype=torch.float32, device=dev)
+        sharded = KVRangeDecoder(cfg) if world > 1 else None
 
         def step(q_n=q_nope, q_r=q_rope, o=out, t=None):
+            if sharded is not None:
+                return sharded(kv, q_r, W_UV, cos, sin, pos_offset=pos_offset, q_nope=q_n, W_UK=W_UK, out=o,
+                               workspace=ws, timer=t)
             ml, oo = _C.mla_decode_partial(kv, q_r, W_UV, cos, sin, *dims, q_nope=q_n, W_UK=W_UK,
                                            kv_pos_offset=pos_offset, workspace=ws, timer=t)
-            if world > 1:
-                dist.all_gather_into_tensor(gathered_ml, ml.unsqueeze(0))
-                dist.all_gather_into_tensor(gathered_o, oo.unsqueeze(0))
-                return _C.mla_combine_partials(gathered_ml, gathered_o, W_UV, *dims, out=o)
             return _C.mla_combine_partials(ml.unsqueeze(0), oo.unsqueeze(0), W_UV, *dims, out=o)
     else:
         def step(q_n=q_nope, q_r=q_rope, o=out, t=None):
