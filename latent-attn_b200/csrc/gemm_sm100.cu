@@ -1,0 +1,540 @@
+// Tensor-core (tcgen05) GEMMs on either side of the decode kernel.
+//
+// 1. Query absorption, per head h:
+//        q_abs[b, h, :] = q_nope[b, h, :] . W_UK[h*dn : (h+1)*dn, :]      (dn x d_c)
+//    (the absorption of tests/test_python.py:98-99 / tests/test_correctness.cu:29-46
+//    in the reference, done there on the caller side) written straight into the
+//    decode kernel's packed query rows qpack = q_scale * [q_abs | q_rope].
+//    It runs transposed, D^T[d_c x tokens] = W_UK_h^T . q_nope_h^T, so the 128-row
+//    M tile is a slice of d_c and any token count (1 .. 256 per CTA) is the N side:
+//      A = W_UK_h^T, MN-major (d_c contiguous), 2 TMA boxes of 64 d_c x dn rows
+//      B = q_nope_h^T, K-major, converted from fp32 to the cache type on load.
+//    CTA = (d_c slice of 128, head, block of up to 256 tokens), 128 threads.
+//
+// 2. Split-KV merge + output projection, per head h:
+//        o_lat[b, h, :] = sum_k w_k o_k     (log-sum-exp weights of the partial records)
+//        out[b, h, j]   = o_lat[b, h, :] . W_UV[h*dv + j, :]   (src/fused_mla.cu:258-267)
+//    Transposed again, D^T[dv x tokens] = W_UV_h . o_lat_h^T with M = dv = 128:
+//      A = W_UV_h, K-major, all d_c / 64 TMA boxes resident (128 KB at d_c = 512)
+//      B = o_lat_h^T, K-major, merged by the CTA's threads from the records (L2).
+//    CTA = (block of up to 64 tokens, head), 256 threads.
+//
+// Both launch W loads by TMA before waiting on the previous kernel
+// (programmatic dependent launch), so weight streaming overlaps its tail.
+// Every wait is bounded; on timeout the status word records it.
+#include <cfloat>
+
+#include "mla_internal.cuh"
+#include "sm100_ptx.cuh"
+#include "tma_host.cuh"
+
+namespace mla {
+using namespace sm100;
+
+namespace {
+
+template <typename T> struct GemmFmt;
+template <> struct GemmFmt<__half> { static constexpr uint32_t v = 0; };
+template <> struct GemmFmt<__nv_bfloat16> { static constexpr uint32_t v = 1; };
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack_pair(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack_pair<__half>(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack_pair<__nv_bfloat16>(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t a, uint32_t b) {
+    asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+
+// query-pack row of token n (single query per sequence: n = b; shared cache: flattened)
+__device__ __forceinline__ long long qpack_row(const DecodePlan& P, int b, int h) {
+    return P.shared ? static_cast<long long>(b) * P.H + h
+                    : static_cast<long long>(b) * P.head_blocks * kGroupRows + h;
+}
+
+constexpr int kAbsorbTok = 256;    // tokens per absorption CTA (MMA N <= 256)
+constexpr int kProjTok = 64;       // tokens per projection CTA
+constexpr int kRedFloats = 8 * 512;  // split partial sums of the merge (S * ntok <= 8 rows of d_c <= 512)
+
+// B operand (dn/64 chunks of ntp rows x 128 B), reused after the MMAs as ntp rows x 128 elements of staging
+__host__ __device__ inline int absorb_b_bytes(int dn, int ntp) {
+    const int b = (dn / 64) * ntp * 128, st = ntp * 256;
+    return b > st ? b : st;
+}
+
+enum : int { kSiteAbsorbA = 12, kSiteAbsorbMma = 13, kSiteProjA = 14, kSiteProjMma = 15 };
+__device__ __forceinline__ int gcode(int site) { return kStatusTimeout | (site << 8); }
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------
+// absorption
+// ------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(128)
+absorb_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ q_nope,
+                    const float* __restrict__ q_rope, float q_scale, T* __restrict__ qpack, int* tile_prefix_out,
+                    int ntp, uint32_t tmem_cols) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int dn = P.dn, dc = P.dc, K = P.dc + P.dR;
+    const uint32_t a_u32 = smem_u32(smem);                   // 2 x (dn rows x 128 B)
+    const uint32_t b_u32 = a_u32 + 2u * dn * 128u;            // dn/64 x (ntp rows x 128 B), then the staging rows
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * dn * 128 + absorb_b_bytes(dn, ntp));
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
+    const uint32_t a_full = smem_u32(&bars[0]), mma_done = smem_u32(&bars[1]);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * 128, h = blockIdx.y, b0 = blockIdx.z * kAbsorbTok;
+    const int ntok = min(kAbsorbTok, P.B - b0);
+    volatile int* err = P.status;
+
+    pdl_launch_dependents();
+    if (tile_prefix_out && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) write_tile_prefix(P, tile_prefix_out);
+    if (threadIdx.x == 0) {
+        mbar_init(a_full, 1);
+        mbar_init(mma_done, 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tmap_w);
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(tmem_slot), tmem_cols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tmem_slot;
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(a_full, 2u * dn * 128u);
+        tma_load_2d(a_u32, &tmap_w, a_full, m0, h * dn);
+        tma_load_2d(a_u32 + dn * 128, &tmap_w, a_full, m0 + 64, h * dn);
+    }
+    // B operand: q_nope of the block's tokens, fp32 -> T, K-major 128-byte-swizzled rows.
+    // Eight 32-byte items per thread are loaded before any is stored, so the loads overlap.
+    const int upr = dn / 8;  // 16-byte units (8 elements) per token row
+    const int items = ntp * upr;
+    for (int i0 = threadIdx.x; i0 < items; i0 += 8 * 128) {
+        float4 x[8], y[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int i = i0 + q * 128, t = i / upr, u = i % upr;
+            x[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            y[q] = x[q];
+            if (i < items && t < ntok) {
+                const float4* src = reinterpret_cast<const float4*>(
+                    q_nope + (static_cast<long long>(b0 + t) * P.H + h) * dn + 8 * u);
+                x[q] = __ldg(src);
+                y[q] = __ldg(src + 1);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int i = i0 + q * 128, t = i / upr, u = i % upr;
+            if (i < items) {
+                const uint32_t dst = b_u32 + (u >> 3) * (ntp * 128) + t * 128 + (((u & 7) ^ (t & 7)) << 4);
+                st_shared_v4(dst, pack_pair<T>(x[q].x, x[q].y), pack_pair<T>(x[q].z, x[q].w),
+                             pack_pair<T>(y[q].x, y[q].y), pack_pair<T>(y[q].z, y[q].w));
+            }
+        }
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        bool ok = mbar_wait(a_full, 0, err, gcode(kSiteAbsorbA));
+        if (ok) {
+            tc_fence_after();
+            const uint32_t idesc = idesc_f16(128, ntp, GemmFmt<T>::v, true, false);
+            for (int k = 0; k < dn / 16; ++k) {
+                const uint64_t ad = smem_desc_sw128(a_u32 + k * 2048, dn * 128, 1024);
+                const uint64_t bd = smem_desc_sw128(b_u32 + (k >> 2) * (ntp * 128) + (k & 3) * 32, 16, 1024);
+                mma_ss(tbase, ad, bd, idesc, k > 0 ? 1u : 0u);
+            }
+        }
+        mma_commit(mma_done);  // also arrives when nothing was issued
+    }
+    // epilogue: thread (warp w, lane) holds d_c index m0 + 32 w + lane for every token column.
+    // The values go through shared memory (the B operand's space, free once the MMAs are done)
+    // as [token][128] rows of T, which are then written to qpack with 16-byte stores.
+    bool ok = mbar_wait(mma_done, 0, err, gcode(kSiteAbsorbMma)) && *err == 0;
+    ok = __all_sync(0xffffffffu, ok);
+    const bool all_ok = __syncthreads_and(ok);
+    T* stage = reinterpret_cast<T*>(smem + 2 * dn * 128);   // ntp x 128 elements <= B operand bytes
+    if (all_ok) {
+        tc_fence_after();
+        const uint32_t trow = tbase + (static_cast<uint32_t>(32 * warp) << 16);
+        for (int c0 = 0; c0 < ntok; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld16(trow + c0, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                stage[(c0 + j) * 128 + 32 * warp + lane] = ElemTraits<T>::from_f(__uint_as_float(r[j]) * q_scale);
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < ntok * 16; i += blockDim.x) {
+            const int n = i >> 4, v = i & 15;
+            const uint4 x = *reinterpret_cast<const uint4*>(stage + n * 128 + 8 * v);
+            *reinterpret_cast<uint4*>(qpack + qpack_row(P, b0 + n, h) * K + m0 + 8 * v) = x;
+        }
+    }
+    if (blockIdx.x == 0) {
+        // rope columns, 4 at a time
+        const int q4 = P.dR / 4;
+        for (int i = threadIdx.x; i < ntok * q4; i += blockDim.x) {
+            const int t = i / q4, j = 4 * (i % q4);
+            const long long flat = static_cast<long long>(b0 + t) * P.H + h;
+            const float4 x = *reinterpret_cast<const float4*>(q_rope + flat * P.dR + j);
+            const uint2 y = make_uint2(pack_pair<T>(x.x * q_scale, x.y * q_scale), pack_pair<T>(x.z * q_scale, x.w * q_scale));
+            *reinterpret_cast<uint2*>(qpack + qpack_row(P, b0 + t, h) * K + dc + j) = y;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tbase, tmem_cols);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// merge + projection
+// ------------------------------------------------------------------------------------------
+// Per-token merge parameters (records are read straight from global memory / L2).
+struct alignas(16) ProjLists {   // size a multiple of 16: the float4 scratch and mbarriers follow it
+    int cnt[kProjTok];           // records of token t (workers w0 .. w0 + cnt - 1)
+    int w0[kProjTok], g[kProjTok], r[kProjTok];   // first worker, group and group row of token t
+    float M[kProjTok];           // max of the records' m (log2 units)
+    float inv[kProjTok];         // 1 / sum_k l_k 2^(m_k - M)
+    uint32_t valid[kProjTok][4]; // bit k: worker w0 + k owns tiles (an empty worker wrote no record); W <= 128
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
+                     const float* __restrict__ rec_o, float* __restrict__ out, int ntp, uint32_t tmem_cols) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int dc = P.dc, dv = P.dv;
+    const int nk = dc / 64;                                   // K chunks
+    const uint32_t a_u32 = smem_u32(smem);                    // nk x (dv rows x 128 B)
+    const uint32_t b_u32 = a_u32 + nk * dv * 128;             // nk x (ntp rows x 128 B)
+    unsigned char* tail = smem + nk * dv * 128 + nk * ntp * 128;
+    ProjLists* L = reinterpret_cast<ProjLists*>(tail);
+    float* red = reinterpret_cast<float*>(tail + sizeof(ProjLists));   // split sums: <= 8 x 512 floats
+    uint64_t* bars = reinterpret_cast<uint64_t*>(tail + sizeof(ProjLists) + kRedFloats * sizeof(float));
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
+    const uint32_t a_full = smem_u32(&bars[0]), mma_done = smem_u32(&bars[1]);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b0 = blockIdx.x * kProjTok, h = blockIdx.y;
+    const int ntok = min(kProjTok, P.B - b0);
+    volatile int* err = P.status;
+
+    if (threadIdx.x == 0) {
+        mbar_init(a_full, 1);
+        mbar_init(mma_done, 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tmap_w);
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(tmem_slot), tmem_cols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tmem_slot;
+    if (threadIdx.x == 0) {
+        // W_UV rows of head h do not depend on the decode kernel: stream them now
+        mbar_arrive_expect_tx(a_full, static_cast<uint32_t>(nk * dv * 128));
+        for (int j = 0; j < nk; ++j) tma_load_2d(a_u32 + j * dv * 128, &tmap_w, a_full, 64 * j, h * dv);
+    }
+    pdl_wait();  // records and status come from the decode kernel
+    const bool failed = *err != kStatusOk;
+    if (failed) {
+        // the decode kernel gave up on a wait: make the failure visible in the output
+        const float nan = __int_as_float(0x7fc00000);
+        for (int i = threadIdx.x; i < ntok * dv; i += blockDim.x)
+            out[(static_cast<long long>(b0 + i / dv) * P.H + h) * dv + i % dv] = nan;
+    } else {
+        // ---- record lists: token t's group row is merged from the workers w0 .. w0 + cnt - 1 of its tiles
+        const int ntiles = total_tiles(P);
+        for (int t = warp; t < ntok; t += 8) {
+            const int b = b0 + t;
+            int g, r;
+            if (P.shared) {
+                const int f = b * P.H + h;
+                g = f / kGroupRows;
+                r = f % kGroupRows;
+            } else {
+                g = b * P.head_blocks + h / kGroupRows;
+                r = h % kGroupRows;
+            }
+            const int gt0 = tile_prefix(P, g), gt1 = tile_prefix(P, g + 1);
+            int n = 0, w0 = 0;
+            if (gt1 > gt0 && ntiles > 0) {
+                w0 = worker_of_tile(ntiles, P.W, gt0);
+                n = worker_of_tile(ntiles, P.W, gt1 - 1) - w0 + 1;
+            }
+            if (lane == 0) {
+                L->cnt[t] = n;
+                L->w0[t] = w0;
+                L->g[t] = g;
+                L->r[t] = r;
+            }
+        }
+        __syncthreads();
+        // every worker owns at least one tile unless there are fewer tiles than workers
+        const bool all_workers_busy = ntiles >= P.W;
+        for (int t = warp; t < ntok; t += 8) {
+            const int n = L->cnt[t], w0 = L->w0[t], row0 = L->g[t] * kGroupRows + L->r[t];
+            float M = -INFINITY, Ls = 0.f;
+            float2 ml[4];
+            bool valid[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {  // lane handles records k = lane + 32 c (n <= W <= 128)
+                const int k = lane + 32 * c, w = w0 + k;
+                valid[c] = k < n && (all_workers_busy ||
+                                     worker_begin(ntiles, P.W, w) != worker_begin(ntiles, P.W, w + 1));
+                const uint32_t mask = __ballot_sync(0xffffffffu, valid[c]);
+                if (lane == 0) L->valid[t][c] = mask;
+                ml[c] = valid[c] ? *reinterpret_cast<const float2*>(rec_ml + static_cast<long long>(row0 + w * kGroupRows) * 2)
+                                 : make_float2(-INFINITY, 0.f);
+                M = fmaxf(M, ml[c].x);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                if (valid[c]) Ls += exp2f(ml[c].x - M) * ml[c].y;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, o);
+            if (lane == 0) {
+                L->M[t] = M;
+                L->inv[t] = Ls > 0.f ? 1.f / Ls : 0.f;
+            }
+        }
+        __syncthreads();
+        // ---- merge into the B operand (fp32 sums, rounded once to T).
+        // Warp job = (token t, record split s): the warp adds records s, s + S, ... of token t,
+        // lane l holding float4 units l, l + 32, l + 64, l + 96 of the d_c row; four records are
+        // loaded before any is accumulated. With fewer than 8 tokens the records of a token are
+        // split over S = 8 / ntok warps and the splits are summed through shared memory.
+        const int U = dc / 4;                                  // float4 units per row, <= 128
+        int S = 8 / ntok;
+        S = S < 1 ? 1 : S;
+        auto store_b = [&](int t, int u, float4 v) {
+            const int c = 4 * u;
+            const uint32_t dst = b_u32 + (c >> 6) * (ntp * 128) + t * 128 + ((((c & 63) >> 3) ^ (t & 7)) << 4) +
+                                 ((c & 7) >> 2) * 8;
+            st_shared_v2(dst, pack_pair<T>(v.x, v.y), pack_pair<T>(v.z, v.w));
+        };
+        const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int p = warp; p < ntok * S; p += 8) {
+            const int t = p % ntok, s = p / ntok;
+            const int n = L->cnt[t], w0 = L->w0[t], row0 = L->g[t] * kGroupRows + L->r[t];
+            const float M = L->M[t], inv = L->inv[t];
+            const uint32_t* vmask = L->valid[t];
+            float4 acc[4] = {zero4, zero4, zero4, zero4};
+            for (int k = s; k < n; k += 4 * S) {
+                float wq[4];
+                long long rq[4];
+                bool vq[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    // record k of the token: row (g + w0 + k) * 128 + r, weight 2^(m_k - M) / sum; an empty
+                    // worker's record is never read (weight 0, load skipped)
+                    const int kk = k + q * S;
+                    rq[q] = static_cast<long long>(row0 + (w0 + kk) * kGroupRows);
+                    vq[q] = kk < n && ((vmask[kk >> 5] >> (kk & 31)) & 1u);
+                    wq[q] = vq[q] ? exp2f(rec_ml[rq[q] * 2] - M) * inv : 0.f;
+                }
+                float4 v[4][4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int u = lane + 32 * j;
+                        v[q][j] = (vq[q] && u < U) ? __ldg(reinterpret_cast<const float4*>(rec_o + rq[q] * dc) + u)
+                                                   : zero4;
+                    }
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        acc[j].x = fmaf(wq[q], v[q][j].x, acc[j].x);
+                        acc[j].y = fmaf(wq[q], v[q][j].y, acc[j].y);
+                        acc[j].z = fmaf(wq[q], v[q][j].z, acc[j].z);
+                        acc[j].w = fmaf(wq[q], v[q][j].w, acc[j].w);
+                    }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int u = lane + 32 * j;
+                if (u < U) {
+                    if (S == 1) store_b(t, u, acc[j]);
+                    else reinterpret_cast<float4*>(red)[(s * ntok + t) * U + u] = acc[j];
+                }
+            }
+        }
+        if (S > 1) {
+            __syncthreads();
+            for (int i = threadIdx.x; i < ntok * U; i += blockDim.x) {
+                const int u = i % U, t = i / U;
+                float4 a = reinterpret_cast<float4*>(red)[t * U + u];
+                for (int s = 1; s < S; ++s) {
+                    const float4 v = reinterpret_cast<float4*>(red)[(s * ntok + t) * U + u];
+                    a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+                }
+                store_b(t, u, a);
+            }
+        }
+        // padding token rows are zero
+        for (int i = threadIdx.x; i < (ntp - ntok) * U; i += blockDim.x)
+            store_b(ntok + i / U, i % U, make_float4(0.f, 0.f, 0.f, 0.f));
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // always wait for the W_UV boxes: shared memory must not be released under a TMA write
+        bool ok = mbar_wait(a_full, 0, err, gcode(kSiteProjA));
+        if (ok && !failed) {
+            tc_fence_after();
+            const uint32_t idesc = idesc_f16(dv, ntp, GemmFmt<T>::v, false, false);
+            for (int k = 0; k < dc / 16; ++k) {
+                const uint64_t ad = smem_desc_sw128(a_u32 + (k >> 2) * (dv * 128) + (k & 3) * 32, 16, 1024);
+                const uint64_t bd = smem_desc_sw128(b_u32 + (k >> 2) * (ntp * 128) + (k & 3) * 32, 16, 1024);
+                mma_ss(tbase, ad, bd, idesc, k > 0 ? 1u : 0u);
+            }
+        }
+        mma_commit(mma_done);
+    }
+    if (warp >= 4 && !failed) {
+        bool ok = mbar_wait(mma_done, 0, err, gcode(kSiteProjMma)) && *err == 0;
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+            tc_fence_after();
+            const int j = 32 * (warp - 4) + lane;
+            const uint32_t trow = tbase + (static_cast<uint32_t>(32 * (warp - 4)) << 16);
+            for (int c0 = 0; c0 < ntok; c0 += 16) {
+                uint32_t r[16];
+                tmem_ld16(trow + c0, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                    const int n = c0 + q;
+                    if (n < ntok) out[(static_cast<long long>(b0 + n) * P.H + h) * dv + j] = __uint_as_float(r[q]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        // the MMAs (if any) completed: mma_done was waited on by warps 4-7, or nothing was issued
+        if (threadIdx.x == 0 && failed) mbar_wait(mma_done, 0, err, gcode(kSiteProjMma));
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tbase, tmem_cols);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------
+namespace {
+uint32_t tmem_cols_for(int n) {
+    uint32_t c = 32;
+    while (c < static_cast<uint32_t>(n)) c <<= 1;
+    return c;
+}
+int pad16(int n) { return (n + 15) / 16 * 16; }
+
+template <typename Kernel, typename... Args>
+cudaError_t launch_ex(Kernel k, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, args...);
+}
+}  // namespace
+
+bool absorb_sm100_supported(const DecodePlan& P) {
+    return P.dc % 128 == 0 && P.dn % 64 == 0 && P.dn <= 256 && P.dR % 8 == 0;
+}
+
+bool project_sm100_supported(const DecodePlan& P) {
+    return P.dv == 128 && P.dc % 64 == 0 && P.dc <= 512 && P.W <= 128;
+}
+
+template <typename T>
+cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const T* W_UK, const float* q_rope,
+                                float q_scale, T* qpack, int* tile_prefix_out, cudaStream_t s) {
+    if (!absorb_sm100_supported(P)) return cudaErrorInvalidValue;
+    CUtensorMap tmap;
+    if (!make_tmap_2d_16b(&tmap, W_UK, static_cast<uint64_t>(P.H) * P.dn, static_cast<uint64_t>(P.dc),
+                          static_cast<uint64_t>(P.dc), static_cast<uint32_t>(P.dn), 64))
+        return cudaErrorInvalidValue;
+    const int ntp = pad16(P.B < kAbsorbTok ? P.B : kAbsorbTok);
+    const size_t smem = 1024 + 2 * P.dn * 128 + absorb_b_bytes(P.dn, ntp) + 64;
+    cudaError_t e = cudaFuncSetAttribute(absorb_sm100_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    dim3 grid(P.dc / 128, P.H, ceil_div(P.B, kAbsorbTok));
+    e = launch_ex(absorb_sm100_kernel<T>, grid, dim3(128), smem, s, false, tmap, P, q_nope, q_rope, q_scale, qpack,
+                  tile_prefix_out, ntp, tmem_cols_for(ntp));
+    count_launches(1);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
+                                 float* out, bool pdl, cudaStream_t s) {
+    if (!project_sm100_supported(P)) return cudaErrorInvalidValue;
+    CUtensorMap tmap;
+    if (!make_tmap_2d_16b(&tmap, W_UV, static_cast<uint64_t>(P.H) * P.dv, static_cast<uint64_t>(P.dc),
+                          static_cast<uint64_t>(P.dc), static_cast<uint32_t>(P.dv), 64))
+        return cudaErrorInvalidValue;
+    const int ntp = pad16(P.B < kProjTok ? P.B : kProjTok);
+    const int nk = P.dc / 64;
+    const size_t smem = 1024 + static_cast<size_t>(nk) * P.dv * 128 + static_cast<size_t>(nk) * ntp * 128 +
+                        sizeof(ProjLists) + kRedFloats * sizeof(float) + 64;
+    cudaError_t e = cudaFuncSetAttribute(project_sm100_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    dim3 grid(ceil_div(P.B, kProjTok), P.H);
+    e = launch_ex(project_sm100_kernel<T>, grid, dim3(256), smem, s, pdl, tmap, P, rec_ml, rec_o, out, ntp,
+                  tmem_cols_for(ntp));
+    count_launches(1);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+#define MLA_INST(T)                                                                                              \
+    template cudaError_t launch_absorb_sm100<T>(const DecodePlan&, const float*, const T*, const float*, float, T*, \
+                                                int*, cudaStream_t);                                             \
+    template cudaError_t launch_project_sm100<T>(const DecodePlan&, const float*, const float*, const T*, float*,   \
+                                                 bool, cudaStream_t);
+MLA_INST(__half)
+MLA_INST(__nv_bfloat16)
+#undef MLA_INST
+
+}  // namespace mla

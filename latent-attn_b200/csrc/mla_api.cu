@@ -83,12 +83,22 @@ int env_path_override() {
     return v;
 }
 
+bool env_gemm_enabled() {
+    static bool v = [] {
+        const char* s = std::getenv("LATENT_ATTN_B200_GEMM");
+        return !(s && !std::strcmp(s, "0"));
+    }();
+    return v;
+}
+
 constexpr size_t kAlign = 256;
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct Plan {
     mla::DecodePlan dp;
     bool use_tc = false;
+    bool use_gemm_absorb = false;   // tcgen05 absorption (gemm_sm100.cu) instead of the CUDA-core pack
+    bool use_gemm_project = false;  // tcgen05 merge + W_UV projection instead of the CUDA-core combine
     size_t off_prefix = 0, off_qpack = 0, off_rec_ml = 0, off_rec_o = 0, off_status = 0, total = 0;
     float q_scale = 0.f;
     int nrec = 0;
@@ -212,6 +222,12 @@ mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan
     off = align_up(off + static_cast<size_t>(p->nrec) * mla::kGroupRows * dc * sizeof(float));
     p->total = off;
 
+    // the tcgen05 GEMMs run on sm_100 whenever their shape constraints hold
+    // (LATENT_ATTN_B200_GEMM=0 keeps the CUDA-core pack / combine kernels)
+    const bool gemm_ok = di.major == 10 && env_gemm_enabled();
+    p->use_gemm_absorb = gemm_ok && mla::absorb_sm100_supported(d);
+    p->use_gemm_project = gemm_ok && mla::project_sm100_supported(d);
+
     float scale = a->softmax_scale > 0.f ? a->softmax_scale : 1.0f / std::sqrt(static_cast<float>(dn + dR));
     p->q_scale = scale * 1.4426950408889634f;  // log2(e): scores in log2 units
     return MLA_OK;
@@ -229,10 +245,18 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
     float* rec_o = reinterpret_cast<float*>(ws + pl.off_rec_o);
     cudaError_t e = cudaMemsetAsync(d.status, 0, sizeof(int), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
-    e = mla::launch_pack_q<T>(d, a->q_absorbed, a->q_absorbed ? nullptr : a->q_nope,
-                              reinterpret_cast<const T*>(a->W_UK), a->q_rope, pl.q_scale, qpack,
-                              d.uniform_len > 0 ? nullptr : prefix, s);
-    if (e != cudaSuccess) return cuda_fail(e, "pack kernel launch");
+    int* prefix_out = d.uniform_len > 0 ? nullptr : prefix;
+    if (!a->q_absorbed && pl.use_gemm_absorb) {
+        e = mla::launch_pack_zero_pad<T>(d, qpack, s);
+        if (e == cudaSuccess)
+            e = mla::launch_absorb_sm100<T>(d, a->q_nope, reinterpret_cast<const T*>(a->W_UK), a->q_rope, pl.q_scale,
+                                            qpack, prefix_out, s);
+        if (e != cudaSuccess) return cuda_fail(e, "absorption kernel launch");
+    } else {
+        e = mla::launch_pack_q<T>(d, a->q_absorbed, a->q_absorbed ? nullptr : a->q_nope,
+                                  reinterpret_cast<const T*>(a->W_UK), a->q_rope, pl.q_scale, qpack, prefix_out, s);
+        if (e != cudaSuccess) return cuda_fail(e, "pack kernel launch");
+    }
     const T* kv = reinterpret_cast<const T*>(a->kv_cache);
     if (a->timer) {
         e = cudaEventRecord(a->timer->begin, s);
@@ -250,7 +274,10 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
         if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(timer)");
         a->timer->recorded = true;
     }
-    e = mla::launch_combine<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, part_ml, part_o, s);
+    if (out && pl.use_gemm_project)
+        e = mla::launch_project_sm100<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, true, s);
+    else
+        e = mla::launch_combine<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, part_ml, part_o, s);
     if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
     return MLA_OK;
 }

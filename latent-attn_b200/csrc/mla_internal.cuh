@@ -114,6 +114,38 @@ __device__ inline int group_of_tile(const DecodePlan& P, int t) {
     return lo;
 }
 
+// Tiles per group, prefix-summed into prefix[0 .. G] (variable-length batches).
+// Run by one whole block; G is small (batch * head_blocks).
+__device__ inline void write_tile_prefix(const DecodePlan& P, int* prefix) {
+    __shared__ int carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (int base = 0; base < P.G; base += blockDim.x) {
+        int g = base + threadIdx.x;
+        int v = 0;
+        if (g < P.G) {
+            int L = P.seq_lens[group_seq(P, g)];
+            L = L < 0 ? 0 : (L > P.max_len ? P.max_len : L);
+            v = ceil_div(L, P.tile);
+        }
+        // inclusive scan across the block (simple Hillis-Steele in shared memory)
+        __shared__ int buf[1024];
+        buf[threadIdx.x] = v;
+        __syncthreads();
+        for (int off = 1; off < blockDim.x; off <<= 1) {
+            int add = threadIdx.x >= off ? buf[threadIdx.x - off] : 0;
+            __syncthreads();
+            buf[threadIdx.x] += add;
+            __syncthreads();
+        }
+        if (g < P.G) prefix[g + 1] = carry + buf[threadIdx.x];
+        __syncthreads();
+        if (threadIdx.x == blockDim.x - 1) carry += buf[threadIdx.x];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) prefix[0] = 0;
+}
+
 __device__ inline int num_records(const DecodePlan& P) { return P.G + P.W - 1; }
 
 template <typename T> struct ElemTraits;
@@ -142,6 +174,17 @@ template <typename T>
 cudaError_t launch_pack_q(const DecodePlan& P, const float* q_absorbed, const float* q_nope,
                           const T* W_UK, const float* q_rope, float q_scale, T* qpack,
                           int* tile_prefix_out, cudaStream_t s);
+template <typename T>
+cudaError_t launch_pack_zero_pad(const DecodePlan& P, T* qpack, cudaStream_t s);
+// gemm_sm100.cu: tcgen05 absorption (q_nope -> qpack) and merge + W_UV projection
+bool absorb_sm100_supported(const DecodePlan& P);
+bool project_sm100_supported(const DecodePlan& P);
+template <typename T>
+cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const T* W_UK, const float* q_rope,
+                                float q_scale, T* qpack, int* tile_prefix_out, cudaStream_t s);
+template <typename T>
+cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
+                                 float* out, bool pdl, cudaStream_t s);
 // decode_simt.cu
 template <typename T>
 cudaError_t launch_decode_simt(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,

@@ -12,37 +12,6 @@
 
 namespace mla {
 
-__device__ void write_tile_prefix(const DecodePlan& P, int* prefix) {
-    // one block; G is small (batch * head_blocks)
-    __shared__ int carry;
-    if (threadIdx.x == 0) carry = 0;
-    __syncthreads();
-    for (int base = 0; base < P.G; base += blockDim.x) {
-        int g = base + threadIdx.x;
-        int v = 0;
-        if (g < P.G) {
-            int L = P.seq_lens[group_seq(P, g)];
-            L = L < 0 ? 0 : (L > P.max_len ? P.max_len : L);
-            v = ceil_div(L, P.tile);
-        }
-        // inclusive scan across the block (simple Hillis-Steele in shared memory)
-        __shared__ int buf[1024];
-        buf[threadIdx.x] = v;
-        __syncthreads();
-        for (int off = 1; off < blockDim.x; off <<= 1) {
-            int add = threadIdx.x >= off ? buf[threadIdx.x - off] : 0;
-            __syncthreads();
-            buf[threadIdx.x] += add;
-            __syncthreads();
-        }
-        if (g < P.G) prefix[g + 1] = carry + buf[threadIdx.x];
-        __syncthreads();
-        if (threadIdx.x == blockDim.x - 1) carry += buf[threadIdx.x];
-        __syncthreads();
-    }
-    if (threadIdx.x == 0) prefix[0] = 0;
-}
-
 // Rows given as q_absorbed: one thread per element.
 template <typename T>
 __global__ void pack_q_copy_kernel(DecodePlan P, const float* __restrict__ q_abs,
@@ -194,6 +163,20 @@ cudaError_t launch_pack_q(const DecodePlan& P, const float* q_absorbed, const fl
     return cudaGetLastError();
 }
 
+template <typename T>
+cudaError_t launch_pack_zero_pad(const DecodePlan& P, T* qpack, cudaStream_t s) {
+    const bool has_pad = P.shared ? (P.B * P.H) % kGroupRows != 0 : P.H % kGroupRows != 0;
+    if (!has_pad) return cudaSuccess;
+    const long long total = static_cast<long long>(P.G) * kGroupRows * (P.dc + P.dR);
+    int blocks = static_cast<int>((total + 255) / 256);
+    if (blocks > 4096) blocks = 4096;
+    pack_q_zero_pad_kernel<T><<<blocks, 256, 0, s>>>(P, qpack);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+template cudaError_t launch_pack_zero_pad<__half>(const DecodePlan&, __half*, cudaStream_t);
+template cudaError_t launch_pack_zero_pad<__nv_bfloat16>(const DecodePlan&, __nv_bfloat16*, cudaStream_t);
 template cudaError_t launch_pack_q<__half>(const DecodePlan&, const float*, const float*, const __half*,
                                            const float*, float, __half*, int*, cudaStream_t);
 template cudaError_t launch_pack_q<__nv_bfloat16>(const DecodePlan&, const float*, const float*,
