@@ -5,33 +5,40 @@
 // rows (heads) of a group form the M = 128 tile, so each cache tile is read from
 // HBM once for every head.
 //
-// The pair splits the 576-wide score reduction and the 512-wide latent output:
-//   CTA 0 owns K = c[0:256] + k_rope[0:64] (320) and output latent columns [0, 256)
-//   CTA 1 owns K = c[256:512]              (256) and output latent columns [256, 512)
-// so each CTA's cache slice serves both of its MMAs from the same shared memory:
-//   score  S_r[128 x 64]  = Q_r(TMEM) . KV_r^T         (K-major B)
-//   latent O_r[128 x 256] += P[128 x 64] . C_r[64 x 256] (P K-major, C MN-major)
-// TMEM per CTA: O_r 256 columns | S 64 | Q_r 160 (CTA 0) or 128 (CTA 1).
-// The full score is S_0 + S_1: each CTA rounds its partial to fp16, ships it to
+// The pair splits the 576-wide score reduction and the 512-wide latent output evenly:
+//   CTA r owns K = c[256 r : 256 r + 256] + the 16 rotate-half frequency pairs
+//   d in [16 r, 16 r + 16) of k_rope (columns d and d + 32), i.e. 288 of the 576,
+//   and output latent columns [256 r, 256 r + 256).
+// Each CTA's cache slice serves both of its MMAs from the same shared memory:
+//   score  S_r[128 x 64]  = Q_r . KV_r^T      (16 K-steps with Q's latent part in TMEM,
+//                                              2 with its rope part in shared memory)
+//   latent O_r[128 x 256] += P[128 x 64](TMEM) . C_r[64 x 256]   (C read MN-major)
+// TMEM per CTA: O_r 256 columns | S 64 | Q_r latent 128 | P 2 x 32.
+// The full score is S_0 + S_1: each CTA rounds its partial to fp16 and ships it to
 // the other CTA's shared memory with st.async (completion counted on the
-// receiver's mbarrier), and both add the same two fp16 halves, so both compute a
+// receiver's mbarrier); both add the same two fp16 halves, so both compute a
 // bit-identical softmax and bit-identical P, m and l.
 //
-// Warp roles (256 threads):
-//   warp 0      TMA producer (one lane): cache tile chunks into a 3-stage ring
-//   warp 1      TMEM allocator + MMA issuer (one lane)
-//   warps 2-3   tile transform: zero rows past the sequence end; CTA 0 also
-//               rotates k_rope in place with the caller's fp32 cos/sin tables
-//               (the rotation of src/fused_mla.cu:34-54 of the reference). The
-//               producer streams each tile's 64 table rows (2 x 8 KB) with TMA into
-//               a 2-slot ring next to the cache chunks, so the rotation never waits
-//               on a global-memory round trip.
-//   warps 4-7   softmax / correction / epilogue: thread t owns query row t
-// Softmax is online in log2 units (Q is pre-scaled by softmax_scale * log2 e) with
-// a lazy rescale: the running max only moves when a tile's max exceeds it by more
-// than 8, which bounds P by 2^8 and makes the O rescale (TMEM ld/scale/st) rare.
+// Warp roles (384 threads):
+//   warp 0      TMA producer (one lane): per tile, 4 latent chunks (128-byte swizzle),
+//               4 rope boxes of 8 columns (no swizzle) and the 16 frequencies' cos/sin
+//               rows of the caller's tables, into a 4-stage ring
+//   warp 1      TMEM allocator + MMA issuer (one lane): issues each tile's score and PV
+//               MMAs as soon as their inputs are ready, in tile order per kind
+//   warps 2-3   tile transform: zero rows past the sequence end, rotate the CTA's
+//               k_rope pairs in place with the tables (the rotation of
+//               src/fused_mla.cu:34-54 of the reference)
+//   warps 4-7   softmax set 0: the even tiles of the worker
+//   warps 8-11  softmax set 1: the odd tiles (thread = query row = TMEM lane)
+// The two softmax sets work on consecutive tiles at the same time: while one waits
+// for the peer's partial scores of its tile, the other computes. Each set has its own
+// P buffer in TMEM. Softmax is online in log2 units (Q is pre-scaled by
+// softmax_scale * log2 e) with a lazy reference max: tile j is exponentiated against
+// the reference of tile j - 1 (handed over by the other set through shared memory),
+// and the reference only moves when the tile's max exceeds it by more than 8, which
+// bounds P by 2^8; only then is O rescaled (rare) and the row sums re-referenced.
 // Every wait is bounded (mbar_wait*); on timeout the kernel records kStatusTimeout
-// in P.status, unwinds, and the combine kernel turns the outputs into NaN.
+// in P.status, unwinds, and the merge kernel turns the outputs into NaN.
 #include <cfloat>
 
 #include "mla_internal.cuh"
@@ -43,23 +50,28 @@ using namespace sm100;
 
 namespace {
 
-constexpr int kTileN = 64;                       // positions per tile
-constexpr int kStages = 3;
-constexpr int kChunkBytes = 64 * 128;            // 64 rows x 64 elements (128 B), 128-byte swizzle
-constexpr int kStageBytes = 5 * kChunkBytes;     // CTA 0 uses 5 chunks, CTA 1 uses 4
-constexpr int kTabBytes = 64 * 32 * 4;           // cos (or sin) rows of one tile, fp32
-constexpr int kTabSlotBytes = 2 * kTabBytes;     // cos | sin
-constexpr int kPBytes = 128 * 128;               // P: 128 rows x 64 positions x 2 B
-constexpr int kXBytes = 128 * 128;               // exchanged partial score: 128 x 64 fp16
-constexpr int kThreads = 256;
+constexpr int kTileN = 64;                          // positions per tile
+constexpr int kStages = 4;
+constexpr int kChunkBytes = 64 * 128;               // 64 rows x 64 latent columns, 128-byte swizzle
+constexpr int kRopeBoxBytes = 64 * 16;              // 64 rows x 8 rope columns, no swizzle
+constexpr int kRopeBytes = 4 * kRopeBoxBytes;
+constexpr int kStageBytes = kRopeBytes + 4 * kChunkBytes;   // [rope boxes | 4 latent chunks]
+constexpr int kTabBytes = 64 * 16 * 4;              // 64 positions x 16 frequencies, fp32
+constexpr int kTabSlotBytes = 2 * kTabBytes;        // cos | sin
+constexpr int kXSlots = 3;
+constexpr int kXBytes = 128 * 128;                  // one slot: 128 rows x 64 fp16 partial scores
+constexpr int kQRopeBoxBytes = 128 * 16;            // 128 rows x 8 rope elements of Q, no swizzle
+constexpr int kQRopeBytes = 4 * kQRopeBoxBytes;
+constexpr int kMSlots = 4;                          // reference-max hand-over slots (tile index mod 4)
+constexpr int kThreads = 384;
+constexpr int kTransformThreads = 64;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 0, kColS = 256, kColQ = 320;
-constexpr float kRescaleThreshold = 8.0f;        // log2 units
+constexpr uint32_t kColO = 0, kColS = 256, kColQ = 320, kColP = 448;   // P buffers at 448 and 480
+constexpr float kRescaleThreshold = 8.0f;           // log2 units
 
 // wait-site codes recorded in the status word's upper bits (debugging aid)
-enum : int { kWaitProducer = 1, kWaitTransform = 2, kWaitMmaTile = 3, kWaitMmaSFree = 4, kWaitMmaP = 5,
-             kWaitMmaQ = 6, kWaitSoftS = 7, kWaitSoftX = 8, kWaitSoftPV = 9, kWaitTeardown = 10,
-             kWaitDrain = 11 };
+enum : int { kWaitProducer = 1, kWaitTransform = 2, kWaitMma = 3, kWaitSoftS = 7, kWaitSoftX = 8,
+             kWaitSoftPV = 9, kWaitTeardown = 10, kWaitDrain = 11, kWaitSoftRef = 12, kWaitCredit = 13 };
 
 // Warp-uniform success: every early exit of a warp that runs warp-collective
 // instructions (tcgen05.ld/st, vote) happens with all 32 lanes together.
@@ -69,17 +81,25 @@ struct __align__(8) Barriers {
     uint64_t kv_full[kStages];
     uint64_t kv_empty[kStages];
     uint64_t tile_ready[kStages];
-    uint64_t s_full, s_free;
-    uint64_t x_full[2];
-    uint64_t p_full[2];
-    uint64_t pv_done[2];
     uint64_t tab_empty[2];
-    uint64_t q_ready, drain, done;
+    uint64_t s_full[2];               // per softmax set: score of its next tile done (score j -> s_full[j & 1])
+    uint64_t s_free;
+    uint64_t p_full[2], pv_done[2];   // per P buffer (tile parity)
+    uint64_t x_full[kXSlots];         // the peer's partial scores of a tile arrived in this CTA
+    uint64_t x_empty[kXSlots];        // credit: the peer has read what this CTA sent into that slot
+    // One barrier per publication slot, not per set: a set whose tile starts a group publishes
+    // without waiting for the other set, so a per-set barrier could complete two phases before
+    // the other set's parity wait for the older one, which then never returns. Per slot, the next
+    // phase of a slot needs the waiter's own later tiles.
+    uint64_t mref[kMSlots];           // m_pub slot j % kMSlots written (tile j's reference max)
+    uint64_t lpub[4];                 // l_pub slot 2 sid + ((j >> 1) & 1) written (set sid's row sum)
+    uint64_t q_ready, o_free, drain, done;
     uint32_t tmem_base;
 };
 
-constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 2 * kTabSlotBytes + 2 * kPBytes +
-                              2 * kXBytes + sizeof(Barriers) + 1024;
+constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 2 * kTabSlotBytes +
+                              static_cast<size_t>(kXSlots) * kXBytes + kQRopeBytes +
+                              kMSlots * 128 * sizeof(float) + 2 * 2 * 128 * sizeof(float2) + sizeof(Barriers) + 1024;
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 __device__ __forceinline__ int code(int site) { return kStatusTimeout | (site << 8); }
@@ -116,6 +136,8 @@ struct TileIter {
     __device__ int np() const { int r = len - pos0(); return r < kTileN ? r : kTileN; }
     __device__ bool seg_first() const { return t == t_begin || t == gt0; }
     __device__ bool seg_last() const { return t + 1 == t_end || t + 1 == gt1; }
+    // the previous tile of this worker starts a segment (so the tile before it, if any, is in another one)
+    __device__ bool prev_seg_first() const { return t - 1 == t_begin || t - 1 == gt0; }
     __device__ void next(const DecodePlan& P) {
         ++t;
         if (t < t_end && t >= gt1) {
@@ -153,21 +175,27 @@ template <typename T>
 __device__ __forceinline__ float2 unpack2(uint32_t v) {
     return ElemTraits<T>::to_f2(*reinterpret_cast<const typename ElemTraits<T>::T2*>(&v));
 }
+__device__ __forceinline__ float2 half2_to_f2(uint32_t v) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&v));
+}
 
 }  // namespace
 
 template <typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_cos,
-                    const __grid_constant__ CUtensorMap tmap_sin, const DecodePlan P, const T* __restrict__ qpack,
-                    float* __restrict__ rec_ml, float* __restrict__ rec_o) {
+decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_rope,
+                    const __grid_constant__ CUtensorMap tmap_cos, const __grid_constant__ CUtensorMap tmap_sin,
+                    const DecodePlan P, const T* __restrict__ qpack, float* __restrict__ rec_ml,
+                    float* __restrict__ rec_o) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     unsigned char* stages = smem;
     unsigned char* tabs = stages + kStages * kStageBytes;
-    unsigned char* pbuf = tabs + 2 * kTabSlotBytes;
-    unsigned char* xbuf = pbuf + 2 * kPBytes;
-    Barriers* bars = reinterpret_cast<Barriers*>(xbuf + 2 * kXBytes);
+    unsigned char* xbuf = tabs + 2 * kTabSlotBytes;
+    unsigned char* qrope = xbuf + kXSlots * kXBytes;                       // Q's rope part, 4 core-matrix boxes
+    float* m_pub = reinterpret_cast<float*>(qrope + kQRopeBytes);         // [kMSlots][128]: reference max of tile j
+    float2* l_pub = reinterpret_cast<float2*>(m_pub + kMSlots * 128);     // [set][2][128]: (row sum, its reference)
+    Barriers* bars = reinterpret_cast<Barriers*>(l_pub + 2 * 2 * 128);
 
     const uint32_t rank = cluster_ctarank();
     const uint32_t peer = rank ^ 1u;
@@ -175,27 +203,48 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
     const int w = blockIdx.x >> 1;
     volatile int* err = P.status;
 
+    if (threadIdx.x == 0) {
+        pdl_launch_dependents();
+        // the first TMA of each map waits for its descriptor: fetch all four right away
+        tma_prefetch_desc(&tmap);
+        tma_prefetch_desc(&tmap_rope);
+        tma_prefetch_desc(&tmap_cos);
+        tma_prefetch_desc(&tmap_sin);
+    }
+    // With variable lengths the tile prefix comes from the query-packing kernel: wait for it
+    // before walking tiles. With uniform lengths only the packed queries depend on that
+    // kernel, and only the softmax warps read them.
+    const bool uniform = P.uniform_len > 0;
+    if (!uniform) pdl_wait();
     const int ntiles = total_tiles(P);
     if (ntiles <= 0 || w >= P.W) return;  // identical for both CTAs of the pair
     const int tb = worker_begin(ntiles, P.W, w), te = worker_begin(ntiles, P.W, w + 1);
     if (tb >= te) return;
+    const int n = te - tb;  // tiles of this worker
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(smem_u32(&bars->kv_full[s]), 1);
             mbar_init(smem_u32(&bars->kv_empty[s]), 1);
-            mbar_init(smem_u32(&bars->tile_ready[s]), 64);
+            mbar_init(smem_u32(&bars->tile_ready[s]), kTransformThreads);
         }
-        mbar_init(smem_u32(&bars->s_full), 1);
+        mbar_init(smem_u32(&bars->tab_empty[0]), kTransformThreads);
+        mbar_init(smem_u32(&bars->tab_empty[1]), kTransformThreads);
+        mbar_init(smem_u32(&bars->s_full[0]), 1);
+        mbar_init(smem_u32(&bars->s_full[1]), 1);
         mbar_init(smem_u32(&bars->s_free), 128);
-        for (int j = 0; j < 2; ++j) {
-            mbar_init(smem_u32(&bars->x_full[j]), 1);
-            mbar_init(smem_u32(&bars->p_full[j]), 128);
-            mbar_init(smem_u32(&bars->pv_done[j]), 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&bars->p_full[b]), 128);
+            mbar_init(smem_u32(&bars->pv_done[b]), 1);
         }
-        mbar_init(smem_u32(&bars->tab_empty[0]), 64);
-        mbar_init(smem_u32(&bars->tab_empty[1]), 64);
+        for (int b = 0; b < kMSlots; ++b) mbar_init(smem_u32(&bars->mref[b]), 128);
+        for (int b = 0; b < 4; ++b) mbar_init(smem_u32(&bars->lpub[b]), 128);
+        for (int s = 0; s < kXSlots; ++s) {
+            mbar_init(smem_u32(&bars->x_full[s]), 1);
+            mbar_init(smem_u32(&bars->x_empty[s]), 4);  // one arrival per warp of the peer's reading set
+        }
         mbar_init(smem_u32(&bars->q_ready), 128);
+        mbar_init(smem_u32(&bars->o_free), 128);
         mbar_init(smem_u32(&bars->drain), 1);
         mbar_init(smem_u32(&bars->done), 1);
         fence_mbar_init();
@@ -204,30 +253,21 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
         tmem_alloc(smem_u32(&bars->tmem_base), kTmemCols);
         tmem_relinquish();
     }
-    if (warp == 0 && lane == 0) {
-        tma_prefetch_desc(&tmap);
-        if (rank == 0) {
-            tma_prefetch_desc(&tmap_cos);
-            tma_prefetch_desc(&tmap_sin);
-        }
-    }
     tc_fence_before();
     cluster_sync();  // both CTAs: barriers initialised, TMEM allocated
     tc_fence_after();
     const uint32_t tbase = bars->tmem_base;
-
-    const int nchunks = rank == 0 ? 5 : 4;
-    const int ksteps = rank == 0 ? 20 : 16;   // score K / 16
     const uint32_t stages_u32 = smem_u32(stages);
     const uint32_t tabs_u32 = smem_u32(tabs);
-    const uint32_t pbuf_u32 = smem_u32(pbuf);
     const uint32_t xbuf_u32 = smem_u32(xbuf);
+    const uint32_t qrope_u32 = smem_u32(qrope);
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             TileIter it;
             it.init(P, tb, te);
+            int issued = 0;
             for (int i = 0; it.valid(); ++i, it.next(P)) {
                 const int st = i % kStages;
                 if (i >= kStages &&
@@ -235,26 +275,32 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                     note_fail(err, kWaitProducer, i);
                     break;
                 }
-                if (rank == 0 && i >= 2 &&
+                if (i >= 2 &&
                     !mbar_wait(smem_u32(&bars->tab_empty[i & 1]), ((i - 2) >> 1) & 1, err, code(kWaitProducer))) {
                     note_fail(err, kWaitProducer, i);
                     break;
                 }
                 const uint32_t full = smem_u32(&bars->kv_full[st]);
-                mbar_arrive_expect_tx(full, nchunks * kChunkBytes + (rank == 0 ? kTabSlotBytes : 0));
+                mbar_arrive_expect_tx(full, kStageBytes + kTabSlotBytes);
                 const int y = static_cast<int>(it.row0 + it.pos0());
                 const uint32_t dst = stages_u32 + st * kStageBytes;
-                for (int j = 0; j < nchunks; ++j) {
-                    const int x = rank == 0 ? (j < 4 ? 64 * j : 512) : 256 + 64 * j;
-                    tma_load_2d(dst + j * kChunkBytes, &tmap, full, x, y);
-                }
-                if (rank == 0) {
-                    const int yt = P.kv_pos_offset + it.pos0();
-                    const uint32_t tdst = tabs_u32 + (i & 1) * kTabSlotBytes;
-                    tma_load_2d(tdst, &tmap_cos, full, 0, yt);
-                    tma_load_2d(tdst + kTabBytes, &tmap_sin, full, 0, yt);
-                }
+                // rope boxes: columns 16 r + {0, 8} and 32 + 16 r + {0, 8} of k_rope
+                for (int b = 0; b < 4; ++b)
+                    tma_load_2d(dst + b * kRopeBoxBytes, &tmap_rope, full,
+                                P.dc + 16 * static_cast<int>(rank) + 8 * (b & 1) + 32 * (b >> 1), y);
+                for (int j = 0; j < 4; ++j)
+                    tma_load_2d(dst + kRopeBytes + j * kChunkBytes, &tmap, full, 256 * static_cast<int>(rank) + 64 * j, y);
+                const int yt = P.kv_pos_offset + it.pos0();
+                const uint32_t tdst = tabs_u32 + (i & 1) * kTabSlotBytes;
+                tma_load_2d(tdst, &tmap_cos, full, 16 * static_cast<int>(rank), yt);
+                tma_load_2d(tdst + kTabBytes, &tmap_sin, full, 16 * static_cast<int>(rank), yt);
+                issued = i + 1;
             }
+            // shared memory must not be released under a TMA write: the last kStages loads (the
+            // earlier ones were consumed before their stage was refilled) land before teardown,
+            // also when another role gave up early
+            for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
+                mbar_wait(smem_u32(&bars->kv_full[i % kStages]), (i / kStages) & 1, err, code(kWaitProducer), 100000000ull);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
@@ -262,73 +308,95 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             constexpr uint32_t fmt = MmaFmt<T>::v;
             constexpr uint32_t idesc_s = idesc_f16(128, kTileN, fmt, false, false);
             constexpr uint32_t idesc_pv = idesc_f16(128, 256, fmt, false, true);
-            bool ok = true;
+            // The issue loops are fully unrolled over precomputed descriptors: adding (bytes >> 4)
+            // to a descriptor advances its 14-bit start-address field (shared addresses stay
+            // below 2^18, so the field never carries).
+            const uint32_t tS = tbase + kColS, tQ = tbase + kColQ, tO = tbase + kColO;
+            const uint64_t dqr = smem_desc_noswz(qrope_u32, kQRopeBoxBytes, 128);   // Q rope, A operand
             auto issue_score = [&](int i) {
                 const uint32_t sa = stages_u32 + (i % kStages) * kStageBytes;
-                for (int k = 0; k < ksteps; ++k) {
-                    const uint64_t bd = smem_desc_sw128(sa + (k >> 2) * kChunkBytes + (k & 3) * 32, 16, 1024);
-                    mma_ts(tbase + kColS, tbase + kColQ + 8 * k, bd, idesc_s, k > 0 ? 1u : 0u);
-                }
-                mma_commit(smem_u32(&bars->s_full));
+                const uint64_t dl = smem_desc_sw128(sa + kRopeBytes, 16, 1024);
+                const uint64_t dr = smem_desc_noswz(sa, kRopeBoxBytes, 128);
+                mma_ts(tS, tQ, dl, idesc_s, 0u);
+#pragma unroll
+                for (int k = 1; k < 16; ++k)
+                    mma_ts(tS, tQ + 8 * k, dl + static_cast<uint64_t>(((k >> 2) * kChunkBytes + (k & 3) * 32) >> 4),
+                           idesc_s, 1u);
+                // rope: two 8-column core-matrix boxes per K = 16 step, 8-row groups 128 bytes apart
+                mma_ss(tS, dqr, dr, idesc_s, 1u);
+                mma_ss(tS, dqr + static_cast<uint64_t>((2 * kQRopeBoxBytes) >> 4),
+                       dr + static_cast<uint64_t>((2 * kRopeBoxBytes) >> 4), idesc_s, 1u);
+                mma_commit(smem_u32(&bars->s_full[i & 1]));
             };
             auto issue_pv = [&](int i, bool first) {
-                const uint32_t sa = stages_u32 + (i % kStages) * kStageBytes;
-                const uint32_t pa = pbuf_u32 + (i & 1) * kPBytes;
-                for (int k = 0; k < kTileN / 16; ++k) {
-                    const uint64_t ad = smem_desc_sw128(pa + 32 * k, 16, 1024);
-                    const uint64_t bd = smem_desc_sw128(sa + 2048 * k, 8192, 1024);
-                    mma_ss(tbase + kColO, ad, bd, idesc_pv, (first && k == 0) ? 0u : 1u);
-                }
+                const uint64_t dc = smem_desc_sw128(stages_u32 + (i % kStages) * kStageBytes + kRopeBytes, 8192, 1024);
+                const uint32_t tP = tbase + kColP + 32 * (i & 1);
+                mma_ts(tO, tP, dc, idesc_pv, first ? 0u : 1u);
+#pragma unroll
+                for (int k = 1; k < kTileN / 16; ++k)
+                    mma_ts(tO, tP + 8 * k, dc + static_cast<uint64_t>((2048 * k) >> 4), idesc_pv, 1u);
                 mma_commit(smem_u32(&bars->pv_done[i & 1]));
                 mma_commit(smem_u32(&bars->kv_empty[i % kStages]));
             };
-            auto wait_tile = [&](int i) {
-                return mbar_wait(smem_u32(&bars->tile_ready[i % kStages]), (i / kStages) & 1, err,
-                                 code(kWaitMmaTile));
-            };
-            TileIter it;
-            it.init(P, tb, te);
-            int seg = 0;
-            ok = mbar_wait(smem_u32(&bars->q_ready), 0, err, code(kWaitMmaQ)) && wait_tile(0);
-            if (ok) {
-                tc_fence_after();
-                issue_score(0);
-            }
-            int fail_i = 0;
-            for (int i = 0; ok && it.valid(); ++i) {
-                fail_i = i;
-                TileIter nx = it;
-                nx.next(P);
-                const bool has_next = nx.valid();
-                const bool next_new_seg = has_next && nx.seg_first();
-                if (has_next && !next_new_seg) {
-                    ok = mbar_wait(smem_u32(&bars->s_free), i & 1, err, code(kWaitMmaSFree)) && wait_tile(i + 1);
-                    if (!ok) break;
-                    tc_fence_after();
-                    issue_score(i + 1);
+            // Scores and PVs are each issued in tile order, but interleaved as their inputs
+            // become ready: score(s) needs S released (s_free of tile s - 1), its stage
+            // transformed and, at a group start, the group's Q; PV(v) needs P(v) and, at a group
+            // start after the first, the previous group's O read out (o_free).
+            TileIter its, itv;
+            its.init(P, tb, te);
+            itv = its;
+            int next_s = 0, next_v = 0, qseg = 0, vseg = 0;
+            bool ok = true;
+            uint64_t t_last = globaltimer_ns();
+            for (uint32_t spin = 0; ok && next_v < n; ++spin) {
+                bool progressed = false;
+                if (next_s < n) {
+                    bool ready = (next_s == 0 || mbar_test(smem_u32(&bars->s_free), (next_s - 1) & 1)) &&
+                                 mbar_test(smem_u32(&bars->tile_ready[next_s % kStages]), (next_s / kStages) & 1) &&
+                                 (!its.seg_first() || mbar_test(smem_u32(&bars->q_ready), qseg & 1));
+                    if (ready) {
+                        tc_fence_after();
+                        issue_score(next_s);
+                        if (its.seg_last()) ++qseg;
+                        its.next(P);
+                        ++next_s;
+                        progressed = true;
+                    }
                 }
-                ok = mbar_wait(smem_u32(&bars->p_full[i & 1]), (i >> 1) & 1, err, code(kWaitMmaP));
-                if (!ok) break;
-                tc_fence_after();
-                issue_pv(i, it.seg_first());
-                if (next_new_seg) {
-                    ++seg;
-                    ok = mbar_wait(smem_u32(&bars->q_ready), seg & 1, err, code(kWaitMmaQ)) &&
-                         mbar_wait(smem_u32(&bars->s_free), i & 1, err, code(kWaitMmaSFree)) && wait_tile(i + 1);
-                    if (!ok) break;
-                    tc_fence_after();
-                    issue_score(i + 1);
+                if (next_v < next_s) {
+                    bool ready = mbar_test(smem_u32(&bars->p_full[next_v & 1]), (next_v >> 1) & 1) &&
+                                 (!itv.seg_first() || vseg == 0 || mbar_test(smem_u32(&bars->o_free), (vseg - 1) & 1));
+                    if (ready) {
+                        tc_fence_after();
+                        issue_pv(next_v, itv.seg_first());
+                        if (itv.seg_last()) ++vseg;
+                        itv.next(P);
+                        ++next_v;
+                        progressed = true;
+                    }
                 }
-                it = nx;
+                if (progressed) {
+                    t_last = globaltimer_ns();
+                    continue;
+                }
+                // back off: this lane shares its SM sub-partition with softmax warps, and every
+                // poll takes an issue slot from them
+                __nanosleep(64);
+                if ((spin & 31u) == 0u) {
+                    if (*err != 0 || globaltimer_ns() - t_last > kDefaultWaitNs) {
+                        atomicCAS(const_cast<int*>(err), 0, code(kWaitMma));
+                        note_fail(err, kWaitMma, next_v);
+                        ok = false;
+                    }
+                }
             }
-            if (!ok) note_fail(err, kWaitMmaP, fail_i);
             // drain: every MMA this thread issued has completed before teardown
             mma_commit(smem_u32(&bars->drain));
             mbar_wait(smem_u32(&bars->drain), 0, err, code(kWaitDrain));
         }
     } else if (warp < 4) {
         // ------------------------------------------------------------ tile transform
-        const int tt = threadIdx.x - 64;  // 0..63
+        const int tt = threadIdx.x - 64;  // 0 .. kTransformThreads - 1
         TileIter it;
         it.init(P, tb, te);
         for (int i = 0; it.valid(); ++i, it.next(P)) {
@@ -342,128 +410,168 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             if (np < kTileN) {
                 // zero whole rows past the sequence end (swizzle permutes within a row only)
                 const int rows = kTileN - np;
-                for (int v = tt; v < nchunks * rows * 8; v += 64) {
+                for (int v = tt; v < 4 * rows * 8; v += kTransformThreads) {
                     const int j = v / (rows * 8), rem = v % (rows * 8);
                     const int r = np + rem / 8, c = rem % 8;
-                    *reinterpret_cast<uint4*>(sp + j * kChunkBytes + r * 128 + c * 16) = make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4*>(sp + kRopeBytes + j * kChunkBytes + r * 128 + c * 16) =
+                        make_uint4(0, 0, 0, 0);
                 }
+                for (int v = tt; v < 4 * rows; v += kTransformThreads)
+                    *reinterpret_cast<uint4*>(sp + (v / rows) * kRopeBoxBytes + (np + v % rows) * 16) =
+                        make_uint4(0, 0, 0, 0);
             }
-            if (rank == 0) {
-                // rotate-half RoPE on the k_rope chunk: pairs (d, d + 32). Thread (q0, m)
-                // rotates the element pairs d = 2m, 2m + 1 of rows q0, q0 + 4, ...; four rows
-                // are loaded into registers before any store, so the loads of a batch
-                // overlap instead of queueing behind the previous row's stores.
-                unsigned char* rc = sp + 4 * kChunkBytes;
-                const float* tc = reinterpret_cast<const float*>(tabs + (i & 1) * kTabSlotBytes);
-                const float* ts = tc + kTabBytes / 4;
-                const int m = tt & 15;
-                const int q0 = tt >> 4;  // 0..3
+            // rotate-half RoPE of this CTA's 16 frequency pairs: item (row p, half h) rotates
+            // box h (columns 16 r + 8 h ..) against box 2 + h (columns 32 + 16 r + 8 h ..)
+            const float* tcs = reinterpret_cast<const float*>(tabs + (i & 1) * kTabSlotBytes);
+            const float* tsn = tcs + kTabBytes / 4;
 #pragma unroll 1
-                for (int pb = 0; pb < np; pb += 16) {
-                    float2 cs[4], sn[4];
-                    uint32_t k0[4], k1[4];
-                    uint32_t* a0[4];
-                    uint32_t* a1[4];
+            for (int u = 0; u < 128 / kTransformThreads; ++u) {
+                const int item = tt + kTransformThreads * u, p = item >> 1, h = item & 1;
+                if (p < np) {
+                    uint4* a = reinterpret_cast<uint4*>(sp + h * kRopeBoxBytes + p * 16);
+                    uint4* b = reinterpret_cast<uint4*>(sp + (2 + h) * kRopeBoxBytes + p * 16);
+                    const uint4 ka = *a, kb = *b;
+                    const float4 c0 = *reinterpret_cast<const float4*>(tcs + p * 16 + 8 * h);
+                    const float4 c1 = *reinterpret_cast<const float4*>(tcs + p * 16 + 8 * h + 4);
+                    const float4 s0 = *reinterpret_cast<const float4*>(tsn + p * 16 + 8 * h);
+                    const float4 s1 = *reinterpret_cast<const float4*>(tsn + p * 16 + 8 * h + 4);
+                    const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+                    const uint32_t xa[4] = {ka.x, ka.y, ka.z, ka.w}, xb[4] = {kb.x, kb.y, kb.z, kb.w};
+                    uint32_t ya[4], yb[4];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int p = pb + q0 + 4 * u;
-                        const int sw = p & 7;
-                        a0[u] = reinterpret_cast<uint32_t*>(rc + p * 128 + (((m >> 2) ^ sw) << 4) + ((m & 3) << 2));
-                        a1[u] = reinterpret_cast<uint32_t*>(rc + p * 128 + ((((m >> 2) + 4) ^ sw) << 4) + ((m & 3) << 2));
-                        cs[u] = *reinterpret_cast<const float2*>(tc + p * 32 + 2 * m);
-                        sn[u] = *reinterpret_cast<const float2*>(ts + p * 32 + 2 * m);
-                        k0[u] = *a0[u];
-                        k1[u] = *a1[u];
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 x0 = unpack2<T>(xa[e]), x1 = unpack2<T>(xb[e]);
+                        const float c_lo = cs[2 * e], c_hi = cs[2 * e + 1], s_lo = sn[2 * e], s_hi = sn[2 * e + 1];
+                        ya[e] = pack2<T>(x0.x * c_lo - x1.x * s_lo, x0.y * c_hi - x1.y * s_hi);
+                        yb[e] = pack2<T>(x0.x * s_lo + x1.x * c_lo, x0.y * s_hi + x1.y * c_hi);
                     }
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int p = pb + q0 + 4 * u;
-                        if (p < np) {
-                            const float2 x0 = unpack2<T>(k0[u]), x1 = unpack2<T>(k1[u]);
-                            *a0[u] = pack2<T>(x0.x * cs[u].x - x1.x * sn[u].x, x0.y * cs[u].y - x1.y * sn[u].y);
-                            *a1[u] = pack2<T>(x0.x * sn[u].x + x1.x * cs[u].x, x0.y * sn[u].y + x1.y * cs[u].y);
-                        }
-                    }
+                    *a = make_uint4(ya[0], ya[1], ya[2], ya[3]);
+                    *b = make_uint4(yb[0], yb[1], yb[2], yb[3]);
                 }
             }
             fence_proxy_async_smem();
             mbar_arrive(smem_u32(&bars->tile_ready[st]));
-            if (rank == 0) mbar_arrive(smem_u32(&bars->tab_empty[i & 1]));
+            mbar_arrive(smem_u32(&bars->tab_empty[i & 1]));
         }
     } else {
-        // ------------------------------------------------------------ softmax warpgroup
-        // Tile i: load S_r(i) from TMEM and release it (the score MMA of tile i+1 can
-        // start), round it to fp16 and send it to the peer's X[i & 1] with st.async
-        // (16 KB counted on the peer's x_full[i & 1]). Slot reuse needs no handshake:
-        // the peer writes X[i & 1] again only for tile i + 2, which it reaches only
-        // after receiving this CTA's tile i + 1, sent after tile i was read here.
-        const int t = threadIdx.x - 128;                       // query row
-        const uint32_t lane_off = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-        const uint32_t taddr_row = tbase + lane_off;
-        const int ncol_q = rank == 0 ? 160 : 128;
+        // ------------------------------------------------------------ softmax sets
+        const int sid = (warp - 4) >> 2;                        // set: tiles j with j % 2 == sid
+        const int t = (warp & 3) * 32 + lane;                   // query row == TMEM lane
+        const uint32_t trow = tbase + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
+        // exchange layout: 16-byte chunk c of row t at c * 2048 + t * 16, so each warp-wide
+        // st.async / ld.shared covers 512 contiguous bytes
+        const uint32_t x_local = xbuf_u32 + t * 16;
+        const uint32_t x_remote = mapa(x_local, peer);
+        if (uniform) pdl_wait();  // packed queries come from the previous kernel
+
+        // Q of group g: latent part (K elements 256 r .. 256 r + 256) into TMEM columns
+        // [kColQ, kColQ + 128), two elements per column; rope part (rope 16 r .. 16 r + 16 and
+        // 32 + 16 r .. + 16) into the 4 core-matrix boxes of qrope. Loaded in two halves so at
+        // most 20 16-byte values are in flight per thread.
         auto load_q = [&](int g) {
-            const uint32_t* src = reinterpret_cast<const uint32_t*>(qpack + (static_cast<long long>(g) * 128 + t) * 576);
-            for (int c = 0; c < ncol_q; c += 64) {
-                uint32_t r0[32], r1[32];
-                const int e0 = rank == 0 ? (c < 128 ? 2 * c : 512 + 2 * (c - 128)) : 256 + 2 * c;
-                const bool two = c + 32 < ncol_q;
-                const int e1 = rank == 0 ? (c + 32 < 128 ? 2 * (c + 32) : 512 + 2 * (c + 32 - 128)) : 256 + 2 * (c + 32);
-                const uint4* s0 = reinterpret_cast<const uint4*>(src + e0 / 2);
-                const uint4* s1 = reinterpret_cast<const uint4*>(src + e1 / 2);
+            const T* src = qpack + (static_cast<long long>(g) * kGroupRows + t) * (P.dc + P.dR);
+            const uint4* lat = reinterpret_cast<const uint4*>(src + 256 * rank);
+            {
+                uint4 v[16], r[4];
 #pragma unroll
-                for (int v = 0; v < 8; ++v) {
-                    uint4 x = __ldg(s0 + v);
-                    r0[4 * v] = x.x; r0[4 * v + 1] = x.y; r0[4 * v + 2] = x.z; r0[4 * v + 3] = x.w;
-                    uint4 y = two ? __ldg(s1 + v) : make_uint4(0, 0, 0, 0);
-                    r1[4 * v] = y.x; r1[4 * v + 1] = y.y; r1[4 * v + 2] = y.z; r1[4 * v + 3] = y.w;
+                for (int k = 0; k < 16; ++k) v[k] = __ldg(lat + k);
+                const uint4* r0 = reinterpret_cast<const uint4*>(src + P.dc + 16 * rank);
+                const uint4* r1 = reinterpret_cast<const uint4*>(src + P.dc + 32 + 16 * rank);
+                r[0] = __ldg(r0);
+                r[1] = __ldg(r0 + 1);
+                r[2] = __ldg(r1);
+                r[3] = __ldg(r1 + 1);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t x[16] = {v[4 * q].x, v[4 * q].y, v[4 * q].z, v[4 * q].w,
+                                            v[4 * q + 1].x, v[4 * q + 1].y, v[4 * q + 1].z, v[4 * q + 1].w,
+                                            v[4 * q + 2].x, v[4 * q + 2].y, v[4 * q + 2].z, v[4 * q + 2].w,
+                                            v[4 * q + 3].x, v[4 * q + 3].y, v[4 * q + 3].z, v[4 * q + 3].w};
+                    tmem_st16(trow + kColQ + 16 * q, x);
                 }
-                tmem_st32(taddr_row + kColQ + c, r0);
-                if (two) tmem_st32(taddr_row + kColQ + c + 32, r1);
+#pragma unroll
+                for (int b = 0; b < 4; ++b)
+                    *reinterpret_cast<uint4*>(qrope + b * kQRopeBoxBytes + t * 16) = r[b];
             }
+            {
+                uint4 v[16];
+#pragma unroll
+                for (int k = 0; k < 16; ++k) v[k] = __ldg(lat + 16 + k);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t x[16] = {v[4 * q].x, v[4 * q].y, v[4 * q].z, v[4 * q].w,
+                                            v[4 * q + 1].x, v[4 * q + 1].y, v[4 * q + 1].z, v[4 * q + 1].w,
+                                            v[4 * q + 2].x, v[4 * q + 2].y, v[4 * q + 2].z, v[4 * q + 2].w,
+                                            v[4 * q + 3].x, v[4 * q + 3].y, v[4 * q + 3].z, v[4 * q + 3].w};
+                    tmem_st16(trow + kColQ + 64 + 16 * q, x);
+                }
+            }
+            fence_proxy_async_smem();
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(smem_u32(&bars->q_ready));
         };
 
-        const uint32_t x_row_local = xbuf_u32 + t * 128;
-        const uint32_t x_row_remote = mapa(x_row_local, peer);
-        const uint32_t p_row = pbuf_u32 + t * 128;
-        const int sw = t & 7;
         TileIter it;
         it.init(P, tb, te);
-        load_q(it.g);
-        float m_run = 0.f, l_run = 0.f;
-        for (int i = 0; it.valid(); ++i, it.next(P)) {
-            const int slot = i & 1;
-            if (t == 0) mbar_arrive_expect_tx(smem_u32(&bars->x_full[slot]), kXBytes);
-            bool got = mbar_wait(smem_u32(&bars->s_full), i & 1, err, code(kWaitSoftS));
+        if (sid == 1) it.next(P);
+        else load_q(it.g);        // the first tile (a group start) belongs to set 0
+        float l_self = 0.f, m_l = 0.f;   // this set's row sum over its tiles of the group, and its reference
+        bool ok = true;
+        for (int j = sid; ok && it.valid(); j += 2) {
+            const int slot = j % kXSlots;
+            // ---- phase A: S_r(j) -> registers, release S, next group's Q, send the fp16 partial.
+            // Every barrier below is waited on phase by phase by its waiters: a parity wait must
+            // never start while the barrier is still one phase short (it would pass at once).
+            // s_full[sid] holds only this set's tiles for that reason.
+            bool got = mbar_wait(smem_u32(&bars->s_full[sid]), (j >> 1) & 1, err, code(kWaitSoftS));
             if (!warp_ok(got)) {
-                if (!got) note_fail(err, kWaitSoftS, i);
+                if (!got) note_fail(err, kWaitSoftS, j);
                 break;
             }
+            // the score of tile j implies the other set has finished with tile j - 3's slot, so the
+            // slot's previous phase is complete before this arrival opens the next one
+            if (t == 0) mbar_arrive_expect_tx(smem_u32(&bars->x_full[slot]), kXBytes);
             tc_fence_after();
-            uint32_t sr[64];
-            tmem_ld32(taddr_row + kColS, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-            tmem_ld32(taddr_row + kColS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-            tmem_ld_wait();
-            tc_fence_before();
-            mbar_arrive(smem_u32(&bars->s_free));
             uint32_t h[32];
+            {
+                uint32_t sr[64];
+                tmem_ld32(trow + kColS, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+                tmem_ld32(trow + kColS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+                tmem_ld_wait();
+                tc_fence_before();
+                mbar_arrive(smem_u32(&bars->s_free));
 #pragma unroll
-            for (int q = 0; q < 32; ++q) h[q] = pack_half2(__uint_as_float(sr[2 * q]), __uint_as_float(sr[2 * q + 1]));
+                for (int q = 0; q < 32; ++q) h[q] = pack_half2(__uint_as_float(sr[2 * q]), __uint_as_float(sr[2 * q + 1]));
+            }
+            if (it.seg_last() && it.t + 1 < it.t_end) {
+                // the score of tile j was the last MMA to read this group's Q
+                TileIter nx = it;
+                nx.next(P);
+                load_q(nx.g);
+            }
+            // the peer reads its slot for tile j - 3 before this CTA writes it again
+            got = j < kXSlots ||
+                  mbar_wait_cluster(smem_u32(&bars->x_empty[slot]), ((j / kXSlots) - 1) & 1, err, code(kWaitCredit));
+            if (!warp_ok(got)) {
+                if (!got) note_fail(err, kWaitCredit, j);
+                break;
+            }
             {
                 const uint32_t rbar = mapa(smem_u32(&bars->x_full[slot]), peer);
-                const uint32_t dst = x_row_remote + slot * kXBytes;
+                const uint32_t dst = x_remote + slot * kXBytes;
 #pragma unroll
                 for (int c = 0; c < 8; ++c)
-                    st_async_v4(dst + ((c ^ sw) << 4), h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3], rbar);
+                    st_async_v4(dst + c * 2048, h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3], rbar);
             }
-            got = mbar_wait_cluster(smem_u32(&bars->x_full[slot]), (i >> 1) & 1, err, code(kWaitSoftX));
+
+            // ---- phase B: full score, reference max, P into TMEM buffer j & 1
+            got = mbar_wait_cluster(smem_u32(&bars->x_full[slot]), (j / kXSlots) & 1, err, code(kWaitSoftX));
             if (!warp_ok(got)) {
-                if (!got) note_fail(err, kWaitSoftX, i);
+                if (!got) note_fail(err, kWaitSoftX, j);
                 break;
             }
-            // full score = fp16(own) + fp16(peer), identical in both CTAs
             float s[64];
             const int np = it.np();
 #pragma unroll
@@ -471,90 +579,118 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                 uint4 v;
                 asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
                              : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                             : "r"(x_row_local + slot * kXBytes + ((c ^ sw) << 4)));
+                             : "r"(x_local + slot * kXBytes + c * 2048));
                 const uint32_t pv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&h[4 * c + q]));
-                    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&pv[q]));
-                    const int j = 8 * c + 2 * q;
-                    s[j] = j < np ? a.x + b.x : -INFINITY;
-                    s[j + 1] = j + 1 < np ? a.y + b.y : -INFINITY;
+                    const float2 a = half2_to_f2(h[4 * c + q]);
+                    const float2 b = half2_to_f2(pv[q]);
+                    const int k = 8 * c + 2 * q;
+                    s[k] = k < np ? a.x + b.x : -INFINITY;
+                    s[k + 1] = k + 1 < np ? a.y + b.y : -INFINITY;
                 }
             }
-            // tile max: tree reduction
+            // credit for the peer: this warp's rows of the slot are read
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(mapa(smem_u32(&bars->x_empty[slot]), peer));
             float mx[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) mx[j] = fmaxf(s[j], s[j + 32]);
+            for (int k = 0; k < 32; ++k) mx[k] = fmaxf(s[k], s[k + 32]);
 #pragma unroll
             for (int w2 = 16; w2 > 0; w2 >>= 1)
 #pragma unroll
-                for (int j = 0; j < w2; ++j) mx[j] = fmaxf(mx[j], mx[j + w2]);
+                for (int k = 0; k < w2; ++k) mx[k] = fmaxf(mx[k], mx[k + w2]);
             const float mt = mx[0];
-            float alpha = 1.f;
+            // reference max: the previous tile's (from the other set) unless this tile exceeds it by
+            // more than the threshold
+            float m = mt, alpha = 1.f;
             bool need = false;
-            if (it.seg_first()) {
-                m_run = mt;
-                l_run = 0.f;
-            } else if (mt > m_run + kRescaleThreshold) {
-                alpha = ex2_approx(m_run - mt);
-                m_run = mt;
-                l_run *= alpha;
-                need = true;
+            if (!it.seg_first()) {
+                got = mbar_wait(smem_u32(&bars->mref[(j - 1) % kMSlots]), ((j - 1) / kMSlots) & 1, err, code(kWaitSoftRef));
+                if (!warp_ok(got)) {
+                    if (!got) note_fail(err, kWaitSoftRef, j);
+                    break;
+                }
+                const float m_prev = m_pub[((j - 1) % kMSlots) * 128 + t];
+                if (mt > m_prev + kRescaleThreshold) {
+                    alpha = ex2_approx(m_prev - mt);
+                    need = true;
+                } else {
+                    m = m_prev;
+                }
             }
+            m_pub[(j % kMSlots) * 128 + t] = m;
+            mbar_arrive(smem_u32(&bars->mref[j % kMSlots]));
             uint32_t pp[32];
             float ls[16];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const uint32_t v = pack2<T>(ex2_approx(s[2 * j] - m_run), ex2_approx(s[2 * j + 1] - m_run));
-                pp[j] = v;
+            for (int q = 0; q < 32; ++q) {
+                const uint32_t v = pack2<T>(ex2_approx(s[2 * q] - m), ex2_approx(s[2 * q + 1] - m));
+                pp[q] = v;
                 const float2 f = unpack2<T>(v);
-                if (j < 16) ls[j] = f.x + f.y;
-                else ls[j - 16] += f.x + f.y;
+                if (q < 16) ls[q] = f.x + f.y;
+                else ls[q - 16] += f.x + f.y;
             }
 #pragma unroll
             for (int w2 = 8; w2 > 0; w2 >>= 1)
 #pragma unroll
-                for (int j = 0; j < w2; ++j) ls[j] += ls[j + w2];
-            l_run += ls[0];
-            // P slot is free once PV(i-2) has completed
-            got = i < 2 || mbar_wait(smem_u32(&bars->pv_done[slot]), ((i - 2) >> 1) & 1, err, code(kWaitSoftPV));
+                for (int k = 0; k < w2; ++k) ls[k] += ls[k + w2];
+            // this set's row sum restarts at its first tile of a group and follows the reference
+            if (it.seg_first() || it.prev_seg_first()) {
+                l_self = 0.f;
+            } else if (m != m_l) {
+                l_self *= ex2_approx(m_l - m);
+            }
+            m_l = m;
+            l_self += ls[0];
+            // P buffer j & 1 is free once PV(j - 2) has completed
+            got = j < 2 || mbar_wait(smem_u32(&bars->pv_done[j & 1]), ((j - 2) >> 1) & 1, err, code(kWaitSoftPV));
             if (!warp_ok(got)) {
-                if (!got) note_fail(err, kWaitSoftPV, i);
+                if (!got) note_fail(err, kWaitSoftPV, j);
                 break;
             }
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-                asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(p_row + slot * kPBytes + ((c ^ sw) << 4)),
-                             "r"(pp[4 * c]), "r"(pp[4 * c + 1]), "r"(pp[4 * c + 2]), "r"(pp[4 * c + 3])
-                             : "memory");
-            fence_proxy_async_smem();
             if (__any_sync(0xffffffffu, need)) {
-                // rescale this warp's O rows once PV(i-1) has completed
-                got = mbar_wait(smem_u32(&bars->pv_done[(i - 1) & 1]), ((i - 1) >> 1) & 1, err, code(kWaitSoftPV));
+                // the reference moved: rescale O (alpha = 1 on rows that keep theirs) once PV(j - 1) is done
+                got = mbar_wait(smem_u32(&bars->pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1, err, code(kWaitSoftPV));
                 if (!warp_ok(got)) {
-                    if (!got) note_fail(err, kWaitSoftPV, i);
+                    if (!got) note_fail(err, kWaitSoftPV, j);
                     break;
                 }
                 tc_fence_after();
 #pragma unroll 1
                 for (int c0 = 0; c0 < 256; c0 += 32) {
                     uint32_t o[32];
-                    tmem_ld32(taddr_row + kColO + c0, o);
+                    tmem_ld32(trow + kColO + c0, o);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
-                    tmem_st32(taddr_row + kColO + c0, o);
+                    for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+                    tmem_st32(trow + kColO + c0, o);
                 }
-                tmem_st_wait();
             }
+            tc_fence_after();
+            tmem_st32(trow + kColP + 32 * (j & 1), pp);
+            tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(smem_u32(&bars->p_full[slot]));
+            mbar_arrive(smem_u32(&bars->p_full[j & 1]));
+            // publish this set's row sum (slot by the set's tile count)
+            l_pub[(sid * 2 + ((j >> 1) & 1)) * 128 + t] = make_float2(l_self, m_l);
+            mbar_arrive(smem_u32(&bars->lpub[sid * 2 + ((j >> 1) & 1)]));
 
             if (it.seg_last()) {
-                got = mbar_wait(smem_u32(&bars->pv_done[slot]), (i >> 1) & 1, err, code(kWaitSoftPV));
+                // ---- group end: partial record of this worker
+                got = mbar_wait(smem_u32(&bars->pv_done[j & 1]), (j >> 1) & 1, err, code(kWaitSoftPV));
+                int site = kWaitSoftPV;
+                float l_tot = l_self;
+                if (warp_ok(got) && !it.seg_first()) {
+                    site = kWaitSoftRef;
+                    // the other set's tiles of the group end at tile j - 1
+                    got = mbar_wait(smem_u32(&bars->lpub[(sid ^ 1) * 2 + (((j - 1) >> 1) & 1)]), ((j - 1) >> 2) & 1, err,
+                                   code(kWaitSoftRef));
+                    const float2 lo = l_pub[((sid ^ 1) * 2 + (((j - 1) >> 1) & 1)) * 128 + t];
+                    l_tot += lo.x * ex2_approx(lo.y - m);
+                }
                 if (!warp_ok(got)) {
-                    if (!got) note_fail(err, kWaitSoftPV, i);
+                    if (!got) note_fail(err, site, j);
                     break;
                 }
                 tc_fence_after();
@@ -564,7 +700,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
 #pragma unroll 1
                 for (int c0 = 0; c0 < 256; c0 += 32) {
                     uint32_t o[32];
-                    tmem_ld32(taddr_row + kColO + c0, o);
+                    tmem_ld32(trow + kColO + c0, o);
                     tmem_ld_wait();
                     if (row_ok) {
 #pragma unroll
@@ -576,14 +712,12 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                 }
                 if (rank == 0 && row_ok)
                     *reinterpret_cast<float2*>(rec_ml + (static_cast<long long>(rec) * kGroupRows + t) * 2) =
-                        make_float2(m_run, l_run);
+                        make_float2(m, l_tot);
                 tc_fence_before();
-                if (it.t + 1 < it.t_end) {
-                    TileIter nx = it;
-                    nx.next(P);
-                    load_q(nx.g);
-                }
+                mbar_arrive(smem_u32(&bars->o_free));
             }
+            it.next(P);
+            it.next(P);
         }
     }
 
@@ -594,6 +728,12 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
         mbar_arrive_remote(mapa(smem_u32(&bars->done), peer));
         if (!mbar_wait_cluster(smem_u32(&bars->done), 0, err, code(kWaitTeardown))) note_fail(err, kWaitTeardown, 0);
     }
+    if (threadIdx.x == 0 && *err != 0) {
+        // after a failure the peer may still have partial scores in flight towards this CTA
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 20000ull) {
+        }
+    }
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tbase, kTmemCols);
@@ -603,27 +743,38 @@ bool decode_sm100_available() { return true; }
 
 template <typename T>
 cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
-                                const float* sin, float* rec_ml, float* rec_o, cudaStream_t s) {
+                                const float* sin, float* rec_ml, float* rec_o, bool pdl, cudaStream_t s) {
     if (P.dc != 512 || P.dR != 64 || P.tile != kTileN) return cudaErrorInvalidValue;
-    CUtensorMap tmap, tcos, tsin;
+    CUtensorMap tmap, tmap_rope, tcos, tsin;
     // tables hold kv_pos_offset + max_len rows of d_R / 2 = 32 floats
     const uint64_t trows = static_cast<uint64_t>(P.kv_pos_offset) + static_cast<uint64_t>(P.max_len);
-    if (!make_tmap_2d_16b(&tmap, kv, static_cast<uint64_t>(P.kv_rows), 576, static_cast<uint64_t>(P.row_stride),
-                          64, 64) ||
-        !make_tmap_2d_f32(&tcos, cos, trows, 32, 32, 64, 32) || !make_tmap_2d_f32(&tsin, sin, trows, 32, 32, 64, 32))
+    const uint64_t rows = static_cast<uint64_t>(P.kv_rows), stride = static_cast<uint64_t>(P.row_stride);
+    if (!make_tmap_2d_16b(&tmap, kv, rows, 576, stride, 64, 64) ||
+        !make_tmap_2d_16b(&tmap_rope, kv, rows, 576, stride, 64, 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_tmap_2d_f32(&tcos, cos, trows, 32, 32, 64, 16) || !make_tmap_2d_f32(&tsin, sin, trows, 32, 32, 64, 16))
         return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(decode_sm100_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
-    decode_sm100_kernel<T><<<2 * P.W, kThreads, kSmemBytes, s>>>(tmap, tcos, tsin, P, qpack, rec_ml, rec_o);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * P.W);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    e = cudaLaunchKernelEx(&cfg, decode_sm100_kernel<T>, tmap, tmap_rope, tcos, tsin, P, qpack, rec_ml, rec_o);
     count_launches(1);
-    return cudaGetLastError();
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template cudaError_t launch_decode_sm100<__half>(const DecodePlan&, const __half*, const __half*, const float*,
-                                                 const float*, float*, float*, cudaStream_t);
+                                                 const float*, float*, float*, bool, cudaStream_t);
 template cudaError_t launch_decode_sm100<__nv_bfloat16>(const DecodePlan&, const __nv_bfloat16*,
                                                         const __nv_bfloat16*, const float*, const float*, float*,
-                                                        float*, cudaStream_t);
+                                                        float*, bool, cudaStream_t);
 
 }  // namespace mla

@@ -263,7 +263,9 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
         if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(timer)");
     }
     if (pl.use_tc)
-        e = mla::launch_decode_sm100<T>(d, kv, qpack, a->rope_cos, a->rope_sin, rec_ml, rec_o, s);
+        // with a timer the decode kernel must not overlap the packing kernel, so that the
+        // events bracket it exactly
+        e = mla::launch_decode_sm100<T>(d, kv, qpack, a->rope_cos, a->rope_sin, rec_ml, rec_o, a->timer == nullptr, s);
     else
         e = mla::launch_decode_simt<T>(d, kv, qpack, a->rope_cos, a->rope_sin, rec_ml, rec_o, s);
     if (e == cudaErrorNoKernelImageForDevice || e == cudaErrorInvalidDeviceFunction)

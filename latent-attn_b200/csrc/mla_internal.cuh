@@ -190,9 +190,11 @@ template <typename T>
 cudaError_t launch_decode_simt(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
                                const float* sin, float* rec_ml, float* rec_o, cudaStream_t s);
 // decode_sm100.cu
+// pdl: launch with a programmatic dependency on the previous kernel (its prologue and
+// cache loads overlap that kernel's tail)
 template <typename T>
 cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
-                                const float* sin, float* rec_ml, float* rec_o, cudaStream_t s);
+                                const float* sin, float* rec_ml, float* rec_o, bool pdl, cudaStream_t s);
 bool decode_sm100_available();
 // combine.cu
 template <typename T>
