@@ -51,14 +51,12 @@ using namespace sm100;
 namespace {
 
 constexpr int kTileN = 64;                          // positions per tile
-constexpr int kStages = 4;
+constexpr int kStages = 5;
 constexpr int kChunkBytes = 64 * 128;               // 64 rows x 64 latent columns, 128-byte swizzle
 constexpr int kRopeBoxBytes = 64 * 16;              // 64 rows x 8 rope columns, no swizzle
 constexpr int kRopeBytes = 4 * kRopeBoxBytes;
 constexpr int kStageBytes = kRopeBytes + 4 * kChunkBytes;   // [rope boxes | 4 latent chunks]
-constexpr int kTabBytes = 64 * 16 * 4;              // 64 positions x 16 frequencies, fp32
-constexpr int kTabSlotBytes = 2 * kTabBytes;        // cos | sin
-constexpr int kXSlots = 3;
+constexpr int kXSlots = 2;                          // slot j & 1: its previous user is the same softmax set
 constexpr int kXBytes = 128 * 128;                  // one slot: 128 rows x 64 fp16 partial scores
 constexpr int kQRopeBoxBytes = 128 * 16;            // 128 rows x 8 rope elements of Q, no swizzle
 constexpr int kQRopeBytes = 4 * kQRopeBoxBytes;
@@ -81,7 +79,6 @@ struct __align__(8) Barriers {
     uint64_t kv_full[kStages];
     uint64_t kv_empty[kStages];
     uint64_t tile_ready[kStages];
-    uint64_t tab_empty[2];
     uint64_t s_full[2];               // per softmax set: score of its next tile done (score j -> s_full[j & 1])
     uint64_t s_free;
     uint64_t p_full[2], pv_done[2];   // per P buffer (tile parity)
@@ -97,9 +94,9 @@ struct __align__(8) Barriers {
     uint32_t tmem_base;
 };
 
-constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 2 * kTabSlotBytes +
+constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes +
                               static_cast<size_t>(kXSlots) * kXBytes + kQRopeBytes +
-                              kMSlots * 128 * sizeof(float) + 2 * 2 * 128 * sizeof(float2) + sizeof(Barriers) + 1024;
+                              kMSlots * 128 * sizeof(float) + 2 * 2 * 128 * sizeof(float) + sizeof(Barriers) + 1024;
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 __device__ __forceinline__ int code(int site) { return kStatusTimeout | (site << 8); }
@@ -179,22 +176,42 @@ __device__ __forceinline__ float2 half2_to_f2(uint32_t v) {
     return __half22float2(*reinterpret_cast<const __half2*>(&v));
 }
 
+// Packed two-lane fp32 arithmetic (one instruction for both lanes on sm_100).
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 f2_sub(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "sub.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 }  // namespace
 
 template <typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_rope,
-                    const __grid_constant__ CUtensorMap tmap_cos, const __grid_constant__ CUtensorMap tmap_sin,
-                    const DecodePlan P, const T* __restrict__ qpack, float* __restrict__ rec_ml,
-                    float* __restrict__ rec_o) {
+                    const DecodePlan P, const T* __restrict__ qpack, const float* __restrict__ cos_tab,
+                    const float* __restrict__ sin_tab, float* __restrict__ rec_ml, float* __restrict__ rec_o) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     unsigned char* stages = smem;
-    unsigned char* tabs = stages + kStages * kStageBytes;
-    unsigned char* xbuf = tabs + 2 * kTabSlotBytes;
+    unsigned char* xbuf = stages + kStages * kStageBytes;
     unsigned char* qrope = xbuf + kXSlots * kXBytes;                       // Q's rope part, 4 core-matrix boxes
     float* m_pub = reinterpret_cast<float*>(qrope + kQRopeBytes);         // [kMSlots][128]: reference max of tile j
-    float2* l_pub = reinterpret_cast<float2*>(m_pub + kMSlots * 128);     // [set][2][128]: (row sum, its reference)
+    float* l_pub = m_pub + kMSlots * 128;  // [set][2][128]: row sum over the set's tiles, referenced to m_pub of its latest
     Barriers* bars = reinterpret_cast<Barriers*>(l_pub + 2 * 2 * 128);
 
     const uint32_t rank = cluster_ctarank();
@@ -205,11 +222,9 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
 
     if (threadIdx.x == 0) {
         pdl_launch_dependents();
-        // the first TMA of each map waits for its descriptor: fetch all four right away
+        // the first TMA of each map waits for its descriptor: fetch both right away
         tma_prefetch_desc(&tmap);
         tma_prefetch_desc(&tmap_rope);
-        tma_prefetch_desc(&tmap_cos);
-        tma_prefetch_desc(&tmap_sin);
     }
     // With variable lengths the tile prefix comes from the query-packing kernel: wait for it
     // before walking tiles. With uniform lengths only the packed queries depend on that
@@ -228,8 +243,6 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             mbar_init(smem_u32(&bars->kv_empty[s]), 1);
             mbar_init(smem_u32(&bars->tile_ready[s]), kTransformThreads);
         }
-        mbar_init(smem_u32(&bars->tab_empty[0]), kTransformThreads);
-        mbar_init(smem_u32(&bars->tab_empty[1]), kTransformThreads);
         mbar_init(smem_u32(&bars->s_full[0]), 1);
         mbar_init(smem_u32(&bars->s_full[1]), 1);
         mbar_init(smem_u32(&bars->s_free), 128);
@@ -258,7 +271,6 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
     tc_fence_after();
     const uint32_t tbase = bars->tmem_base;
     const uint32_t stages_u32 = smem_u32(stages);
-    const uint32_t tabs_u32 = smem_u32(tabs);
     const uint32_t xbuf_u32 = smem_u32(xbuf);
     const uint32_t qrope_u32 = smem_u32(qrope);
 
@@ -275,13 +287,8 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                     note_fail(err, kWaitProducer, i);
                     break;
                 }
-                if (i >= 2 &&
-                    !mbar_wait(smem_u32(&bars->tab_empty[i & 1]), ((i - 2) >> 1) & 1, err, code(kWaitProducer))) {
-                    note_fail(err, kWaitProducer, i);
-                    break;
-                }
                 const uint32_t full = smem_u32(&bars->kv_full[st]);
-                mbar_arrive_expect_tx(full, kStageBytes + kTabSlotBytes);
+                mbar_arrive_expect_tx(full, kStageBytes);
                 const int y = static_cast<int>(it.row0 + it.pos0());
                 const uint32_t dst = stages_u32 + st * kStageBytes;
                 // rope boxes: columns 16 r + {0, 8} and 32 + 16 r + {0, 8} of k_rope
@@ -290,10 +297,6 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                                 P.dc + 16 * static_cast<int>(rank) + 8 * (b & 1) + 32 * (b >> 1), y);
                 for (int j = 0; j < 4; ++j)
                     tma_load_2d(dst + kRopeBytes + j * kChunkBytes, &tmap, full, 256 * static_cast<int>(rank) + 64 * j, y);
-                const int yt = P.kv_pos_offset + it.pos0();
-                const uint32_t tdst = tabs_u32 + (i & 1) * kTabSlotBytes;
-                tma_load_2d(tdst, &tmap_cos, full, 16 * static_cast<int>(rank), yt);
-                tma_load_2d(tdst + kTabBytes, &tmap_sin, full, 16 * static_cast<int>(rank), yt);
                 issued = i + 1;
             }
             // shared memory must not be released under a TMA write: the last kStages loads (the
@@ -313,15 +316,21 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             // below 2^18, so the field never carries).
             const uint32_t tS = tbase + kColS, tQ = tbase + kColQ, tO = tbase + kColO;
             const uint64_t dqr = smem_desc_noswz(qrope_u32, kQRopeBoxBytes, 128);   // Q rope, A operand
-            auto issue_score = [&](int i) {
+            // The latent part of a score reads only the landed stage and Q, so it is issued as soon
+            // as the stage lands and runs while the transform rotates the rope part (rows past a
+            // sequence end may still be zeroed meanwhile: their score columns are masked).
+            auto issue_score_latent = [&](int i) {
                 const uint32_t sa = stages_u32 + (i % kStages) * kStageBytes;
                 const uint64_t dl = smem_desc_sw128(sa + kRopeBytes, 16, 1024);
-                const uint64_t dr = smem_desc_noswz(sa, kRopeBoxBytes, 128);
                 mma_ts(tS, tQ, dl, idesc_s, 0u);
 #pragma unroll
                 for (int k = 1; k < 16; ++k)
                     mma_ts(tS, tQ + 8 * k, dl + static_cast<uint64_t>(((k >> 2) * kChunkBytes + (k & 3) * 32) >> 4),
                            idesc_s, 1u);
+            };
+            auto issue_score_rope = [&](int i) {
+                const uint32_t sa = stages_u32 + (i % kStages) * kStageBytes;
+                const uint64_t dr = smem_desc_noswz(sa, kRopeBoxBytes, 128);
                 // rope: two 8-column core-matrix boxes per K = 16 step, 8-row groups 128 bytes apart
                 mma_ss(tS, dqr, dr, idesc_s, 1u);
                 mma_ss(tS, dqr + static_cast<uint64_t>((2 * kQRopeBoxBytes) >> 4),
@@ -339,31 +348,40 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                 mma_commit(smem_u32(&bars->kv_empty[i % kStages]));
             };
             // Scores and PVs are each issued in tile order, but interleaved as their inputs
-            // become ready: score(s) needs S released (s_free of tile s - 1), its stage
-            // transformed and, at a group start, the group's Q; PV(v) needs P(v) and, at a group
-            // start after the first, the previous group's O read out (o_free).
+            // become ready: the latent part of score(s) needs S released (s_free of tile s - 1),
+            // its stage landed and, at a group start, the group's Q; the rope part needs the stage
+            // transformed; PV(v) needs P(v) and, at a group start after the first, the previous
+            // group's O read out (o_free).
             TileIter its, itv;
             its.init(P, tb, te);
             itv = its;
-            int next_s = 0, next_v = 0, qseg = 0, vseg = 0;
+            int next_s = 0, next_r = 0, next_v = 0, qseg = 0, vseg = 0;
             bool ok = true;
-            uint64_t t_last = globaltimer_ns();
+            long long t_last = clock64();
+            const long long budget = wait_budget_cycles(kDefaultWaitNs);
             for (uint32_t spin = 0; ok && next_v < n; ++spin) {
                 bool progressed = false;
-                if (next_s < n) {
+                if (next_s < n && next_r == next_s) {
                     bool ready = (next_s == 0 || mbar_test(smem_u32(&bars->s_free), (next_s - 1) & 1)) &&
-                                 mbar_test(smem_u32(&bars->tile_ready[next_s % kStages]), (next_s / kStages) & 1) &&
+                                 mbar_test(smem_u32(&bars->kv_full[next_s % kStages]), (next_s / kStages) & 1) &&
                                  (!its.seg_first() || mbar_test(smem_u32(&bars->q_ready), qseg & 1));
                     if (ready) {
                         tc_fence_after();
-                        issue_score(next_s);
+                        issue_score_latent(next_s);
                         if (its.seg_last()) ++qseg;
                         its.next(P);
                         ++next_s;
                         progressed = true;
                     }
                 }
-                if (next_v < next_s) {
+                if (next_r < next_s &&
+                    mbar_test(smem_u32(&bars->tile_ready[next_r % kStages]), (next_r / kStages) & 1)) {
+                    tc_fence_after();
+                    issue_score_rope(next_r);
+                    ++next_r;
+                    progressed = true;
+                }
+                if (next_v < next_r) {
                     bool ready = mbar_test(smem_u32(&bars->p_full[next_v & 1]), (next_v >> 1) & 1) &&
                                  (!itv.seg_first() || vseg == 0 || mbar_test(smem_u32(&bars->o_free), (vseg - 1) & 1));
                     if (ready) {
@@ -376,14 +394,15 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                     }
                 }
                 if (progressed) {
-                    t_last = globaltimer_ns();
+                    t_last = clock64();
                     continue;
                 }
                 // back off: this lane shares its SM sub-partition with softmax warps, and every
                 // poll takes an issue slot from them
                 __nanosleep(64);
                 if ((spin & 31u) == 0u) {
-                    if (*err != 0 || globaltimer_ns() - t_last > kDefaultWaitNs) {
+                    const long long dt = clock64() - t_last;
+                    if ((dt > kErrPollCycles && *err != 0) || dt > budget) {
                         atomicCAS(const_cast<int*>(err), 0, code(kWaitMma));
                         note_fail(err, kWaitMma, next_v);
                         ok = false;
@@ -397,10 +416,45 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
     } else if (warp < 4) {
         // ------------------------------------------------------------ tile transform
         const int tt = threadIdx.x - 64;  // 0 .. kTransformThreads - 1
+        // rotate-half RoPE of this CTA's 16 frequency pairs: item (row p, half h) rotates
+        // box h (columns 16 r + 8 h ..) against box 2 + h (columns 32 + 16 r + 8 h ..) with the
+        // 8 cos / sin values of table row kv_pos_offset + position, columns 16 r + 8 h ..
+        // Each thread owns items tt and tt + 64 of every tile and reads their table values
+        // from global memory one tile ahead, so the loads overlap the tile before.
+        constexpr int kItems = 128 / kTransformThreads;
+        float4 tab_next[kItems][4];  // per item: cos[0:4], cos[4:8], sin[0:4], sin[4:8]
+        auto load_tabs = [&](const TileIter& ti) {
+            const int tnp = ti.np();
+#pragma unroll
+            for (int u = 0; u < kItems; ++u) {
+                const int item = tt + kTransformThreads * u, p = item >> 1, h = item & 1;
+                if (p < tnp) {
+                    const long long off = (static_cast<long long>(P.kv_pos_offset) + ti.pos0() + p) * 32 +
+                                          16 * static_cast<int>(rank) + 8 * h;
+                    const float4* c4 = reinterpret_cast<const float4*>(cos_tab + off);
+                    const float4* s4 = reinterpret_cast<const float4*>(sin_tab + off);
+                    tab_next[u][0] = __ldg(c4);
+                    tab_next[u][1] = __ldg(c4 + 1);
+                    tab_next[u][2] = __ldg(s4);
+                    tab_next[u][3] = __ldg(s4 + 1);
+                }
+            }
+        };
         TileIter it;
         it.init(P, tb, te);
+        load_tabs(it);
         for (int i = 0; it.valid(); ++i, it.next(P)) {
             const int st = i % kStages;
+            float4 tab[kItems][4];
+#pragma unroll
+            for (int u = 0; u < kItems; ++u)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) tab[u][q] = tab_next[u][q];
+            {
+                TileIter nx = it;
+                nx.next(P);
+                if (nx.valid()) load_tabs(nx);
+            }
             if (!mbar_wait(smem_u32(&bars->kv_full[st]), (i / kStages) & 1, err, code(kWaitTransform))) {
                 note_fail(err, kWaitTransform, i);
                 break;
@@ -420,23 +474,17 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                     *reinterpret_cast<uint4*>(sp + (v / rows) * kRopeBoxBytes + (np + v % rows) * 16) =
                         make_uint4(0, 0, 0, 0);
             }
-            // rotate-half RoPE of this CTA's 16 frequency pairs: item (row p, half h) rotates
-            // box h (columns 16 r + 8 h ..) against box 2 + h (columns 32 + 16 r + 8 h ..)
-            const float* tcs = reinterpret_cast<const float*>(tabs + (i & 1) * kTabSlotBytes);
-            const float* tsn = tcs + kTabBytes / 4;
-#pragma unroll 1
-            for (int u = 0; u < 128 / kTransformThreads; ++u) {
+#pragma unroll
+            for (int u = 0; u < kItems; ++u) {
                 const int item = tt + kTransformThreads * u, p = item >> 1, h = item & 1;
                 if (p < np) {
                     uint4* a = reinterpret_cast<uint4*>(sp + h * kRopeBoxBytes + p * 16);
                     uint4* b = reinterpret_cast<uint4*>(sp + (2 + h) * kRopeBoxBytes + p * 16);
                     const uint4 ka = *a, kb = *b;
-                    const float4 c0 = *reinterpret_cast<const float4*>(tcs + p * 16 + 8 * h);
-                    const float4 c1 = *reinterpret_cast<const float4*>(tcs + p * 16 + 8 * h + 4);
-                    const float4 s0 = *reinterpret_cast<const float4*>(tsn + p * 16 + 8 * h);
-                    const float4 s1 = *reinterpret_cast<const float4*>(tsn + p * 16 + 8 * h + 4);
-                    const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+                    const float cs[8] = {tab[u][0].x, tab[u][0].y, tab[u][0].z, tab[u][0].w,
+                                         tab[u][1].x, tab[u][1].y, tab[u][1].z, tab[u][1].w};
+                    const float sn[8] = {tab[u][2].x, tab[u][2].y, tab[u][2].z, tab[u][2].w,
+                                         tab[u][3].x, tab[u][3].y, tab[u][3].z, tab[u][3].w};
                     const uint32_t xa[4] = {ka.x, ka.y, ka.z, ka.w}, xb[4] = {kb.x, kb.y, kb.z, kb.w};
                     uint32_t ya[4], yb[4];
 #pragma unroll
@@ -452,7 +500,6 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             }
             fence_proxy_async_smem();
             mbar_arrive(smem_u32(&bars->tile_ready[st]));
-            mbar_arrive(smem_u32(&bars->tab_empty[i & 1]));
         }
     } else {
         // ------------------------------------------------------------ softmax sets
@@ -530,8 +577,8 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                 if (!got) note_fail(err, kWaitSoftS, j);
                 break;
             }
-            // the score of tile j implies the other set has finished with tile j - 3's slot, so the
-            // slot's previous phase is complete before this arrival opens the next one
+            // the slot's previous user is this set's tile j - 2, whose data this set has already
+            // waited for: the slot's previous phase is complete before this arrival opens the next
             if (t == 0) mbar_arrive_expect_tx(smem_u32(&bars->x_full[slot]), kXBytes);
             tc_fence_after();
             uint32_t h[32];
@@ -551,7 +598,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                 nx.next(P);
                 load_q(nx.g);
             }
-            // the peer reads its slot for tile j - 3 before this CTA writes it again
+            // the peer reads its slot for tile j - 2 before this CTA writes it again
             got = j < kXSlots ||
                   mbar_wait_cluster(smem_u32(&bars->x_empty[slot]), ((j / kXSlots) - 1) & 1, err, code(kWaitCredit));
             if (!warp_ok(got)) {
@@ -573,7 +620,6 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                 break;
             }
             float s[64];
-            const int np = it.np();
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 uint4 v;
@@ -583,16 +629,26 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                 const uint32_t pv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    const float2 a = half2_to_f2(h[4 * c + q]);
-                    const float2 b = half2_to_f2(pv[q]);
-                    const int k = 8 * c + 2 * q;
-                    s[k] = k < np ? a.x + b.x : -INFINITY;
-                    s[k + 1] = k + 1 < np ? a.y + b.y : -INFINITY;
+                    const float2 r = f2_add(half2_to_f2(h[4 * c + q]), half2_to_f2(pv[q]));
+                    s[8 * c + 2 * q] = r.x;
+                    s[8 * c + 2 * q + 1] = r.y;
                 }
             }
-            // credit for the peer: this warp's rows of the slot are read
+            // credit for the peer: this warp's rows of the slot are read. The arrive is relaxed: a
+            // cluster-scope release would first wait for the acknowledgement of this thread's
+            // st.async stores above (most of a microsecond under load). What it must follow are
+            // reads of this CTA's own shared memory, issued before the __syncwarp; the peer writes
+            // the slot again only after this arrive has crossed the cluster and the peer has
+            // observed it and sent new data back.
             __syncwarp();
-            if (lane == 0) mbar_arrive_remote(mapa(smem_u32(&bars->x_empty[slot]), peer));
+            if (lane == 0) mbar_arrive_remote_relaxed(mapa(smem_u32(&bars->x_empty[slot]), peer));
+            const int np = it.np();
+            if (np < kTileN) {
+                // the group's last tile: positions past the sequence end take no weight
+#pragma unroll
+                for (int k = 0; k < kTileN; ++k)
+                    if (k >= np) s[k] = -INFINITY;
+            }
             float mx[32];
 #pragma unroll
             for (int k = 0; k < 32; ++k) mx[k] = fmaxf(s[k], s[k + 32]);
@@ -621,20 +677,21 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             }
             m_pub[(j % kMSlots) * 128 + t] = m;
             mbar_arrive(smem_u32(&bars->mref[j % kMSlots]));
+            // P = 2^(s - m) rounded to the cache type for the PV MMA; the row sum adds the fp32 values
             uint32_t pp[32];
-            float ls[16];
+            float2 ls[8];
+            const float2 m2 = make_float2(m, m);
 #pragma unroll
             for (int q = 0; q < 32; ++q) {
-                const uint32_t v = pack2<T>(ex2_approx(s[2 * q] - m), ex2_approx(s[2 * q + 1] - m));
-                pp[q] = v;
-                const float2 f = unpack2<T>(v);
-                if (q < 16) ls[q] = f.x + f.y;
-                else ls[q - 16] += f.x + f.y;
+                const float2 d = f2_sub(make_float2(s[2 * q], s[2 * q + 1]), m2);
+                const float2 e = make_float2(ex2_approx(d.x), ex2_approx(d.y));
+                pp[q] = pack2<T>(e.x, e.y);
+                ls[q & 7] = q < 8 ? e : f2_add(ls[q & 7], e);
             }
 #pragma unroll
-            for (int w2 = 8; w2 > 0; w2 >>= 1)
+            for (int w2 = 4; w2 > 0; w2 >>= 1)
 #pragma unroll
-                for (int k = 0; k < w2; ++k) ls[k] += ls[k + w2];
+                for (int k = 0; k < w2; ++k) ls[k] = f2_add(ls[k], ls[k + w2]);
             // this set's row sum restarts at its first tile of a group and follows the reference
             if (it.seg_first() || it.prev_seg_first()) {
                 l_self = 0.f;
@@ -642,7 +699,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                 l_self *= ex2_approx(m_l - m);
             }
             m_l = m;
-            l_self += ls[0];
+            l_self += ls[0].x + ls[0].y;
             // P buffer j & 1 is free once PV(j - 2) has completed
             got = j < 2 || mbar_wait(smem_u32(&bars->pv_done[j & 1]), ((j - 2) >> 1) & 1, err, code(kWaitSoftPV));
             if (!warp_ok(got)) {
@@ -673,7 +730,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             tc_fence_before();
             mbar_arrive(smem_u32(&bars->p_full[j & 1]));
             // publish this set's row sum (slot by the set's tile count)
-            l_pub[(sid * 2 + ((j >> 1) & 1)) * 128 + t] = make_float2(l_self, m_l);
+            l_pub[(sid * 2 + ((j >> 1) & 1)) * 128 + t] = l_self;
             mbar_arrive(smem_u32(&bars->lpub[sid * 2 + ((j >> 1) & 1)]));
 
             if (it.seg_last()) {
@@ -686,8 +743,9 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                     // the other set's tiles of the group end at tile j - 1
                     got = mbar_wait(smem_u32(&bars->lpub[(sid ^ 1) * 2 + (((j - 1) >> 1) & 1)]), ((j - 1) >> 2) & 1, err,
                                    code(kWaitSoftRef));
-                    const float2 lo = l_pub[((sid ^ 1) * 2 + (((j - 1) >> 1) & 1)) * 128 + t];
-                    l_tot += lo.x * ex2_approx(lo.y - m);
+                    // its reference is tile j - 1's, still in m_pub (tile j + 3 overwrites that slot)
+                    const float lo = l_pub[((sid ^ 1) * 2 + (((j - 1) >> 1) & 1)) * 128 + t];
+                    l_tot += lo * ex2_approx(m_pub[((j - 1) % kMSlots) * 128 + t] - m);
                 }
                 if (!warp_ok(got)) {
                     if (!got) note_fail(err, site, j);
@@ -726,7 +784,8 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
     if (threadIdx.x == 0) {
         // the pair finishes together: no CTA leaves while the other may still address it
         mbar_arrive_remote(mapa(smem_u32(&bars->done), peer));
-        if (!mbar_wait_cluster(smem_u32(&bars->done), 0, err, code(kWaitTeardown))) note_fail(err, kWaitTeardown, 0);
+        if (!mbar_wait_cluster_full(smem_u32(&bars->done), 0, err, code(kWaitTeardown)))
+            note_fail(err, kWaitTeardown, 0);
     }
     if (threadIdx.x == 0 && *err != 0) {
         // after a failure the peer may still have partial scores in flight towards this CTA
@@ -745,13 +804,12 @@ template <typename T>
 cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
                                 const float* sin, float* rec_ml, float* rec_o, bool pdl, cudaStream_t s) {
     if (P.dc != 512 || P.dR != 64 || P.tile != kTileN) return cudaErrorInvalidValue;
-    CUtensorMap tmap, tmap_rope, tcos, tsin;
-    // tables hold kv_pos_offset + max_len rows of d_R / 2 = 32 floats
-    const uint64_t trows = static_cast<uint64_t>(P.kv_pos_offset) + static_cast<uint64_t>(P.max_len);
+    CUtensorMap tmap, tmap_rope;
     const uint64_t rows = static_cast<uint64_t>(P.kv_rows), stride = static_cast<uint64_t>(P.row_stride);
+    // the tables (kv_pos_offset + max_len rows of d_R / 2 = 32 floats) are read as float4
+    if ((reinterpret_cast<uintptr_t>(cos) | reinterpret_cast<uintptr_t>(sin)) & 15u) return cudaErrorInvalidValue;
     if (!make_tmap_2d_16b(&tmap, kv, rows, 576, stride, 64, 64) ||
-        !make_tmap_2d_16b(&tmap_rope, kv, rows, 576, stride, 64, 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_tmap_2d_f32(&tcos, cos, trows, 32, 32, 64, 16) || !make_tmap_2d_f32(&tsin, sin, trows, 32, 32, 64, 16))
+        !make_tmap_2d_16b(&tmap_rope, kv, rows, 576, stride, 64, 8, CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(decode_sm100_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kSmemBytes));
@@ -766,7 +824,7 @@ cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    e = cudaLaunchKernelEx(&cfg, decode_sm100_kernel<T>, tmap, tmap_rope, tcos, tsin, P, qpack, rec_ml, rec_o);
+    e = cudaLaunchKernelEx(&cfg, decode_sm100_kernel<T>, tmap, tmap_rope, P, qpack, cos, sin, rec_ml, rec_o);
     count_launches(1);
     return e != cudaSuccess ? e : cudaGetLastError();
 }

@@ -39,6 +39,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
+// Arrive without release semantics. A cluster-scope release waits until every earlier
+// store of the thread, remote st.async included, has been acknowledged; use this form
+// where the arrive only has to follow the thread's earlier reads of its own CTA's memory.
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -81,34 +87,51 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
-// Bounded waits: give up after `timeout_ns` of wall time (read from %globaltimer,
-// so the bound holds whatever try_wait's internal suspend time is), record `code`
-// in *err and return false; also return early once another thread has recorded
-// an error. Never hangs.
+// Bounded waits: give up after `timeout_ns` (counted in SM clock cycles at two per
+// nanosecond, so the bound is at least `timeout_ns` at any clock up to 2 GHz and holds
+// whatever try_wait's internal suspend time is), record `code` in *err and return false.
+// A wait that has already lasted kErrPollCycles also returns early once another thread
+// has recorded an error. The error word is read only on that slow path: a global load
+// in the polling loop of a wait on the critical path would delay the wait's return by
+// an L2 round trip whenever the barrier completes during the load. Never hangs.
 constexpr uint64_t kDefaultWaitNs = 2000000000ull;  // 2 s
+constexpr long long kErrPollCycles = 2000000;      // about 1 ms
 
-template <bool kCluster>
+__device__ __forceinline__ long long wait_budget_cycles(uint64_t timeout_ns) {
+    return static_cast<long long>(2 * timeout_ns);
+}
+
+template <bool kCluster, bool kPollErr>
 __device__ __forceinline__ bool mbar_wait_impl(uint32_t bar, uint32_t parity, volatile int* err, int code,
                                                uint64_t timeout_ns) {
     if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
+    const long long c0 = clock64();
+    const long long budget = wait_budget_cycles(timeout_ns);
     for (uint32_t i = 1;; ++i) {
         if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 0u) {
-            if (*err != 0) return false;
-            if (globaltimer_ns() - t0 > timeout_ns) break;
+            const long long dt = clock64() - c0;
+            if (kPollErr && dt > kErrPollCycles && *err != 0) return false;
+            if (dt > budget) break;
         }
     }
     atomicCAS(const_cast<int*>(err), 0, code);
     return false;
 }
+
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* err, int code,
                                           uint64_t timeout_ns = kDefaultWaitNs) {
-    return mbar_wait_impl<false>(bar, parity, err, code, timeout_ns);
+    return mbar_wait_impl<false, true>(bar, parity, err, code, timeout_ns);
 }
 __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* err, int code,
                                                   uint64_t timeout_ns = kDefaultWaitNs) {
-    return mbar_wait_impl<true>(bar, parity, err, code, timeout_ns);
+    return mbar_wait_impl<true, true>(bar, parity, err, code, timeout_ns);
+}
+// Cluster wait that only ends on completion or timeout, also after another thread recorded
+// an error: for hand-shakes that keep a CTA alive while its peer may still address it.
+__device__ __forceinline__ bool mbar_wait_cluster_full(uint32_t bar, uint32_t parity, volatile int* err, int code,
+                                                       uint64_t timeout_ns = kDefaultWaitNs) {
+    return mbar_wait_impl<true, false>(bar, parity, err, code, timeout_ns);
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
