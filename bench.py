@@ -20,6 +20,12 @@ The metric is the latent-cache bytes a step reads divided by the step time
 (whole job: summed over GPUs, time = max over GPUs); the step time itself is
 reported as ms_per_step / us_per_step. L2 is flushed (256 MiB write) before
 every timed step because the config-1 inputs fit in the 126 MB L2.
+
+Device-timed leg: each timed step is one replay of a CUDA graph captured from the
+public call (latent_attn.functional.mla_decode), so the events bracket the step's
+kernels rather than the host's time to enqueue them (--eager launches it directly).
+The multi-GPU KV-range step holds an NCCL collective and always runs eagerly.
+The end-to-end leg calls the public API every step, with the host copies inside.
 """
 
 from __future__ import annotations
@@ -50,6 +56,7 @@ def parse_args():
     ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default="cfg1")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU baseline leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="launch the device-timed steps directly, not from CUDA graphs")
     return ap.parse_args()
 
 
@@ -330,6 +337,21 @@ def main():
     status_word = ws[:4].view(torch.int32)
     status_sum = torch.zeros(1, dtype=torch.int32, device=dev)
     host_s = 0.0
+    use_graphs = not args.eager and not (spec["sharding"] == "kv-range" and world > 1)
+    graphs = []
+    if use_graphs:
+        # one graph per timed step, each with its own decode-kernel timer
+        launches0 = _lib.kernel_launch_count()
+        side = torch.cuda.Stream(dev)
+        for k in range(args.steps):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                step(t=timers[k])
+            graphs.append(g)
+        per_step = (_lib.kernel_launch_count() - launches0) / args.steps
+        for g in graphs[:3]:
+            g.replay()
+        torch.cuda.synchronize(dev)
     launches0 = _lib.kernel_launch_count()
     barrier()
     clocks.mark(True)
@@ -337,13 +359,18 @@ def main():
         flush.zero_()
         ev0[k].record(stream)
         h0 = time.perf_counter()
-        step(t=timers[k])
+        if use_graphs:
+            graphs[k].replay()
+        else:
+            step(t=timers[k])
         host_s += time.perf_counter() - h0
         ev1[k].record(stream)
         status_sum.add_(status_word[:1].clamp(0, 1))
     barrier()
     clocks.mark(False)
     launches = _lib.kernel_launch_count() - launches0
+    if use_graphs:
+        launches = int(round(per_step * args.steps))  # the graphs' kernels, counted when captured
     step_ms = [a.elapsed_time(b) for a, b in zip(ev0, ev1)]
     dec_ms = [t.decode_ms() for t in timers]
     for t in timers:
@@ -422,6 +449,7 @@ def main():
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_max / args.steps, 5),
                     "api": "latent_attn.functional.mla_decode (q_nope/q_rope pinned host -> device, output -> host)"},
             "gpu_launches": int(launches),
+            "launch": "cuda-graph replay per step" if use_graphs else "direct",
             "host_us_per_step_call": round(host_s / args.steps * 1e6, 1),
             "decode_status_errors": status_errors,
             "output_finite": bool(torch.isfinite(out).all()),

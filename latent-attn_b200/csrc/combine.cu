@@ -272,8 +272,8 @@ cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const float
                            float* out, float* part_ml, float* part_o, cudaStream_t s) {
     if (P.W > kMaxRec) return cudaErrorInvalidValue;
     const size_t smem = static_cast<size_t>(kTok) * P.dc * sizeof(float);
-    cudaError_t e = cudaFuncSetAttribute(combine_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    cudaError_t e =
+        ensure_dynamic_smem(reinterpret_cast<const void*>(combine_kernel<T>), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     dim3 grid(P.H, ceil_div(P.B, kTok));
     combine_kernel<T><<<grid, kThreads, smem, s>>>(P, rec_ml, rec_o, W_UV, out, part_ml, part_o);
@@ -286,8 +286,8 @@ cudaError_t launch_combine_parts(int B, int H, int dc, int dv, int parts, const 
                                  const float* part_o, const T* W_UV, float* out, cudaStream_t s) {
     if (parts > 64) return cudaErrorInvalidValue;
     const size_t smem = static_cast<size_t>(kTok) * dc * sizeof(float);
-    cudaError_t e = cudaFuncSetAttribute(combine_parts_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    cudaError_t e =
+        ensure_dynamic_smem(reinterpret_cast<const void*>(combine_parts_kernel<T>), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     dim3 grid(H, ceil_div(B, kTok));
     combine_parts_kernel<T><<<grid, kThreads, smem, s>>>(B, H, dc, dv, parts, part_ml, part_o, W_UV, out);

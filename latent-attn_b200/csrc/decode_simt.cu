@@ -161,8 +161,8 @@ cudaError_t launch_decode_simt(const DecodePlan& P, const T* kv, const T* qpack,
     const int K = P.dc + P.dR;
     size_t smem = static_cast<size_t>(kTile) * (K / 2 + 1) * 4 + static_cast<size_t>(kTile) * (P.dR + 1) * 4 +
                   static_cast<size_t>(kWarps) * K * 4;
-    cudaError_t e = cudaFuncSetAttribute(decode_simt_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    cudaError_t e =
+        ensure_dynamic_smem(reinterpret_cast<const void*>(decode_simt_kernel<T>), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     dim3 grid(P.W, kGroupRows / kWarps);
     decode_simt_kernel<T><<<grid, kWarps * 32, smem, s>>>(P, kv, qpack, cos, sin, rec_ml, rec_o);

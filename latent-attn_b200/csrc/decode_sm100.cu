@@ -176,6 +176,16 @@ __device__ __forceinline__ float2 half2_to_f2(uint32_t v) {
     return __half22float2(*reinterpret_cast<const __half2*>(&v));
 }
 
+// 32 consecutive fp32 values (32-byte aligned) as four 256-bit stores.
+__device__ __forceinline__ void st_row32(float* p, const uint32_t (&v)[32]) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p + 8 * q), "r"(v[8 * q]),
+                     "r"(v[8 * q + 1]), "r"(v[8 * q + 2]), "r"(v[8 * q + 3]), "r"(v[8 * q + 4]), "r"(v[8 * q + 5]),
+                     "r"(v[8 * q + 6]), "r"(v[8 * q + 7])
+                     : "memory");
+}
+
 // Packed two-lane fp32 arithmetic (one instruction for both lanes on sm_100).
 __device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
     float2 d;
@@ -755,18 +765,19 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                 const int rec = it.g + w;
                 const bool row_ok = t < group_rows(P, it.g);
                 float* orow = rec_o + (static_cast<long long>(rec) * kGroupRows + t) * 512 + 256 * rank;
-#pragma unroll 1
-                for (int c0 = 0; c0 < 256; c0 += 32) {
-                    uint32_t o[32];
-                    tmem_ld32(trow + kColO + c0, o);
-                    tmem_ld_wait();
-                    if (row_ok) {
+                // 32 columns at a time, the next chunk's TMEM load in flight during this chunk's
+                // stores; 32-byte stores halve the store instructions of this row-per-thread layout
+                uint32_t oa[32], ob[32];
+                tmem_ld32(trow + kColO, oa);
+                tmem_ld_wait();
 #pragma unroll
-                        for (int v = 0; v < 8; ++v)
-                            *reinterpret_cast<float4*>(orow + c0 + 4 * v) =
-                                make_float4(__uint_as_float(o[4 * v]), __uint_as_float(o[4 * v + 1]),
-                                            __uint_as_float(o[4 * v + 2]), __uint_as_float(o[4 * v + 3]));
-                    }
+                for (int c0 = 0; c0 < 256; c0 += 64) {
+                    tmem_ld32(trow + kColO + c0 + 32, ob);
+                    if (row_ok) st_row32(orow + c0, oa);
+                    tmem_ld_wait();
+                    if (c0 + 64 < 256) tmem_ld32(trow + kColO + c0 + 64, oa);
+                    if (row_ok) st_row32(orow + c0 + 32, ob);
+                    tmem_ld_wait();
                 }
                 if (rank == 0 && row_ok)
                     *reinterpret_cast<float2*>(rec_ml + (static_cast<long long>(rec) * kGroupRows + t) * 2) =
@@ -811,8 +822,8 @@ cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack
     if (!make_tmap_2d_16b(&tmap, kv, rows, 576, stride, 64, 64) ||
         !make_tmap_2d_16b(&tmap_rope, kv, rows, 576, stride, 64, 8, CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(decode_sm100_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmemBytes));
+    cudaError_t e =
+        ensure_dynamic_smem(reinterpret_cast<const void*>(decode_sm100_kernel<T>), static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * P.W);

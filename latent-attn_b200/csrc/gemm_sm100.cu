@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(128)
 absorb_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ q_nope,
                     const float* __restrict__ q_rope, float q_scale, T* __restrict__ qpack, int* tile_prefix_out,
                     int ntp, uint32_t tmem_cols) {
+    clear_status(P);
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int dn = P.dn, dc = P.dc, K = P.dc + P.dR;
@@ -496,8 +497,7 @@ cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const 
         return cudaErrorInvalidValue;
     const int ntp = pad16(P.B < kAbsorbTok ? P.B : kAbsorbTok);
     const size_t smem = 1024 + 2 * P.dn * 128 + absorb_b_bytes(P.dn, ntp) + 64;
-    cudaError_t e = cudaFuncSetAttribute(absorb_sm100_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(absorb_sm100_kernel<T>), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     dim3 grid(P.dc / 128, P.H, ceil_div(P.B, kAbsorbTok));
     e = launch_ex(absorb_sm100_kernel<T>, grid, dim3(128), smem, s, false, tmap, P, q_nope, q_rope, q_scale, qpack,
@@ -518,8 +518,7 @@ cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const
     const int nk = P.dc / 64;
     const size_t smem = 1024 + static_cast<size_t>(nk) * P.dv * 128 + static_cast<size_t>(nk) * ntp * 128 +
                         sizeof(ProjLists) + kRedFloats * sizeof(float) + 64;
-    cudaError_t e = cudaFuncSetAttribute(project_sm100_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(project_sm100_kernel<T>), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     dim3 grid(ceil_div(P.B, kProjTok), P.H);
     e = launch_ex(project_sm100_kernel<T>, grid, dim3(256), smem, s, pdl, tmap, P, rec_ml, rec_o, out, ntp,

@@ -243,8 +243,8 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
     T* qpack = reinterpret_cast<T*>(ws + pl.off_qpack);
     float* rec_ml = reinterpret_cast<float*>(ws + pl.off_rec_ml);
     float* rec_o = reinterpret_cast<float*>(ws + pl.off_rec_o);
-    cudaError_t e = cudaMemsetAsync(d.status, 0, sizeof(int), s);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
+    // the status words are cleared by the first kernel below (clear_status)
+    cudaError_t e = cudaSuccess;
     int* prefix_out = d.uniform_len > 0 ? nullptr : prefix;
     if (!a->q_absorbed && pl.use_gemm_absorb) {
         e = mla::launch_pack_zero_pad<T>(d, qpack, s);
@@ -259,7 +259,9 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
     }
     const T* kv = reinterpret_cast<const T*>(a->kv_cache);
     if (a->timer) {
-        e = cudaEventRecord(a->timer->begin, s);
+        // External: under stream capture the record becomes a graph node that fires on every
+        // replay (a plain record would only express a dependency); otherwise a normal record.
+        e = cudaEventRecordWithFlags(a->timer->begin, s, cudaEventRecordExternal);
         if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(timer)");
     }
     if (pl.use_tc)
@@ -272,7 +274,7 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
         return fail(MLA_ERR_NO_DEVICE_CODE, "decode kernel: %s (library is built for sm_100a)", cudaGetErrorString(e));
     if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
     if (a->timer) {
-        e = cudaEventRecord(a->timer->end, s);
+        e = cudaEventRecordWithFlags(a->timer->end, s, cudaEventRecordExternal);
         if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(timer)");
         a->timer->recorded = true;
     }

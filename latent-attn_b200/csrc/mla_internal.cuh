@@ -20,6 +20,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <mutex>
+#include <vector>
 
 namespace mla {
 
@@ -114,6 +116,13 @@ __device__ inline int group_of_tile(const DecodePlan& P, int t) {
     return lo;
 }
 
+// The first kernel of a decode call clears the status words (the decode kernel writes
+// them only after a wait has failed, at least a millisecond after it starts).
+__device__ inline void clear_status(const DecodePlan& P) {
+    if (P.status && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x < 4)
+        P.status[threadIdx.x] = 0;
+}
+
 // Tiles per group, prefix-summed into prefix[0 .. G] (variable-length batches).
 // Run by one whole block; G is small (batch * head_blocks).
 __device__ inline void write_tile_prefix(const DecodePlan& P, int* prefix) {
@@ -203,5 +212,31 @@ cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const float
 template <typename T>
 cudaError_t launch_combine_parts(int B, int H, int dc, int dv, int parts, const float* part_ml,
                                  const float* part_o, const T* W_UV, float* out, cudaStream_t s);
+
+// Raises a kernel's dynamic shared-memory limit once per device: the attribute persists,
+// and setting it on every launch would cost host time in every decode call.
+inline cudaError_t ensure_dynamic_smem(const void* kernel, int bytes) {
+    struct Entry {
+        const void* kernel;
+        int dev, bytes;
+    };
+    static std::mutex mu;
+    static std::vector<Entry> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    for (const Entry& x : done)
+        if (x.kernel == kernel && x.dev == dev && x.bytes >= bytes) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    for (Entry& x : done)
+        if (x.kernel == kernel && x.dev == dev) {
+            x.bytes = bytes;
+            return e;
+        }
+    done.push_back({kernel, dev, bytes});
+    return e;
+}
 
 }  // namespace mla

@@ -17,6 +17,7 @@ template <typename T>
 __global__ void pack_q_copy_kernel(DecodePlan P, const float* __restrict__ q_abs,
                                    const float* __restrict__ q_rope, float q_scale,
                                    T* __restrict__ qpack, int* tile_prefix_out) {
+    clear_status(P);
     if (tile_prefix_out && blockIdx.x == 0) write_tile_prefix(P, tile_prefix_out);
     const int K = P.dc + P.dR;
     const long long total = static_cast<long long>(P.G) * kGroupRows * K;
@@ -47,6 +48,7 @@ __global__ void __launch_bounds__(256)
 pack_q_absorb_kernel(DecodePlan P, const float* __restrict__ q_nope, const T* __restrict__ W_UK,
                      const float* __restrict__ q_rope, float q_scale, T* __restrict__ qpack,
                      int* tile_prefix_out) {
+    clear_status(P);
     if (tile_prefix_out && blockIdx.x == 0 && blockIdx.y == 0) write_tile_prefix(P, tile_prefix_out);
     extern __shared__ float smem[];
     const int h = blockIdx.x;
@@ -153,8 +155,8 @@ cudaError_t launch_pack_q(const DecodePlan& P, const float* q_absorbed, const fl
     const int RG = 256 / ncg > 0 ? 256 / ncg : 1;
     size_t smem = (static_cast<size_t>(kTok) * P.dn + static_cast<size_t>(RG) * kTok * P.dc) * sizeof(float);
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(pack_q_absorb_kernel<T, kTok>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        cudaError_t e =
+            ensure_dynamic_smem(reinterpret_cast<const void*>(pack_q_absorb_kernel<T, kTok>), static_cast<int>(smem));
         if (e != cudaSuccess) return e;
     }
     pack_q_absorb_kernel<T, kTok><<<grid, 256, smem, s>>>(P, q_nope, W_UK, q_rope, q_scale, qpack,
