@@ -65,7 +65,10 @@ __device__ __forceinline__ long long qpack_row(const DecodePlan& P, int b, int h
 
 constexpr int kAbsorbTok = 256;    // tokens per absorption CTA (MMA N <= 256)
 constexpr int kProjTok = 64;       // tokens per projection CTA
-constexpr int kRedFloats = 8 * 512;  // split partial sums of the merge (S * ntok <= 8 rows of d_c <= 512)
+constexpr int kProjWarps = 16;     // projection CTA: 16 warps merge, warp 0 issues the MMA, warps 4-7 store
+// rows of split partial sums of the merge (S * ntok <= rows): 16 when the token operand is at most
+// 16 rows, else 8, which keeps the largest configuration inside the shared-memory limit
+__host__ __device__ constexpr int proj_red_rows(int ntp) { return ntp <= 16 ? 16 : 8; }
 
 // B operand (dn/64 chunks of ntp rows x 128 B), reused after the MMAs as ntp rows x 128 elements of staging
 __host__ __device__ inline int absorb_b_bytes(int dn, int ntp) {
@@ -222,7 +225,7 @@ struct alignas(16) ProjLists {   // size a multiple of 16: the float4 scratch an
 };
 
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(32 * kProjWarps)
 project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
                      const float* __restrict__ rec_o, float* __restrict__ out, int ntp, uint32_t tmem_cols) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -233,8 +236,9 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
     const uint32_t b_u32 = a_u32 + nk * dv * 128;             // nk x (ntp rows x 128 B)
     unsigned char* tail = smem + nk * dv * 128 + nk * ntp * 128;
     ProjLists* L = reinterpret_cast<ProjLists*>(tail);
-    float* red = reinterpret_cast<float*>(tail + sizeof(ProjLists));   // split sums: <= 8 x 512 floats
-    uint64_t* bars = reinterpret_cast<uint64_t*>(tail + sizeof(ProjLists) + kRedFloats * sizeof(float));
+    float* red = reinterpret_cast<float*>(tail + sizeof(ProjLists));   // split sums: proj_red_rows(ntp) x d_c
+    uint64_t* bars = reinterpret_cast<uint64_t*>(tail + sizeof(ProjLists) +
+                                                 static_cast<size_t>(proj_red_rows(ntp)) * dc * sizeof(float));
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
     const uint32_t a_full = smem_u32(&bars[0]), mma_done = smem_u32(&bars[1]);
 
@@ -272,7 +276,7 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
     } else {
         // ---- record lists: token t's group row is merged from the workers w0 .. w0 + cnt - 1 of its tiles
         const int ntiles = total_tiles(P);
-        for (int t = warp; t < ntok; t += 8) {
+        for (int t = warp; t < ntok; t += kProjWarps) {
             const int b = b0 + t;
             int g, r;
             if (P.shared) {
@@ -299,7 +303,7 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
         __syncthreads();
         // every worker owns at least one tile unless there are fewer tiles than workers
         const bool all_workers_busy = ntiles >= P.W;
-        for (int t = warp; t < ntok; t += 8) {
+        for (int t = warp; t < ntok; t += kProjWarps) {
             const int n = L->cnt[t], w0 = L->w0[t], row0 = L->g[t] * kGroupRows + L->r[t];
             float M = -INFINITY, Ls = 0.f;
             float2 ml[4];
@@ -329,12 +333,13 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
         }
         __syncthreads();
         // ---- merge into the B operand (fp32 sums, rounded once to T).
-        // Warp job = (token t, record split s): the warp adds records s, s + S, ... of token t,
-        // lane l holding float4 units l, l + 32, l + 64, l + 96 of the d_c row; four records are
-        // loaded before any is accumulated. With fewer than 8 tokens the records of a token are
-        // split over S = 8 / ntok warps and the splits are summed through shared memory.
+        // Job p = (token p % ntok, record split p / ntok): the records s, s + S, ... of the token,
+        // lane l holding float4 units l, l + 32, l + 64, l + 96 of the d_c row. A warp carries two
+        // jobs at once and loads two records of each before accumulating, so up to four 2 KB rows
+        // per warp (128 KB per CTA) are in flight. With few tokens the records of a token are split
+        // over S warps and the splits are summed through shared memory.
         const int U = dc / 4;                                  // float4 units per row, <= 128
-        int S = 8 / ntok;
+        int S = proj_red_rows(ntp) / ntok;
         S = S < 1 ? 1 : S;
         auto store_b = [&](int t, int u, float4 v) {
             const int c = 4 * u;
@@ -343,50 +348,84 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
             st_shared_v2(dst, pack_pair<T>(v.x, v.y), pack_pair<T>(v.z, v.w));
         };
         const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int p = warp; p < ntok * S; p += 8) {
-            const int t = p % ntok, s = p / ntok;
-            const int n = L->cnt[t], w0 = L->w0[t], row0 = L->g[t] * kGroupRows + L->r[t];
-            const float M = L->M[t], inv = L->inv[t];
-            const uint32_t* vmask = L->valid[t];
-            float4 acc[4] = {zero4, zero4, zero4, zero4};
-            for (int k = s; k < n; k += 4 * S) {
-                float wq[4];
-                long long rq[4];
-                bool vq[4];
+        const int njobs = ntok * S;
+        for (int p0 = warp; p0 < njobs; p0 += 2 * kProjWarps) {
+            int tj[2], sj[2], nj[2], w0j[2], row0j[2];
+            float Mj[2], invj[2];
+            const uint32_t* vmask[2];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    // record k of the token: row (g + w0 + k) * 128 + r, weight 2^(m_k - M) / sum; an empty
-                    // worker's record is never read (weight 0, load skipped)
-                    const int kk = k + q * S;
-                    rq[q] = static_cast<long long>(row0 + (w0 + kk) * kGroupRows);
-                    vq[q] = kk < n && ((vmask[kk >> 5] >> (kk & 31)) & 1u);
-                    wq[q] = vq[q] ? exp2f(rec_ml[rq[q] * 2] - M) * inv : 0.f;
-                }
-                float4 v[4][4];
+            for (int j = 0; j < 2; ++j) {
+                const int p = p0 + j * kProjWarps;
+                const bool on = p < njobs;
+                tj[j] = on ? p % ntok : 0;
+                sj[j] = on ? p / ntok : 0;
+                nj[j] = on ? L->cnt[tj[j]] : 0;
+                w0j[j] = L->w0[tj[j]];
+                row0j[j] = L->g[tj[j]] * kGroupRows + L->r[tj[j]];
+                Mj[j] = L->M[tj[j]];
+                invj[j] = L->inv[tj[j]];
+                vmask[j] = L->valid[tj[j]];
+            }
+            float4 acc[2][4];
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
+            for (int j = 0; j < 2; ++j)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int u = lane + 32 * j;
-                        v[q][j] = (vq[q] && u < U) ? __ldg(reinterpret_cast<const float4*>(rec_o + rq[q] * dc) + u)
-                                                   : zero4;
+                for (int u = 0; u < 4; ++u) acc[j][u] = zero4;
+            for (int i = 0;; i += 2) {
+                bool more = false;
+                long long rq[2][2];
+                bool vq[2][2];
+#pragma unroll
+                for (int j = 0; j < 2; ++j)
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        // record k of the token: row (g + w0 + k) * 128 + r; an empty worker's record
+                        // is never read (weight 0, load skipped)
+                        const int kk = sj[j] + (i + q) * S;
+                        more |= kk < nj[j];
+                        rq[j][q] = static_cast<long long>(row0j[j] + (w0j[j] + kk) * kGroupRows);
+                        vq[j][q] = kk < nj[j] && ((vmask[j][kk >> 5] >> (kk & 31)) & 1u);
+                    }
+                if (!more) break;
+                float mq[2][2];
+                float4 v[2][2][4];
+#pragma unroll
+                for (int j = 0; j < 2; ++j)
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        mq[j][q] = vq[j][q] ? __ldg(rec_ml + rq[j][q] * 2) : 0.f;
+#pragma unroll
+                        for (int u4 = 0; u4 < 4; ++u4) {
+                            const int u = lane + 32 * u4;
+                            v[j][q][u4] = (vq[j][q] && u < U)
+                                              ? __ldg(reinterpret_cast<const float4*>(rec_o + rq[j][q] * dc) + u)
+                                              : zero4;
+                        }
                     }
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
+                for (int j = 0; j < 2; ++j)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        acc[j].x = fmaf(wq[q], v[q][j].x, acc[j].x);
-                        acc[j].y = fmaf(wq[q], v[q][j].y, acc[j].y);
-                        acc[j].z = fmaf(wq[q], v[q][j].z, acc[j].z);
-                        acc[j].w = fmaf(wq[q], v[q][j].w, acc[j].w);
+                    for (int q = 0; q < 2; ++q) {
+                        const float w = vq[j][q] ? exp2f(mq[j][q] - Mj[j]) * invj[j] : 0.f;
+#pragma unroll
+                        for (int u4 = 0; u4 < 4; ++u4) {
+                            acc[j][u4].x = fmaf(w, v[j][q][u4].x, acc[j][u4].x);
+                            acc[j][u4].y = fmaf(w, v[j][q][u4].y, acc[j][u4].y);
+                            acc[j][u4].z = fmaf(w, v[j][q][u4].z, acc[j][u4].z);
+                            acc[j][u4].w = fmaf(w, v[j][q][u4].w, acc[j][u4].w);
+                        }
                     }
             }
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int u = lane + 32 * j;
-                if (u < U) {
-                    if (S == 1) store_b(t, u, acc[j]);
-                    else reinterpret_cast<float4*>(red)[(s * ntok + t) * U + u] = acc[j];
+            for (int j = 0; j < 2; ++j) {
+                if (p0 + j * kProjWarps >= njobs) continue;
+#pragma unroll
+                for (int u4 = 0; u4 < 4; ++u4) {
+                    const int u = lane + 32 * u4;
+                    if (u < U) {
+                        if (S == 1) store_b(tj[j], u, acc[j][u4]);
+                        else reinterpret_cast<float4*>(red)[(sj[j] * ntok + tj[j]) * U + u] = acc[j][u4];
+                    }
                 }
             }
         }
@@ -422,7 +461,8 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
         }
         mma_commit(mma_done);
     }
-    if (warp >= 4 && !failed) {
+    if (warp >= 4 && warp < 8 && !failed) {
+        // warps 4-7: warp w reads TMEM lanes 32 (w - 4) .. + 31, i.e. output columns j < dv = 128
         bool ok = mbar_wait(mma_done, 0, err, gcode(kSiteProjMma)) && *err == 0;
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
@@ -517,11 +557,11 @@ cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const
     const int ntp = pad16(P.B < kProjTok ? P.B : kProjTok);
     const int nk = P.dc / 64;
     const size_t smem = 1024 + static_cast<size_t>(nk) * P.dv * 128 + static_cast<size_t>(nk) * ntp * 128 +
-                        sizeof(ProjLists) + kRedFloats * sizeof(float) + 64;
+                        sizeof(ProjLists) + static_cast<size_t>(proj_red_rows(ntp)) * P.dc * sizeof(float) + 64;
     cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(project_sm100_kernel<T>), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     dim3 grid(ceil_div(P.B, kProjTok), P.H);
-    e = launch_ex(project_sm100_kernel<T>, grid, dim3(256), smem, s, pdl, tmap, P, rec_ml, rec_o, out, ntp,
+    e = launch_ex(project_sm100_kernel<T>, grid, dim3(32 * kProjWarps), smem, s, pdl, tmap, P, rec_ml, rec_o, out, ntp,
                   tmem_cols_for(ntp));
     count_launches(1);
     return e != cudaSuccess ? e : cudaGetLastError();
