@@ -101,6 +101,12 @@ __device__ __forceinline__ long long wait_budget_cycles(uint64_t timeout_ns) {
     return static_cast<long long>(2 * timeout_ns);
 }
 
+// The timeout record, out of line: it runs only on failure, and every wait site would
+// otherwise carry its own copy in the instruction stream.
+static __device__ __noinline__ void record_timeout(volatile int* err, int code) {
+    atomicCAS(const_cast<int*>(err), 0, code);
+}
+
 template <bool kCluster, bool kPollErr>
 __device__ __forceinline__ bool mbar_wait_impl(uint32_t bar, uint32_t parity, volatile int* err, int code,
                                                uint64_t timeout_ns) {
@@ -115,7 +121,7 @@ __device__ __forceinline__ bool mbar_wait_impl(uint32_t bar, uint32_t parity, vo
             if (dt > budget) break;
         }
     }
-    atomicCAS(const_cast<int*>(err), 0, code);
+    record_timeout(err, code);
     return false;
 }
 
