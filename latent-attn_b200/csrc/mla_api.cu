@@ -83,6 +83,15 @@ int env_path_override() {
     return v;
 }
 
+// LATENT_ATTN_B200_WORKERS = n caps the split-KV worker count (0 / unset: the planner's choice).
+int env_workers() {
+    static int v = [] {
+        const char* s = std::getenv("LATENT_ATTN_B200_WORKERS");
+        return s ? std::atoi(s) : 0;
+    }();
+    return v;
+}
+
 bool env_gemm_enabled() {
     static bool v = [] {
         const char* s = std::getenv("LATENT_ATTN_B200_GEMM");
@@ -205,6 +214,7 @@ mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan
     int cap = use_tc ? di.sms / 2 : 64;
     if (cap > 128) cap = 128;  // the combine kernel merges at most 128 records per row
     if (max_workers > 0 && cap > max_workers) cap = max_workers;
+    if (env_workers() > 0 && cap > env_workers()) cap = env_workers();
     if (cap < 1) cap = 1;
     int W = cap;
     if (T >= 0 && T < W) W = T > 0 ? static_cast<int>(T) : 1;
