@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the decode kernel uses:
-// mbarriers, TMA tiled loads (no multicast), tcgen05 MMA / TMEM, cluster shared
+// mbarriers, TMA tiled loads into this CTA only, tcgen05 MMA / TMEM, cluster shared
 // memory (mapa, st.async, remote mbarrier arrive).
 //
 // Descriptor encodings (PTX ISA, tcgen05 "matrix descriptors"):
