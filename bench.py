@@ -22,9 +22,10 @@ reported as ms_per_step / us_per_step. L2 is flushed (256 MiB write) before
 every timed step because the config-1 inputs fit in the 126 MB L2.
 
 Device-timed leg: each timed step is one replay of a CUDA graph captured from the
-public call (latent_attn.functional.mla_decode), so the events bracket the step's
-kernels rather than the host's time to enqueue them (--eager launches it directly).
-The multi-GPU KV-range step holds an NCCL collective and always runs eagerly.
+public call (latent_attn.functional.mla_decode, or the KV-range decoder with its
+NCCL all-gather on several GPUs), so the events bracket the step's kernels rather
+than the host's time to enqueue them (--eager launches it directly). Graphs that
+hold NCCL calls are released before the process group is destroyed.
 The end-to-end leg calls the public API every step, with the host copies inside.
 """
 
@@ -208,7 +209,16 @@ def cpu_oracle_rate(lens, seconds, H=128):
 
 # ----------------------------------------------------------------------------- reference arm
 
-def run_reference(args, rank):
+def json_stdout():
+    """The real stdout, kept for the one JSON line; file descriptor 1 then goes to stderr, so whatever
+    else libraries print there (NCCL's version banner on rank 0, for one) cannot add lines to it."""
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    return out
+
+
+def run_reference(args, rank, out):
     if rank != 0:
         return
     spec = workload_spec(args.workload)
@@ -223,18 +233,19 @@ def run_reference(args, rank):
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "ms_per_step": round(spec["lens"][0] * CACHE_ROW_BYTES / gbs / 1e6, 4),
     }
-    print(json.dumps(line), flush=True)
+    print(json.dumps(line), file=out, flush=True)
 
 
 # ----------------------------------------------------------------------------- main arm
 
 def main():
+    out = json_stdout()
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, out)
         return
 
     import torch
@@ -337,17 +348,16 @@ def main():
     status_word = ws[:4].view(torch.int32)
     status_sum = torch.zeros(1, dtype=torch.int32, device=dev)
     host_s = 0.0
-    use_graphs = not args.eager and not (spec["sharding"] == "kv-range" and world > 1)
+    use_graphs = not args.eager
     graphs = []
     if use_graphs:
         # one graph per timed step, each with its own decode-kernel timer
         launches0 = _lib.kernel_launch_count()
         side = torch.cuda.Stream(dev)
         for k in range(args.steps):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=side):
+            graphs.append(torch.cuda.CUDAGraph())
+            with torch.cuda.graph(graphs[-1], stream=side):
                 step(t=timers[k])
-            graphs.append(g)
         per_step = (_lib.kernel_launch_count() - launches0) / args.steps
         for g in graphs[:3]:
             g.replay()
@@ -371,6 +381,11 @@ def main():
     launches = _lib.kernel_launch_count() - launches0
     if use_graphs:
         launches = int(round(per_step * args.steps))  # the graphs' kernels, counted when captured
+    # before any process-group teardown: a graph that holds NCCL calls keeps the teardown waiting
+    for gr in graphs:
+        gr.reset()
+    graphs.clear()
+    torch.cuda.synchronize(dev)
     step_ms = [a.elapsed_time(b) for a, b in zip(ev0, ev1)]
     dec_ms = [t.decode_ms() for t in timers]
     for t in timers:
@@ -455,7 +470,7 @@ def main():
             "output_finite": bool(torch.isfinite(out).all()),
             "clocks": clock_info,
         }
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=out, flush=True)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()

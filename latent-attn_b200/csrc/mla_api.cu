@@ -243,6 +243,17 @@ mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan
     return MLA_OK;
 }
 
+// Timer event record. Under stream capture it must be an external record, which becomes a
+// graph node that fires on every replay (a plain record would only express a dependency);
+// outside capture the external flag is not accepted, so a plain record is used.
+cudaError_t timer_record(cudaEvent_t ev, cudaStream_t s) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(s, &cs);
+    if (e != cudaSuccess) return e;
+    return cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal)
+                                               : cudaEventRecord(ev, s);
+}
+
 template <typename T>
 mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned char* ws, float* out,
                         float* part_ml, float* part_o, cudaStream_t s) {
@@ -269,9 +280,7 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
     }
     const T* kv = reinterpret_cast<const T*>(a->kv_cache);
     if (a->timer) {
-        // External: under stream capture the record becomes a graph node that fires on every
-        // replay (a plain record would only express a dependency); otherwise a normal record.
-        e = cudaEventRecordWithFlags(a->timer->begin, s, cudaEventRecordExternal);
+        e = timer_record(a->timer->begin, s);
         if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(timer)");
     }
     if (pl.use_tc)
@@ -284,7 +293,7 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
         return fail(MLA_ERR_NO_DEVICE_CODE, "decode kernel: %s (library is built for sm_100a)", cudaGetErrorString(e));
     if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
     if (a->timer) {
-        e = cudaEventRecordWithFlags(a->timer->end, s, cudaEventRecordExternal);
+        e = timer_record(a->timer->end, s);
         if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(timer)");
         a->timer->recorded = true;
     }
