@@ -20,14 +20,15 @@
 // bit-identical softmax and bit-identical P, m and l.
 //
 // Warp roles (384 threads):
-//   warp 0      TMA producer (one lane): per tile, 4 latent chunks (128-byte swizzle),
-//               4 rope boxes of 8 columns (no swizzle) and the 16 frequencies' cos/sin
-//               rows of the caller's tables, into a 4-stage ring
-//   warp 1      TMEM allocator + MMA issuer (one lane): issues each tile's score and PV
-//               MMAs as soon as their inputs are ready, in tile order per kind
+//   warp 0      TMA producer (one lane): per tile, 4 latent chunks (128-byte swizzle) and
+//               4 rope boxes of 8 columns (no swizzle), into a 5-stage ring
+//   warp 1      TMEM allocator + MMA issuer (one lane): issues each tile's score (latent
+//               part on arrival, rope part after the transform) and PV MMAs as soon as
+//               their inputs are ready, in tile order per kind
 //   warps 2-3   tile transform: zero rows past the sequence end, rotate the CTA's
-//               k_rope pairs in place with the tables (the rotation of
-//               src/fused_mla.cu:34-54 of the reference)
+//               k_rope pairs in place with the caller's cos/sin tables, read from global
+//               memory one tile ahead (the rotation of src/fused_mla.cu:34-54 of the
+//               reference)
 //   warps 4-7   softmax set 0: the even tiles of the worker
 //   warps 8-11  softmax set 1: the odd tiles (thread = query row = TMEM lane)
 // The two softmax sets work on consecutive tiles at the same time: while one waits
