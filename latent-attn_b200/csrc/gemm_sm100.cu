@@ -77,6 +77,7 @@ __host__ __device__ inline int absorb_b_bytes(int dn, int ntp) {
 }
 
 enum : int { kSiteAbsorbA = 12, kSiteAbsorbMma = 13, kSiteProjA = 14, kSiteProjMma = 15 };
+}
 __device__ __forceinline__ int gcode(int site) { return kStatusTimeout | (site << 8); }
 
 }  // namespace
@@ -217,8 +218,9 @@ absorb_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
 // ------------------------------------------------------------------------------------------
 // Per-token merge parameters (records are read straight from global memory / L2).
 struct alignas(16) ProjLists {   // size a multiple of 16: the float4 scratch and mbarriers follow it
-    int cnt[kProjTok];           // records of token t (workers w0 .. w0 + cnt - 1)
-    int w0[kProjTok], g[kProjTok], r[kProjTok];   // first worker, group and group row of token t
+    int cnt[kProjTok];           // records of token t
+    int base[kProjTok];          // row of token t's first record; record k is at row base + k * step
+    int w0[kProjTok];            // first worker of token t (records of the decode kernel)
     float M[kProjTok];           // max of the records' m (log2 units)
     float inv[kProjTok];         // 1 / sum_k l_k 2^(m_k - M)
     uint32_t valid[kProjTok][4]; // bit k: worker w0 + k owns tiles (an empty worker wrote no record); W <= 128
@@ -227,7 +229,11 @@ struct alignas(16) ProjLists {   // size a multiple of 16: the float4 scratch an
 template <typename T>
 __global__ void __launch_bounds__(32 * kProjWarps)
 project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
-                     const float* __restrict__ rec_o, float* __restrict__ out, int ntp, uint32_t tmem_cols) {
+                     const float* __restrict__ rec_o, float* __restrict__ out, int ntp, uint32_t tmem_cols,
+                     int parts) {
+    // parts == 0: the decode kernel's partial records (m in log2 units, record g + w of group g).
+    // parts > 0: that many partial sets in the layout of mla_decode_partial, [part][B][H] rows with
+    // m in natural-log units and l = 0 for an empty part (the KV-range shards' merge).
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int dc = P.dc, dv = P.dv;
@@ -267,7 +273,9 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
         for (int j = 0; j < nk; ++j) tma_load_2d(a_u32 + j * dv * 128, &tmap_w, a_full, 64 * j, h * dv);
     }
     pdl_wait();  // records and status come from the decode kernel
-    const bool failed = *err != kStatusOk;
+    const bool failed = parts == 0 && *err != kStatusOk;
+    const int step = parts ? P.B * P.H : kGroupRows;          // rows between a token's consecutive records
+    const float mscale = parts ? 1.4426950408889634f : 1.f;   // m in log2 units
     if (failed) {
         // the decode kernel gave up on a wait: make the failure visible in the output
         const float nan = __int_as_float(0x7fc00000);
@@ -275,48 +283,55 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
             out[(static_cast<long long>(b0 + i / dv) * P.H + h) * dv + i % dv] = nan;
     } else {
         // ---- record lists: token t's group row is merged from the workers w0 .. w0 + cnt - 1 of its tiles
-        const int ntiles = total_tiles(P);
+        const int ntiles = parts ? 0 : total_tiles(P);
         for (int t = warp; t < ntok; t += kProjWarps) {
             const int b = b0 + t;
-            int g, r;
-            if (P.shared) {
-                const int f = b * P.H + h;
-                g = f / kGroupRows;
-                r = f % kGroupRows;
-            } else {
-                g = b * P.head_blocks + h / kGroupRows;
-                r = h % kGroupRows;
-            }
-            const int gt0 = tile_prefix(P, g), gt1 = tile_prefix(P, g + 1);
-            int n = 0, w0 = 0;
-            if (gt1 > gt0 && ntiles > 0) {
-                w0 = worker_of_tile(ntiles, P.W, gt0);
-                n = worker_of_tile(ntiles, P.W, gt1 - 1) - w0 + 1;
+            int n = parts, w0 = 0, base = b * P.H + h;
+            if (!parts) {
+                int g, r;
+                if (P.shared) {
+                    const int f = b * P.H + h;
+                    g = f / kGroupRows;
+                    r = f % kGroupRows;
+                } else {
+                    g = b * P.head_blocks + h / kGroupRows;
+                    r = h % kGroupRows;
+                }
+                const int gt0 = tile_prefix(P, g), gt1 = tile_prefix(P, g + 1);
+                n = 0;
+                if (gt1 > gt0 && ntiles > 0) {
+                    w0 = worker_of_tile(ntiles, P.W, gt0);
+                    n = worker_of_tile(ntiles, P.W, gt1 - 1) - w0 + 1;
+                }
+                base = (g + w0) * kGroupRows + r;
             }
             if (lane == 0) {
                 L->cnt[t] = n;
                 L->w0[t] = w0;
-                L->g[t] = g;
-                L->r[t] = r;
+                L->base[t] = base;
             }
         }
         __syncthreads();
         // every worker owns at least one tile unless there are fewer tiles than workers
         const bool all_workers_busy = ntiles >= P.W;
         for (int t = warp; t < ntok; t += kProjWarps) {
-            const int n = L->cnt[t], w0 = L->w0[t], row0 = L->g[t] * kGroupRows + L->r[t];
+            const int n = L->cnt[t], w0 = L->w0[t], base = L->base[t];
             float M = -INFINITY, Ls = 0.f;
             float2 ml[4];
             bool valid[4];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {  // lane handles records k = lane + 32 c (n <= W <= 128)
+            for (int c = 0; c < 4; ++c) {  // lane handles records k = lane + 32 c (n <= 128)
                 const int k = lane + 32 * c, w = w0 + k;
-                valid[c] = k < n && (all_workers_busy ||
-                                     worker_begin(ntiles, P.W, w) != worker_begin(ntiles, P.W, w + 1));
+                // a record of the decode kernel exists unless its worker owns no tile; a partial set
+                // contributes unless its l is 0
+                const bool in = k < n && (parts || all_workers_busy ||
+                                          worker_begin(ntiles, P.W, w) != worker_begin(ntiles, P.W, w + 1));
+                ml[c] = in ? *reinterpret_cast<const float2*>(rec_ml + (static_cast<long long>(base) + static_cast<long long>(k) * step) * 2)
+                           : make_float2(-INFINITY, 0.f);
+                valid[c] = in && (!parts || ml[c].y > 0.f);
+                ml[c] = valid[c] ? make_float2(ml[c].x * mscale, ml[c].y) : make_float2(-INFINITY, 0.f);
                 const uint32_t mask = __ballot_sync(0xffffffffu, valid[c]);
                 if (lane == 0) L->valid[t][c] = mask;
-                ml[c] = valid[c] ? *reinterpret_cast<const float2*>(rec_ml + static_cast<long long>(row0 + w * kGroupRows) * 2)
-                                 : make_float2(-INFINITY, 0.f);
                 M = fmaxf(M, ml[c].x);
             }
 #pragma unroll
@@ -350,7 +365,7 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
         const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
         const int njobs = ntok * S;
         for (int p0 = warp; p0 < njobs; p0 += 2 * kProjWarps) {
-            int tj[2], sj[2], nj[2], w0j[2], row0j[2];
+            int tj[2], sj[2], nj[2], basej[2];
             float Mj[2], invj[2];
             const uint32_t* vmask[2];
 #pragma unroll
@@ -360,8 +375,7 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                 tj[j] = on ? p % ntok : 0;
                 sj[j] = on ? p / ntok : 0;
                 nj[j] = on ? L->cnt[tj[j]] : 0;
-                w0j[j] = L->w0[tj[j]];
-                row0j[j] = L->g[tj[j]] * kGroupRows + L->r[tj[j]];
+                basej[j] = L->base[tj[j]];
                 Mj[j] = L->M[tj[j]];
                 invj[j] = L->inv[tj[j]];
                 vmask[j] = L->valid[tj[j]];
@@ -379,11 +393,11 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                 for (int j = 0; j < 2; ++j)
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
-                        // record k of the token: row (g + w0 + k) * 128 + r; an empty worker's record
-                        // is never read (weight 0, load skipped)
+                        // record kk of the token: row base + kk * step; an empty record is never read
+                        // (weight 0, load skipped)
                         const int kk = sj[j] + (i + q) * S;
                         more |= kk < nj[j];
-                        rq[j][q] = static_cast<long long>(row0j[j] + (w0j[j] + kk) * kGroupRows);
+                        rq[j][q] = static_cast<long long>(basej[j]) + static_cast<long long>(kk) * step;
                         vq[j][q] = kk < nj[j] && ((vmask[j][kk >> 5] >> (kk & 31)) & 1u);
                     }
                 if (!more) break;
@@ -393,7 +407,7 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                 for (int j = 0; j < 2; ++j)
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
-                        mq[j][q] = vq[j][q] ? __ldg(rec_ml + rq[j][q] * 2) : 0.f;
+                        mq[j][q] = vq[j][q] ? __ldg(rec_ml + rq[j][q] * 2) * mscale : 0.f;
 #pragma unroll
                         for (int u4 = 0; u4 < 4; ++u4) {
                             const int u = lane + 32 * u4;
@@ -479,6 +493,11 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                     if (n < ntok) out[(static_cast<long long>(b0 + n) * P.H + h) * dv + j] = __uint_as_float(r[q]);
                 }
             }
+        } else {
+            // a wait gave up (the status word holds where): the output shows it
+            const int j = 32 * (warp - 4) + lane;
+            for (int n = 0; n < ntok; ++n)
+                out[(static_cast<long long>(b0 + n) * P.H + h) * dv + j] = __int_as_float(0x7fc00000);
         }
     }
     tc_fence_before();
@@ -547,9 +566,8 @@ cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const 
 }
 
 template <typename T>
-cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
-                                 float* out, bool pdl, cudaStream_t s) {
-    if (!project_sm100_supported(P)) return cudaErrorInvalidValue;
+cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
+                                float* out, bool pdl, int parts, cudaStream_t s) {
     CUtensorMap tmap;
     if (!make_tmap_2d_16b(&tmap, W_UV, static_cast<uint64_t>(P.H) * P.dv, static_cast<uint64_t>(P.dc),
                           static_cast<uint64_t>(P.dc), static_cast<uint32_t>(P.dv), 64))
@@ -562,16 +580,64 @@ cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const
     if (e != cudaSuccess) return e;
     dim3 grid(ceil_div(P.B, kProjTok), P.H);
     e = launch_ex(project_sm100_kernel<T>, grid, dim3(32 * kProjWarps), smem, s, pdl, tmap, P, rec_ml, rec_o, out, ntp,
-                  tmem_cols_for(ntp));
+                  tmem_cols_for(ntp), parts);
     count_launches(1);
     return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
+                                 float* out, bool pdl, cudaStream_t s) {
+    if (!project_sm100_supported(P)) return cudaErrorInvalidValue;
+    return launch_project_impl<T>(P, rec_ml, rec_o, W_UV, out, pdl, 0, s);
+}
+
+// Status word of the partial-set merge: that path has no decode status to check, but the
+// kernel's bounded waits need somewhere to record a timeout. Never read.
+static __device__ int g_parts_status;
+
+bool project_parts_sm100_supported(int H, int dc, int dv, int parts) {
+    return dv == 128 && dc % 64 == 0 && dc <= 512 && parts >= 1 && parts <= 128 && H >= 1;
+}
+
+template <typename T>
+cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, const float* part_ml,
+                                       const float* part_o, const T* W_UV, float* out, cudaStream_t s) {
+    if (!project_parts_sm100_supported(H, dc, dv, parts)) return cudaErrorInvalidValue;
+    static std::mutex mu;
+    static std::vector<int*> status_addr;  // per device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    int* status = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (static_cast<int>(status_addr.size()) <= dev) status_addr.resize(dev + 1, nullptr);
+        if (!status_addr[dev]) {
+            void* a = nullptr;
+            e = cudaGetSymbolAddress(&a, g_parts_status);
+            if (e != cudaSuccess) return e;
+            status_addr[dev] = static_cast<int*>(a);
+        }
+        status = status_addr[dev];
+    }
+    DecodePlan P{};
+    P.dc = dc;
+    P.dv = dv;
+    P.H = H;
+    P.B = B;
+    P.head_blocks = ceil_div(H, kGroupRows);
+    P.status = status;
+    return launch_project_impl<T>(P, part_ml, part_o, W_UV, out, false, parts, s);
 }
 
 #define MLA_INST(T)                                                                                              \
     template cudaError_t launch_absorb_sm100<T>(const DecodePlan&, const float*, const T*, const float*, float, T*, \
                                                 int*, cudaStream_t);                                             \
     template cudaError_t launch_project_sm100<T>(const DecodePlan&, const float*, const float*, const T*, float*,   \
-                                                 bool, cudaStream_t);
+                                                 bool, cudaStream_t);                                             \
+    template cudaError_t launch_project_parts_sm100<T>(int, int, int, int, int, const float*, const float*, const T*, \
+                                                       float*, cudaStream_t);
 MLA_INST(__half)
 MLA_INST(__nv_bfloat16)
 #undef MLA_INST

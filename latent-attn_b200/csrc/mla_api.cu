@@ -405,9 +405,24 @@ mla_status_t mla_combine_partials(const mla_config_t* cfg, mla_dtype_t dtype, in
     if (!partial_ml || !partial_o || !W_UV || !output) return fail(MLA_ERR_INVALID_ARGUMENT, "null pointer");
     if (cfg->kv_lora_rank > 1024 || cfg->v_head_dim > 256)
         return fail(MLA_ERR_UNSUPPORTED, "kv_lora_rank <= 1024 and v_head_dim <= 256 required");
+    if (dtype != MLA_DTYPE_BF16 && dtype != MLA_DTYPE_F16) return fail(MLA_ERR_UNSUPPORTED, "dtype must be F16 or BF16");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    DeviceInfo di;
+    if (!device_info(&di)) return fail(MLA_ERR_CUDA, "no CUDA device");
+    // tcgen05 merge + W_UV GEMM when the shape fits, else the CUDA-core combine
+    const bool gemm = di.major == 10 && env_gemm_enabled() &&
+                      mla::project_parts_sm100_supported(cfg->num_heads, cfg->kv_lora_rank, cfg->v_head_dim,
+                                                         num_parts);
     cudaError_t e;
-    if (dtype == MLA_DTYPE_BF16)
+    if (gemm && dtype == MLA_DTYPE_BF16)
+        e = mla::launch_project_parts_sm100<__nv_bfloat16>(batch, cfg->num_heads, cfg->kv_lora_rank,
+                                                          cfg->v_head_dim, num_parts, partial_ml, partial_o,
+                                                          static_cast<const __nv_bfloat16*>(W_UV), output, s);
+    else if (gemm)
+        e = mla::launch_project_parts_sm100<__half>(batch, cfg->num_heads, cfg->kv_lora_rank, cfg->v_head_dim,
+                                                   num_parts, partial_ml, partial_o,
+                                                   static_cast<const __half*>(W_UV), output, s);
+    else if (dtype == MLA_DTYPE_BF16)
         e = mla::launch_combine_parts<__nv_bfloat16>(batch, cfg->num_heads, cfg->kv_lora_rank, cfg->v_head_dim,
                                                      num_parts, partial_ml, partial_o,
                                                      static_cast<const __nv_bfloat16*>(W_UV), output, s);
@@ -415,8 +430,6 @@ mla_status_t mla_combine_partials(const mla_config_t* cfg, mla_dtype_t dtype, in
         e = mla::launch_combine_parts<__half>(batch, cfg->num_heads, cfg->kv_lora_rank, cfg->v_head_dim,
                                               num_parts, partial_ml, partial_o,
                                               static_cast<const __half*>(W_UV), output, s);
-    else
-        return fail(MLA_ERR_UNSUPPORTED, "dtype must be F16 or BF16");
     if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
     return MLA_OK;
 }

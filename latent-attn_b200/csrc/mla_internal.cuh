@@ -194,6 +194,12 @@ cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const 
 template <typename T>
 cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
                                  float* out, bool pdl, cudaStream_t s);
+// merge of gathered partial sets part_ml[parts][B][H][2] (natural-log max, sum; sum 0 = empty)
+// and part_o[parts][B][H][dc], followed by the W_UV projection
+bool project_parts_sm100_supported(int H, int dc, int dv, int parts);
+template <typename T>
+cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, const float* part_ml,
+                                       const float* part_o, const T* W_UV, float* out, cudaStream_t s);
 // decode_simt.cu
 template <typename T>
 cudaError_t launch_decode_simt(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,

@@ -259,6 +259,34 @@ def test_kv_range_shards_combine():
     assert_close(out[0], ref, "sharded vs oracle")
 
 
+@pytest.mark.parametrize("parts,B", [(1, 3), (40, 5), (128, 70)])
+def test_combine_partials_many_parts_with_empty(parts, B):
+    """mla_combine_partials on synthetic partial sets: natural-log maxima spread over a wide
+    range, every third part empty (l = 0, o = 0), more than one block of tokens; checked
+    against the log-sum-exp merge and the W_UV projection in numpy."""
+    dev = torch.device("cuda")
+    H, dc, dv = 16, 512, 128
+    g = torch.Generator().manual_seed(parts * 131 + B)
+    m = torch.randn(parts, B, H, generator=g) * 4.0
+    l = torch.rand(parts, B, H, generator=g) * 50.0 + 0.5
+    o = torch.randn(parts, B, H, dc, generator=g) * l[..., None]   # unnormalised sums
+    if parts > 1:
+        l[::3] = 0.0
+        o[::3] = 0.0
+        m[::3] = -1e30
+    W_UV = (torch.randn(H * dv, dc, generator=g) * 0.05).to(torch.bfloat16)
+    ml = torch.stack([m, l], dim=-1).contiguous()
+    out = _C.mla_combine_partials(ml.to(dev), o.contiguous().to(dev), W_UV.to(dev), 0, dc, 128, 64, H,
+                                  dv).cpu().numpy()
+    mm = np.where(l.numpy() > 0, m.numpy(), -np.inf).astype(np.float64)
+    ll, oo = l.numpy().astype(np.float64), o.numpy().astype(np.float64)
+    W = W_UV.float().numpy().astype(np.float64).reshape(H, dv, dc)
+    for b in range(B):
+        olat = O.combine_partials(mm[:, b], ll[:, b], oo[:, b])             # (H, dc)
+        ref = np.einsum("hc,hjc->hj", olat, W)
+        assert_close(out[b], ref, f"parts={parts} b={b}")
+
+
 def test_errors_raise_runtime_error():
     dev = torch.device("cuda")
     cfg = MLAConfig.deepseek_v2()
