@@ -77,7 +77,6 @@ __host__ __device__ inline int absorb_b_bytes(int dn, int ntp) {
 }
 
 enum : int { kSiteAbsorbA = 12, kSiteAbsorbMma = 13, kSiteProjA = 14, kSiteProjMma = 15 };
-}
 __device__ __forceinline__ int gcode(int site) { return kStatusTimeout | (site << 8); }
 
 }  // namespace
