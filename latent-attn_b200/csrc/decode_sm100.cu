@@ -70,7 +70,8 @@ constexpr float kRescaleThreshold = 8.0f;           // log2 units
 
 // wait-site codes recorded in the status word's upper bits (debugging aid)
 enum : int { kWaitProducer = 1, kWaitTransform = 2, kWaitMma = 3, kWaitSoftS = 7, kWaitSoftX = 8,
-             kWaitSoftPV = 9, kWaitTeardown = 10, kWaitDrain = 11, kWaitSoftRef = 12, kWaitCredit = 13 };
+             kWaitSoftPV = 9, kWaitTeardown = 10, kWaitDrain = 11, kWaitSoftRef = 12, kWaitCredit = 13,
+             kWaitEpilogue = 14 };
 
 // Warp-uniform success: every early exit of a warp that runs warp-collective
 // instructions (tcgen05.ld/st, vote) happens with all 32 lanes together.
@@ -92,6 +93,10 @@ struct __align__(8) Barriers {
     uint64_t mref[kMSlots];           // m_pub slot j % kMSlots written (tile j's reference max)
     uint64_t lpub[4];                 // l_pub slot 2 sid + ((j >> 1) & 1) written (set sid's row sum)
     uint64_t q_ready, o_free, drain, done;
+    // the worker's last record: the set owning the last tile arrives once PV of that tile is done,
+    // and the other set, idle by then, writes half of the record's O columns
+    uint64_t epi_go;
+    int epi_rec, epi_rows;            // that record's index and valid rows
     uint32_t tmem_base;
 };
 
@@ -187,6 +192,23 @@ __device__ __forceinline__ void st_row32(float* p, const uint32_t (&v)[32]) {
                      : "memory");
 }
 
+// Writes `ncols` (a multiple of 64) fp32 columns of this thread's TMEM row to `orow` (skipped when
+// !row_ok): 32 columns at a time, the next chunk's TMEM load in flight during this chunk's stores;
+// 32-byte stores halve the store instructions of this row-per-thread layout. Warp-collective.
+__device__ __forceinline__ void write_o_cols(uint32_t tsrc, float* orow, bool row_ok, int ncols) {
+    uint32_t oa[32], ob[32];
+    tmem_ld32(tsrc, oa);
+    tmem_ld_wait();
+    for (int c0 = 0; c0 < ncols; c0 += 64) {
+        tmem_ld32(tsrc + c0 + 32, ob);
+        if (row_ok) st_row32(orow + c0, oa);
+        tmem_ld_wait();
+        if (c0 + 64 < ncols) tmem_ld32(tsrc + c0 + 64, oa);
+        if (row_ok) st_row32(orow + c0 + 32, ob);
+        tmem_ld_wait();
+    }
+}
+
 // Packed two-lane fp32 arithmetic (one instruction for both lanes on sm_100).
 __device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
     float2 d;
@@ -271,6 +293,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
         mbar_init(smem_u32(&bars->o_free), 128);
         mbar_init(smem_u32(&bars->drain), 1);
         mbar_init(smem_u32(&bars->done), 1);
+        mbar_init(smem_u32(&bars->epi_go), 128);
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -764,23 +787,20 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                 }
                 tc_fence_after();
                 const int rec = it.g + w;
-                const bool row_ok = t < group_rows(P, it.g);
-                float* orow = rec_o + (static_cast<long long>(rec) * kGroupRows + t) * 512 + 256 * rank;
-                // 32 columns at a time, the next chunk's TMEM load in flight during this chunk's
-                // stores; 32-byte stores halve the store instructions of this row-per-thread layout
-                uint32_t oa[32], ob[32];
-                tmem_ld32(trow + kColO, oa);
-                tmem_ld_wait();
-#pragma unroll
-                for (int c0 = 0; c0 < 256; c0 += 64) {
-                    tmem_ld32(trow + kColO + c0 + 32, ob);
-                    if (row_ok) st_row32(orow + c0, oa);
-                    tmem_ld_wait();
-                    if (c0 + 64 < 256) tmem_ld32(trow + kColO + c0 + 64, oa);
-                    if (row_ok) st_row32(orow + c0 + 32, ob);
-                    tmem_ld_wait();
+                const int rows = group_rows(P, it.g);
+                // the worker's last tile: the other set has no tile left and writes columns 128..255
+                const bool shared_epi = j == n - 1;
+                if (shared_epi) {
+                    if (t == 0) {
+                        bars->epi_rec = rec;
+                        bars->epi_rows = rows;
+                    }
+                    tc_fence_before();
+                    mbar_arrive(smem_u32(&bars->epi_go));
                 }
-                if (rank == 0 && row_ok)
+                write_o_cols(trow + kColO, rec_o + (static_cast<long long>(rec) * kGroupRows + t) * 512 + 256 * rank,
+                             t < rows, shared_epi ? 128 : 256);
+                if (rank == 0 && t < rows)
                     *reinterpret_cast<float2*>(rec_ml + (static_cast<long long>(rec) * kGroupRows + t) * 2) =
                         make_float2(m, l_tot);
                 tc_fence_before();
@@ -788,6 +808,18 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             }
             it.next(P);
             it.next(P);
+        }
+        if (ok && ((n - 1) & 1) != sid) {
+            // the worker's last tile is the other set's: write columns 128..255 of its record
+            const bool got = mbar_wait(smem_u32(&bars->epi_go), 0, err, code(kWaitEpilogue));
+            if (warp_ok(got)) {
+                tc_fence_after();
+                const int rec = bars->epi_rec;
+                write_o_cols(trow + kColO + 128, rec_o + (static_cast<long long>(rec) * kGroupRows + t) * 512 + 256 * rank + 128,
+                             t < bars->epi_rows, 128);
+            } else if (!got) {
+                note_fail(err, kWaitEpilogue, n - 1);
+            }
         }
     }
 

@@ -66,9 +66,11 @@ __device__ __forceinline__ long long qpack_row(const DecodePlan& P, int b, int h
 constexpr int kAbsorbTok = 256;    // tokens per absorption CTA (MMA N <= 256)
 constexpr int kProjTok = 64;       // tokens per projection CTA
 constexpr int kProjWarps = 16;     // projection CTA: 16 warps merge, warp 0 issues the MMA, warps 4-7 store
-// rows of split partial sums of the merge (S * ntok <= rows): 16 when the token operand is at most
-// 16 rows, else 8, which keeps the largest configuration inside the shared-memory limit
-__host__ __device__ constexpr int proj_red_rows(int ntp) { return ntp <= 16 ? 16 : 8; }
+// rows of split partial sums of the merge (S * ntok <= rows): 32 when the token operand is at most
+// 16 rows (32 merge jobs for the 16 warps), else 8, which keeps the largest configuration inside the
+// shared-memory limit
+__host__ __device__ constexpr int proj_red_rows(int ntp) { return ntp <= 16 ? 32 : 8; }
+constexpr int kProjRedMax = 32;    // the largest proj_red_rows
 
 // B operand (dn/64 chunks of ntp rows x 128 B), reused after the MMAs as ntp rows x 128 elements of staging
 __host__ __device__ inline int absorb_b_bytes(int dn, int ntp) {
@@ -215,14 +217,13 @@ absorb_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
 // ------------------------------------------------------------------------------------------
 // merge + projection
 // ------------------------------------------------------------------------------------------
-// Per-token merge parameters (records are read straight from global memory / L2).
+// Per-token record lists (records are read straight from global memory / L2).
 struct alignas(16) ProjLists {   // size a multiple of 16: the float4 scratch and mbarriers follow it
     int cnt[kProjTok];           // records of token t
     int base[kProjTok];          // row of token t's first record; record k is at row base + k * step
-    int w0[kProjTok];            // first worker of token t (records of the decode kernel)
-    float M[kProjTok];           // max of the records' m (log2 units)
-    float inv[kProjTok];         // 1 / sum_k l_k 2^(m_k - M)
-    uint32_t valid[kProjTok][4]; // bit k: worker w0 + k owns tiles (an empty worker wrote no record); W <= 128
+    uint32_t valid[kProjTok][4]; // bit k: record k exists (a worker that owns no tile of the group wrote none)
+    float2 split_ml[kProjRedMax];   // per (split, token) job: running max (log2 units) and row sum
+    float split_w[kProjRedMax];     // per (split, token): weight of the split's sum in the token's row
 };
 
 template <typename T>
@@ -241,7 +242,7 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
     const uint32_t b_u32 = a_u32 + nk * dv * 128;             // nk x (ntp rows x 128 B)
     unsigned char* tail = smem + nk * dv * 128 + nk * ntp * 128;
     ProjLists* L = reinterpret_cast<ProjLists*>(tail);
-    float* red = reinterpret_cast<float*>(tail + sizeof(ProjLists));   // split sums: proj_red_rows(ntp) x d_c
+    float* red = reinterpret_cast<float*>(tail + sizeof(ProjLists));   // split partial sums: proj_red_rows(ntp) x d_c
     uint64_t* bars = reinterpret_cast<uint64_t*>(tail + sizeof(ProjLists) +
                                                  static_cast<size_t>(proj_red_rows(ntp)) * dc * sizeof(float));
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
@@ -272,17 +273,18 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
         for (int j = 0; j < nk; ++j) tma_load_2d(a_u32 + j * dv * 128, &tmap_w, a_full, 64 * j, h * dv);
     }
     pdl_wait();  // records and status come from the decode kernel
-    const bool failed = parts == 0 && *err != kStatusOk;
+    // The status load is issued now (unconditionally, so nothing waits for it here) and consumed
+    // after the merge, so it overlaps the record loads; a failed decode leaves garbage in the
+    // records, which are merged but never multiplied.
+    const int status0 = *err;
     const int step = parts ? P.B * P.H : kGroupRows;          // rows between a token's consecutive records
     const float mscale = parts ? 1.4426950408889634f : 1.f;   // m in log2 units
-    if (failed) {
-        // the decode kernel gave up on a wait: make the failure visible in the output
-        const float nan = __int_as_float(0x7fc00000);
-        for (int i = threadIdx.x; i < ntok * dv; i += blockDim.x)
-            out[(static_cast<long long>(b0 + i / dv) * P.H + h) * dv + i % dv] = nan;
-    } else {
-        // ---- record lists: token t's group row is merged from the workers w0 .. w0 + cnt - 1 of its tiles
+    {
+        // ---- record lists: token t's group row is merged from the workers w0 .. w0 + cnt - 1 of its
+        // tiles (decode records) or from all parts
         const int ntiles = parts ? 0 : total_tiles(P);
+        // every worker owns at least one tile unless there are fewer tiles than workers
+        const bool all_workers_busy = ntiles >= P.W;
         for (int t = warp; t < ntok; t += kProjWarps) {
             const int b = b0 + t;
             int n = parts, w0 = 0, base = b * P.H + h;
@@ -304,54 +306,27 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                 }
                 base = (g + w0) * kGroupRows + r;
             }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {  // lane handles records k = lane + 32 c (n <= 128)
+                const int k = lane + 32 * c, w = w0 + k;
+                const bool in = k < n && (parts || all_workers_busy ||
+                                          worker_begin(ntiles, P.W, w) != worker_begin(ntiles, P.W, w + 1));
+                const uint32_t mask = __ballot_sync(0xffffffffu, in);
+                if (lane == 0) L->valid[t][c] = mask;
+            }
             if (lane == 0) {
                 L->cnt[t] = n;
-                L->w0[t] = w0;
                 L->base[t] = base;
             }
         }
         __syncthreads();
-        // every worker owns at least one tile unless there are fewer tiles than workers
-        const bool all_workers_busy = ntiles >= P.W;
-        for (int t = warp; t < ntok; t += kProjWarps) {
-            const int n = L->cnt[t], w0 = L->w0[t], base = L->base[t];
-            float M = -INFINITY, Ls = 0.f;
-            float2 ml[4];
-            bool valid[4];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {  // lane handles records k = lane + 32 c (n <= 128)
-                const int k = lane + 32 * c, w = w0 + k;
-                // a record of the decode kernel exists unless its worker owns no tile; a partial set
-                // contributes unless its l is 0
-                const bool in = k < n && (parts || all_workers_busy ||
-                                          worker_begin(ntiles, P.W, w) != worker_begin(ntiles, P.W, w + 1));
-                ml[c] = in ? *reinterpret_cast<const float2*>(rec_ml + (static_cast<long long>(base) + static_cast<long long>(k) * step) * 2)
-                           : make_float2(-INFINITY, 0.f);
-                valid[c] = in && (!parts || ml[c].y > 0.f);
-                ml[c] = valid[c] ? make_float2(ml[c].x * mscale, ml[c].y) : make_float2(-INFINITY, 0.f);
-                const uint32_t mask = __ballot_sync(0xffffffffu, valid[c]);
-                if (lane == 0) L->valid[t][c] = mask;
-                M = fmaxf(M, ml[c].x);
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-                if (valid[c]) Ls += exp2f(ml[c].x - M) * ml[c].y;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, o);
-            if (lane == 0) {
-                L->M[t] = M;
-                L->inv[t] = Ls > 0.f ? 1.f / Ls : 0.f;
-            }
-        }
-        __syncthreads();
         // ---- merge into the B operand (fp32 sums, rounded once to T).
-        // Job p = (token p % ntok, record split p / ntok): the records s, s + S, ... of the token,
-        // lane l holding float4 units l, l + 32, l + 64, l + 96 of the d_c row. A warp carries two
-        // jobs at once and loads two records of each before accumulating, so up to four 2 KB rows
-        // per warp (128 KB per CTA) are in flight. With few tokens the records of a token are split
-        // over S warps and the splits are summed through shared memory.
+        // Job p = (token p % ntok, record split p / ntok) takes the records s, s + S, ... of the token,
+        // lane l holding float4 units l, l + 32, l + 64, l + 96 of the d_c row. A warp carries two jobs
+        // at once and loads the (m, l) pair and the o row of two records of each in one round trip,
+        // folding them into a running log-sum-exp (max, row sum, rescaled o sum). With few tokens the
+        // records of a token are split over S jobs (32 jobs in all), whose partial sums are rescaled
+        // to the common max and added through shared memory.
         const int U = dc / 4;                                  // float4 units per row, <= 128
         int S = proj_red_rows(ntp) / ntok;
         S = S < 1 ? 1 : S;
@@ -365,7 +340,6 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
         const int njobs = ntok * S;
         for (int p0 = warp; p0 < njobs; p0 += 2 * kProjWarps) {
             int tj[2], sj[2], nj[2], basej[2];
-            float Mj[2], invj[2];
             const uint32_t* vmask[2];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
@@ -375,10 +349,9 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                 sj[j] = on ? p / ntok : 0;
                 nj[j] = on ? L->cnt[tj[j]] : 0;
                 basej[j] = L->base[tj[j]];
-                Mj[j] = L->M[tj[j]];
-                invj[j] = L->inv[tj[j]];
                 vmask[j] = L->valid[tj[j]];
             }
+            float mrun[2] = {-INFINITY, -INFINITY}, lrun[2] = {0.f, 0.f};
             float4 acc[2][4];
 #pragma unroll
             for (int j = 0; j < 2; ++j)
@@ -392,21 +365,21 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                 for (int j = 0; j < 2; ++j)
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
-                        // record kk of the token: row base + kk * step; an empty record is never read
-                        // (weight 0, load skipped)
+                        // record kk of the token: row base + kk * step; a missing record is never read
                         const int kk = sj[j] + (i + q) * S;
                         more |= kk < nj[j];
                         rq[j][q] = static_cast<long long>(basej[j]) + static_cast<long long>(kk) * step;
                         vq[j][q] = kk < nj[j] && ((vmask[j][kk >> 5] >> (kk & 31)) & 1u);
                     }
                 if (!more) break;
-                float mq[2][2];
+                float2 mlq[2][2];
                 float4 v[2][2][4];
 #pragma unroll
                 for (int j = 0; j < 2; ++j)
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
-                        mq[j][q] = vq[j][q] ? __ldg(rec_ml + rq[j][q] * 2) * mscale : 0.f;
+                        mlq[j][q] = vq[j][q] ? __ldg(reinterpret_cast<const float2*>(rec_ml + rq[j][q] * 2))
+                                             : make_float2(-INFINITY, 0.f);
 #pragma unroll
                         for (int u4 = 0; u4 < 4; ++u4) {
                             const int u = lane + 32 * u4;
@@ -416,47 +389,95 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                         }
                     }
 #pragma unroll
-                for (int j = 0; j < 2; ++j)
+                for (int j = 0; j < 2; ++j) {
+                    float mq[2];
 #pragma unroll
-                    for (int q = 0; q < 2; ++q) {
-                        const float w = vq[j][q] ? exp2f(mq[j][q] - Mj[j]) * invj[j] : 0.f;
+                    for (int q = 0; q < 2; ++q)   // an empty part (l = 0) contributes nothing
+                        mq[q] = mlq[j][q].y > 0.f ? mlq[j][q].x * mscale : -INFINITY;
+                    const float mnew = fmaxf(mrun[j], fmaxf(mq[0], mq[1]));
+                    if (mnew == -INFINITY) continue;   // nothing in this job yet
+                    const float sc = exp2f(mrun[j] - mnew);
+                    const float w0 = exp2f(mq[0] - mnew), w1 = exp2f(mq[1] - mnew);
+                    mrun[j] = mnew;
+                    lrun[j] = fmaf(lrun[j], sc, fmaf(w0, mlq[j][0].y, w1 * mlq[j][1].y));
 #pragma unroll
-                        for (int u4 = 0; u4 < 4; ++u4) {
-                            acc[j][u4].x = fmaf(w, v[j][q][u4].x, acc[j][u4].x);
-                            acc[j][u4].y = fmaf(w, v[j][q][u4].y, acc[j][u4].y);
-                            acc[j][u4].z = fmaf(w, v[j][q][u4].z, acc[j][u4].z);
-                            acc[j][u4].w = fmaf(w, v[j][q][u4].w, acc[j][u4].w);
-                        }
+                    for (int u4 = 0; u4 < 4; ++u4) {
+                        acc[j][u4].x = fmaf(acc[j][u4].x, sc, fmaf(w0, v[j][0][u4].x, w1 * v[j][1][u4].x));
+                        acc[j][u4].y = fmaf(acc[j][u4].y, sc, fmaf(w0, v[j][0][u4].y, w1 * v[j][1][u4].y));
+                        acc[j][u4].z = fmaf(acc[j][u4].z, sc, fmaf(w0, v[j][0][u4].z, w1 * v[j][1][u4].z));
+                        acc[j][u4].w = fmaf(acc[j][u4].w, sc, fmaf(w0, v[j][0][u4].w, w1 * v[j][1][u4].w));
                     }
+                }
             }
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 if (p0 + j * kProjWarps >= njobs) continue;
+                if (S == 1) {
+                    const float inv = lrun[j] > 0.f ? 1.f / lrun[j] : 0.f;
 #pragma unroll
-                for (int u4 = 0; u4 < 4; ++u4) {
-                    const int u = lane + 32 * u4;
-                    if (u < U) {
-                        if (S == 1) store_b(tj[j], u, acc[j][u4]);
-                        else reinterpret_cast<float4*>(red)[(sj[j] * ntok + tj[j]) * U + u] = acc[j][u4];
+                    for (int u4 = 0; u4 < 4; ++u4) {
+                        const int u = lane + 32 * u4;
+                        if (u < U)
+                            store_b(tj[j], u, make_float4(acc[j][u4].x * inv, acc[j][u4].y * inv,
+                                                          acc[j][u4].z * inv, acc[j][u4].w * inv));
                     }
+                } else {
+                    const int row = sj[j] * ntok + tj[j];
+#pragma unroll
+                    for (int u4 = 0; u4 < 4; ++u4) {
+                        const int u = lane + 32 * u4;
+                        if (u < U) reinterpret_cast<float4*>(red)[row * U + u] = acc[j][u4];
+                    }
+                    if (lane == 0) L->split_ml[row] = make_float2(mrun[j], lrun[j]);
                 }
             }
         }
         if (S > 1) {
             __syncthreads();
-            for (int i = threadIdx.x; i < ntok * U; i += blockDim.x) {
-                const int u = i % U, t = i / U;
-                float4 a = reinterpret_cast<float4*>(red)[t * U + u];
-                for (int s = 1; s < S; ++s) {
-                    const float4 v = reinterpret_cast<float4*>(red)[(s * ntok + t) * U + u];
-                    a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+            // per token: the splits' common max and final weights 2^(m_s - M) / sum_s 2^(m_s - M) l_s
+            // (lane s of a warp takes split s; S <= 32)
+            for (int t = warp; t < ntok; t += kProjWarps) {
+                const float2 ml = lane < S ? L->split_ml[lane * ntok + t] : make_float2(-INFINITY, 0.f);
+                float M = ml.x;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+                const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);   // an empty split weighs 0
+                float l = w * ml.y;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+                if (lane < S) L->split_w[lane * ntok + t] = l > 0.f ? w / l : 0.f;
+            }
+            __syncthreads();
+            // weighted sum over the splits: four lanes per (token, unit), each taking every fourth
+            // split, then two shuffles (ntok * U * 4 is a multiple of 64: whole warps take part)
+            for (int i = threadIdx.x; i < ntok * U * 4; i += blockDim.x) {
+                const int q = i & 3, tu = i >> 2, u = tu % U, t = tu / U;
+                float4 a = zero4;
+                for (int sp = q; sp < S; sp += 4) {
+                    const float w = L->split_w[sp * ntok + t];
+                    const float4 v = reinterpret_cast<float4*>(red)[(sp * ntok + t) * U + u];
+                    a.x = fmaf(w, v.x, a.x); a.y = fmaf(w, v.y, a.y); a.z = fmaf(w, v.z, a.z); a.w = fmaf(w, v.w, a.w);
                 }
-                store_b(t, u, a);
+#pragma unroll
+                for (int o = 1; o < 4; o <<= 1) {
+                    a.x += __shfl_xor_sync(0xffffffffu, a.x, o);
+                    a.y += __shfl_xor_sync(0xffffffffu, a.y, o);
+                    a.z += __shfl_xor_sync(0xffffffffu, a.z, o);
+                    a.w += __shfl_xor_sync(0xffffffffu, a.w, o);
+                }
+                if (q == 0) store_b(t, u, a);
             }
         }
         // padding token rows are zero
         for (int i = threadIdx.x; i < (ntp - ntok) * U; i += blockDim.x)
             store_b(ntok + i / U, i % U, make_float4(0.f, 0.f, 0.f, 0.f));
+    }
+    const bool failed = parts == 0 && status0 != kStatusOk;
+    if (failed) {
+        // the decode kernel gave up on a wait: make the failure visible in the output
+        const float nan = __int_as_float(0x7fc00000);
+        for (int i = threadIdx.x; i < ntok * dv; i += blockDim.x)
+            out[(static_cast<long long>(b0 + i / dv) * P.H + h) * dv + i % dv] = nan;
     }
     fence_proxy_async_smem();
     __syncthreads();

@@ -81,9 +81,10 @@ inline bool make_tmap_2d_16b(CUtensorMap* map, const void* base, uint64_t rows, 
     return true;
 }
 
-// 2-D row-major fp32 tensor (rows x cols, row pitch in elements), no swizzle.
+// 2-D row-major fp32 tensor (rows x cols, row pitch in elements).
 inline bool make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
-                             uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols) {
+                             uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols,
+                             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
     auto enc = tensor_map_encoder();
     if (!enc) return false;
     if (reinterpret_cast<uintptr_t>(base) % 16 != 0 || (row_stride_elems * 4) % 16 != 0) return false;
@@ -92,7 +93,7 @@ inline bool make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, 
     cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
