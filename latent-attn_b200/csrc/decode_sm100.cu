@@ -109,7 +109,7 @@ __device__ __forceinline__ int code(int site) { return kStatusTimeout | (site <<
 
 // Diagnostics after a wait gave up: status[1] counts failures, status[2] holds
 // the first failing (block + 1) << 16 | tile, status[3] ORs the failing sites.
-__device__ __forceinline__ void note_fail(volatile int* err, int site, int tile) {
+static __device__ __noinline__ void note_fail(volatile int* err, int site, int tile) {
     int* e = const_cast<int*>(err);
     atomicAdd(e + 1, 1);
     atomicCAS(e + 2, 0, ((static_cast<int>(blockIdx.x) + 1) << 16) | (tile & 0xFFFF));

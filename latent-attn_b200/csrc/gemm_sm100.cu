@@ -53,6 +53,19 @@ __device__ __forceinline__ uint32_t pack_pair<__nv_bfloat16>(float a, float b) {
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
+// AND of `pred` over the `nthreads` threads (whole warps) that reach named barrier `id`.
+__device__ __forceinline__ bool bar_red_and(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
 __device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t a, uint32_t b) {
     asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
 }
@@ -157,9 +170,10 @@ absorb_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
     }
     fence_proxy_async_smem();
     __syncthreads();
+    bool issued = true;   // thread 0: the W boxes landed and the MMAs were issued
     if (threadIdx.x == 0) {
-        bool ok = mbar_wait(a_full, 0, err, gcode(kSiteAbsorbA));
-        if (ok) {
+        issued = mbar_wait(a_full, 0, err, gcode(kSiteAbsorbA));
+        if (issued) {
             tc_fence_after();
             const uint32_t idesc = idesc_f16(128, ntp, GemmFmt<T>::v, true, false);
             for (int k = 0; k < dn / 16; ++k) {
@@ -173,7 +187,8 @@ absorb_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
     // epilogue: thread (warp w, lane) holds d_c index m0 + 32 w + lane for every token column.
     // The values go through shared memory (the B operand's space, free once the MMAs are done)
     // as [token][128] rows of T, which are then written to qpack with 16-byte stores.
-    bool ok = mbar_wait(mma_done, 0, err, gcode(kSiteAbsorbMma)) && *err == 0;
+    // the block-wide AND carries thread 0's result to every thread (no global status read)
+    bool ok = mbar_wait(mma_done, 0, err, gcode(kSiteAbsorbMma)) && issued;
     ok = __all_sync(0xffffffffu, ok);
     const bool all_ok = __syncthreads_and(ok);
     T* stage = reinterpret_cast<T*>(smem + 2 * dn * 128);   // ntp x 128 elements <= B operand bytes
@@ -481,10 +496,11 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
     }
     fence_proxy_async_smem();
     __syncthreads();
+    bool issued = true;   // thread 0: the W_UV boxes landed (and, unless failed, the MMAs were issued)
     if (threadIdx.x == 0) {
         // always wait for the W_UV boxes: shared memory must not be released under a TMA write
-        bool ok = mbar_wait(a_full, 0, err, gcode(kSiteProjA));
-        if (ok && !failed) {
+        issued = mbar_wait(a_full, 0, err, gcode(kSiteProjA));
+        if (issued && !failed) {
             tc_fence_after();
             const uint32_t idesc = idesc_f16(dv, ntp, GemmFmt<T>::v, false, false);
             for (int k = 0; k < dc / 16; ++k) {
@@ -495,9 +511,14 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
         }
         mma_commit(mma_done);
     }
+    if (warp == 0 || (warp >= 4 && warp < 8)) {
+        // thread 0's result reaches the epilogue warps through an AND over a named barrier of
+        // warps 0 and 4-7 (no global status read)
+        issued = bar_red_and(1, 160, issued);
+    }
     if (warp >= 4 && warp < 8 && !failed) {
         // warps 4-7: warp w reads TMEM lanes 32 (w - 4) .. + 31, i.e. output columns j < dv = 128
-        bool ok = mbar_wait(mma_done, 0, err, gcode(kSiteProjMma)) && *err == 0;
+        bool ok = mbar_wait(mma_done, 0, err, gcode(kSiteProjMma)) && issued;
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
             tc_fence_after();

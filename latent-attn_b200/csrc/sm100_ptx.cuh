@@ -108,9 +108,8 @@ static __device__ __noinline__ void record_timeout(volatile int* err, int code) 
 }
 
 template <bool kCluster, bool kPollErr>
-__device__ __forceinline__ bool mbar_wait_impl(uint32_t bar, uint32_t parity, volatile int* err, int code,
-                                               uint64_t timeout_ns) {
-    if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* err, int code,
+                                                   uint64_t timeout_ns) {
     const long long c0 = clock64();
     const long long budget = wait_budget_cycles(timeout_ns);
     for (uint32_t i = 1;; ++i) {
@@ -123,6 +122,15 @@ __device__ __forceinline__ bool mbar_wait_impl(uint32_t bar, uint32_t parity, vo
     }
     record_timeout(err, code);
     return false;
+}
+// The first try_wait inline, the retry loop out of line: the decode kernel's roles run
+// different code on the same SM, and instruction fetch is the most frequent warp stall there,
+// so every inlined copy of a rarely-run loop costs time (10% at large batches).
+template <bool kCluster, bool kPollErr>
+__device__ __forceinline__ bool mbar_wait_impl(uint32_t bar, uint32_t parity, volatile int* err, int code,
+                                               uint64_t timeout_ns) {
+    if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+    return mbar_wait_slow<kCluster, kPollErr>(bar, parity, err, code, timeout_ns);
 }
 
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* err, int code,
