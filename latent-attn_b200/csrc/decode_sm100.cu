@@ -192,20 +192,14 @@ __device__ __forceinline__ void st_row32(float* p, const uint32_t (&v)[32]) {
                      : "memory");
 }
 
-// Writes `ncols` (a multiple of 64) fp32 columns of this thread's TMEM row to `orow` (skipped when
-// !row_ok): 32 columns at a time, the next chunk's TMEM load in flight during this chunk's stores;
-// 32-byte stores halve the store instructions of this row-per-thread layout. Warp-collective.
+// Writes `ncols` (a multiple of 32) fp32 columns of this thread's TMEM row to `orow` (skipped when
+// !row_ok), 32 columns at a time; 32-byte stores halve the store instructions of this
+// row-per-thread layout. Warp-collective.
 __device__ __forceinline__ void write_o_cols(uint32_t tsrc, float* orow, bool row_ok, int ncols) {
-    uint32_t oa[32], ob[32];
-    tmem_ld32(tsrc, oa);
-    tmem_ld_wait();
-    for (int c0 = 0; c0 < ncols; c0 += 64) {
-        tmem_ld32(tsrc + c0 + 32, ob);
-        if (row_ok) st_row32(orow + c0, oa);
-        tmem_ld_wait();
-        if (c0 + 64 < ncols) tmem_ld32(tsrc + c0 + 64, oa);
-        if (row_ok) st_row32(orow + c0 + 32, ob);
-        tmem_ld_wait();
+    for (int c0 = 0; c0 < ncols; c0 += 32) {
+        uint32_t o[32];
+        tmem_ld32_sync(tsrc + c0, o);
+        if (row_ok) st_row32(orow + c0, o);
     }
 }
 
@@ -617,9 +611,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             uint32_t h[32];
             {
                 uint32_t sr[64];
-                tmem_ld32(trow + kColS, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-                tmem_ld32(trow + kColS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-                tmem_ld_wait();
+                tmem_ld64_sync(trow + kColS, sr);
                 tc_fence_before();
                 mbar_arrive(smem_u32(&bars->s_free));
 #pragma unroll
@@ -750,8 +742,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
 #pragma unroll 1
                 for (int c0 = 0; c0 < 256; c0 += 32) {
                     uint32_t o[32];
-                    tmem_ld32(trow + kColO + c0, o);
-                    tmem_ld_wait();
+                    tmem_ld32_sync(trow + kColO + c0, o);
 #pragma unroll
                     for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
                     tmem_st32(trow + kColO + c0, o);

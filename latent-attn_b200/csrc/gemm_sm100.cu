@@ -197,8 +197,7 @@ absorb_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
         const uint32_t trow = tbase + (static_cast<uint32_t>(32 * warp) << 16);
         for (int c0 = 0; c0 < ntok; c0 += 16) {
             uint32_t r[16];
-            tmem_ld16(trow + c0, r);
-            tmem_ld_wait();
+            tmem_ld16_sync(trow + c0, r);
 #pragma unroll
             for (int j = 0; j < 16; ++j)
                 stage[(c0 + j) * 128 + 32 * warp + lane] = ElemTraits<T>::from_f(__uint_as_float(r[j]) * q_scale);
@@ -526,8 +525,7 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
             const uint32_t trow = tbase + (static_cast<uint32_t>(32 * (warp - 4)) << 16);
             for (int c0 = 0; c0 < ntok; c0 += 16) {
                 uint32_t r[16];
-                tmem_ld16(trow + c0, r);
-                tmem_ld_wait();
+                tmem_ld16_sync(trow + c0, r);
 #pragma unroll
                 for (int q = 0; q < 16; ++q) {
                     const int n = c0 + q;
