@@ -196,10 +196,13 @@ __device__ __forceinline__ void st_row32(float* p, const uint32_t (&v)[32]) {
 // !row_ok), 32 columns at a time; 32-byte stores halve the store instructions of this
 // row-per-thread layout. Warp-collective.
 __device__ __forceinline__ void write_o_cols(uint32_t tsrc, float* orow, bool row_ok, int ncols) {
-    for (int c0 = 0; c0 < ncols; c0 += 32) {
-        uint32_t o[32];
-        tmem_ld32_sync(tsrc + c0, o);
-        if (row_ok) st_row32(orow + c0, o);
+    for (int c0 = 0; c0 < ncols; c0 += 64) {
+        uint32_t o[64];
+        tmem_ld64_sync(tsrc + c0, o);
+        if (row_ok) {
+            st_row32(orow + c0, *reinterpret_cast<const uint32_t(*)[32]>(&o[0]));
+            st_row32(orow + c0 + 32, *reinterpret_cast<const uint32_t(*)[32]>(&o[32]));
+        }
     }
 }
 
