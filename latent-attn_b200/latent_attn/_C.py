@@ -47,17 +47,29 @@ def _check_f32(t: torch.Tensor, name: str) -> None:
 
 
 def _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim):
-    c = _lib.MlaConfig(int(d_model), int(kv_lora_rank), int(qk_nope_head_dim), int(qk_rope_head_dim),
-                       int(num_heads), int(v_head_dim))
-    # MLAConfig::validate (src/mla_config.cuh:35-40) raises std::invalid_argument -> ValueError
-    if kv_lora_rank <= 0 or qk_nope_head_dim <= 0 or qk_rope_head_dim <= 0:
-        raise ValueError("MLA dims must be positive")
-    if num_heads <= 0 or v_head_dim <= 0:
-        raise ValueError("num_heads and v_head_dim must be positive")
+    key = (int(d_model), int(kv_lora_rank), int(qk_nope_head_dim), int(qk_rope_head_dim), int(num_heads),
+           int(v_head_dim))
+    c = _CFG_CACHE.get(key)
+    if c is None:
+        # MLAConfig::validate (src/mla_config.cuh:35-40) raises std::invalid_argument -> ValueError
+        if kv_lora_rank <= 0 or qk_nope_head_dim <= 0 or qk_rope_head_dim <= 0:
+            raise ValueError("MLA dims must be positive")
+        if num_heads <= 0 or v_head_dim <= 0:
+            raise ValueError("num_heads and v_head_dim must be positive")
+        # the C side only reads the struct: one instance per configuration serves every call
+        c = _lib.MlaConfig(*key)
+        _CFG_CACHE[key] = c
     return c
 
 
+_CFG_CACHE: dict = {}
+# the raw current-stream query skips building a torch.cuda.Stream object on every call
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device: torch.device) -> int:
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -236,10 +248,19 @@ def _run_decode(cfg, dtype, batch, shared, kv_cache, max_seq_len, q_rope, W_UV, 
                 workspace=None, **kw):
     args = _decode_args(dtype, batch, shared, kv_cache, max_seq_len, q_rope, W_UV, rope_cos, rope_sin, out,
                         **kw)
-    ws = _workspace(cfg, args, kv_cache.device, workspace)
     lib = _lib.load()
+    stream = C.c_void_p(_stream(kv_cache.device))
+    if workspace is not None and workspace.data_ptr() % 256 == 0:
+        # a caller's workspace is tried as it is: the call itself checks its size, and only a
+        # too-small one costs the size query and an allocation
+        st = lib.mla_decode(C.byref(cfg), C.byref(args), C.c_void_p(workspace.data_ptr()),
+                            C.c_size_t(workspace.numel() * workspace.element_size()), stream)
+        if st != _lib.MLA_ERR_WORKSPACE:
+            _lib.check(st)
+            return workspace
+    ws = _workspace(cfg, args, kv_cache.device, workspace)
     _lib.check(lib.mla_decode(C.byref(cfg), C.byref(args), C.c_void_p(ws.data_ptr()),
-                              C.c_size_t(ws.numel()), C.c_void_p(_stream(kv_cache.device))))
+                              C.c_size_t(ws.numel() * ws.element_size()), stream))
     return ws
 
 

@@ -12,10 +12,17 @@ if TYPE_CHECKING:
     from latent_attn import MLAConfig
 
 
+_EXT = None
+
+
 def _load_ext():
+    global _EXT
+    if _EXT is not None:
+        return _EXT
     try:
         from latent_attn import _C, _lib
         _lib.load()
+        _EXT = _C
         return _C
     except ImportError as e:
         raise ImportError(
