@@ -16,8 +16,10 @@
 //        out[b, h, j]   = o_lat[b, h, :] . W_UV[h*dv + j, :]   (src/fused_mla.cu:258-267)
 //    Transposed again, D^T[dv x tokens] = W_UV_h . o_lat_h^T with M = dv = 128:
 //      A = W_UV_h, K-major, all d_c / 64 TMA boxes resident (128 KB at d_c = 512)
-//      B = o_lat_h^T, K-major, merged by the CTA's threads from the records (L2).
-//    CTA = (block of up to 64 tokens, head), 256 threads.
+//      B = o_lat_h^T, K-major, merged by the CTA's threads from the records (L2) in one pass:
+//          each record's (m, l) is loaded with its row and folded into a running log-sum-exp.
+//    CTA = (block of up to 64 tokens, head), 512 threads. The same kernel merges the gathered
+//    partial sets of KV-range shards (mla_combine_partials).
 //
 // Both launch W loads by TMA before waiting on the previous kernel
 // (programmatic dependent launch), so weight streaming overlaps its tail.
