@@ -124,3 +124,18 @@ cudaError_t call(const __half* kv, int S, const float* qa, const float* qr, cons
         r = subprocess.run(["nvcc", "-std=c++17", "-I", INC, "-I", os.path.join(INC, "latent_attn_b200"),
                             "-c", f, "-o", os.path.join(d, "caller.o")], capture_output=True, text=True)
         assert r.returncode == 0, r.stderr
+
+
+def test_binding_config_cache_validates_and_reuses():
+    """The binding builds one read-only config struct per configuration and still rejects
+    invalid dimensions the way MLAConfig::validate does (ValueError)."""
+    from latent_attn import _C
+    a = _C._cfg(0, 512, 128, 64, 128, 128)
+    b = _C._cfg(0, 512, 128, 64, 128, 128)
+    assert a is b
+    assert (a.kv_lora_rank, a.qk_nope_head_dim, a.qk_rope_head_dim, a.num_heads, a.v_head_dim) == (512, 128, 64, 128, 128)
+    assert _C._cfg(0, 512, 128, 64, 16, 128) is not a
+    with pytest.raises(ValueError):
+        _C._cfg(0, 0, 128, 64, 128, 128)
+    with pytest.raises(ValueError):
+        _C._cfg(0, 512, 128, 64, 0, 128)
