@@ -72,13 +72,16 @@ def measured_peaks():
     return HBM_FALLBACK_GBS, "fallback (6.65 TB/s, earlier pool measurement)"
 
 
-def ncu_traffic(workload):
-    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary, if any."""
+def ncu_traffic(workload, share=1.0):
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary (a one-GPU launch
+    over the whole workload), scaled by the share of the workload's cache rows this rank's launch
+    decodes (the traffic grows in proportion to the rows); None without a summary."""
     p = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return d.get(workload)
+        t = d.get(workload)
+        return None if t is None else int(round(t * share))
     return None
 
 
@@ -413,17 +416,21 @@ def main():
     total_ms = sum(step_ms)
 
     # ---- end-to-end: host buffers, H2D of the step's queries and D2H of the output inside the timed span
-    qn_h = inp.q_nope.float().pin_memory()
-    qr_h = inp.q_rope.float().pin_memory()
+    # the step's queries live in one pinned host buffer (q_nope then q_rope), so one copy uploads them
+    nqn, nqr = q_nope.numel(), q_rope.numel()
+    q_h = torch.empty(nqn + nqr, dtype=torch.float32).pin_memory()
+    q_h[:nqn].copy_(inp.q_nope.float().reshape(-1))
+    q_h[nqn:].copy_(inp.q_rope.float().reshape(-1))
+    qn_h, qr_h = q_h[:nqn], q_h[nqn:]
     out_h = torch.empty(B, 128, 128, dtype=torch.float32).pin_memory()
-    qn_d, qr_d = torch.empty_like(q_nope), torch.empty_like(q_rope)
+    q_d = torch.empty(nqn + nqr, dtype=torch.float32, device=dev)
+    qn_d, qr_d = q_d[:nqn].view(q_nope.shape), q_d[nqn:].view(q_rope.shape)
     e2e_ms = []
     barrier()
     for k in range(args.steps):
         flush.zero_()
         ev0[k].record(stream)
-        qn_d.copy_(qn_h, non_blocking=True)
-        qr_d.copy_(qr_h, non_blocking=True)
+        q_d.copy_(q_h, non_blocking=True)
         o = step(q_n=qn_d, q_r=qr_d)
         out_h.copy_(o, non_blocking=True)
         ev1[k].record(stream)
@@ -453,7 +460,8 @@ def main():
             dmean = statistics.mean(dec_ms)
             achieved = bytes_per_step / dmean / 1e6
             roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                    "frac": round(achieved / peak, 4), "traffic": ncu_traffic(args.workload),
+                    "frac": round(achieved / peak, 4),
+                    "traffic": ncu_traffic(args.workload, sum(my_lens) / sum(lens_all)),
                     "kernel": "mla::decode_sm100_kernel", "kernel_us": round(dmean * 1e3, 3),
                     "algorithmic_bytes": bytes_per_step, "peak_source": peak_src + " -- fraction is of measured"}
         cpu = None
