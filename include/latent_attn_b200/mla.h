@@ -22,6 +22,8 @@
  *                             (m, l, o_latent) out of one shard; log-sum-exp merge of
  *                             G shards' partials + the W_UV projection of
  *                             src/fused_mla.cu:258-267)
+ *   mla_cache_append          LatentKVCache::append_host (src/mla_config.cuh:58-72),
+ *                             moved to the device for a whole batch
  *   mla_config_validate       MLAConfig::validate() (src/mla_config.cuh:35-40)
  */
 #ifndef LATENT_ATTN_B200_MLA_H_
@@ -189,6 +191,24 @@ MLA_API mla_status_t mla_decode_partial(const mla_config_t* cfg, const mla_decod
 MLA_API mla_status_t mla_combine_partials(const mla_config_t* cfg, mla_dtype_t dtype, int batch,
                                   int num_parts, const float* partial_ml, const float* partial_o,
                                   const void* W_UV, float* output, mla_stream_t stream);
+
+/* Device-side cache append, one new row per sequence: for each b, row
+ * (kv_offsets ? kv_offsets[b] : b * max_seq_len) + seq_lens[b] of kv_cache receives
+ * [c_t[b] (d_c) | k_rope[b] (d_R)] (k_rope unrotated, as the cache stores it) and
+ * seq_lens[b] advances by one. Everything happens on the stream: no host copy, no
+ * synchronisation, so a decode step can append and attend without the host.
+ * Replaces LatentKVCache::append_host (src/mla_config.cuh:58-72), which copies one
+ * position from host memory and synchronises the stream per token.
+ * - c_t (batch, d_c) and k_rope (batch, d_R): device, element type `dtype`.
+ * - seq_lens (batch,) int32 device, read and advanced; kv_offsets (batch,) int64
+ *   device or NULL (sequence b starts at row b * max_seq_len).
+ * - A sequence that already holds max_seq_len rows is left unchanged; if status is
+ *   non-NULL (a device int), bit 0 of *status is set for it.
+ * - kv_row_stride: elements between rows, 0 meaning d_c + d_R. */
+MLA_API mla_status_t mla_cache_append(const mla_config_t* cfg, mla_dtype_t dtype, void* kv_cache,
+                              int64_t kv_row_stride, int batch, const void* c_t, const void* k_rope,
+                              const int64_t* kv_offsets, int* seq_lens, int max_seq_len, int* status,
+                              mla_stream_t stream);
 
 /* Kernel timing for benchmarks: a timer passed in mla_decode_args_t.timer gets
  * CUDA events recorded on the call's stream immediately before and after the

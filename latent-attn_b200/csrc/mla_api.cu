@@ -434,6 +434,36 @@ mla_status_t mla_combine_partials(const mla_config_t* cfg, mla_dtype_t dtype, in
     return MLA_OK;
 }
 
+mla_status_t mla_cache_append(const mla_config_t* cfg, mla_dtype_t dtype, void* kv_cache, int64_t kv_row_stride,
+                              int batch, const void* c_t, const void* k_rope, const int64_t* kv_offsets,
+                              int* seq_lens, int max_seq_len, int* status, mla_stream_t stream) {
+    mla_status_t st = validate_cfg(cfg);
+    if (st != MLA_OK) return st;
+    if (!kv_cache || !c_t || !k_rope || !seq_lens) return fail(MLA_ERR_INVALID_ARGUMENT, "null pointer");
+    if (batch <= 0) return fail(MLA_ERR_INVALID_ARGUMENT, "batch must be positive, got %d", batch);
+    if (max_seq_len <= 0) return fail(MLA_ERR_INVALID_ARGUMENT, "max_seq_len must be positive, got %d", max_seq_len);
+    const int dc = cfg->kv_lora_rank, dR = cfg->qk_rope_head_dim;
+    const int64_t stride = kv_row_stride ? kv_row_stride : (dc + dR);
+    if (stride < dc + dR) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_row_stride %lld < d_c + d_R", (long long)stride);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    if (dtype == MLA_DTYPE_BF16)
+        e = mla::launch_cache_append<__nv_bfloat16>(static_cast<__nv_bfloat16*>(kv_cache), stride, dc, dR, batch,
+                                                    static_cast<const __nv_bfloat16*>(c_t),
+                                                    static_cast<const __nv_bfloat16*>(k_rope), kv_offsets, seq_lens,
+                                                    max_seq_len, status, s);
+    else if (dtype == MLA_DTYPE_F16)
+        e = mla::launch_cache_append<__half>(static_cast<__half*>(kv_cache), stride, dc, dR, batch,
+                                             static_cast<const __half*>(c_t), static_cast<const __half*>(k_rope),
+                                             kv_offsets, seq_lens, max_seq_len, status, s);
+    else
+        return fail(MLA_ERR_UNSUPPORTED, "dtype must be F16 or BF16");
+    if (e == cudaErrorNoKernelImageForDevice || e == cudaErrorInvalidDeviceFunction)
+        return fail(MLA_ERR_NO_DEVICE_CODE, "cache append kernel: %s (library is built for sm_100a)", cudaGetErrorString(e));
+    if (e != cudaSuccess) return cuda_fail(e, "cache append kernel launch");
+    return MLA_OK;
+}
+
 mla_status_t mla_launch_fused(const mla_fused_params_t* p, mla_dtype_t dtype, mla_stream_t stream) {
     if (!p) return fail(MLA_ERR_INVALID_ARGUMENT, "params is null");
     mla_status_t st = validate_cfg(p->cfg);

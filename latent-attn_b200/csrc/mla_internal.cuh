@@ -211,6 +211,10 @@ template <typename T>
 cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
                                 const float* sin, float* rec_ml, float* rec_o, bool pdl, cudaStream_t s);
 bool decode_sm100_available();
+// cache.cu
+template <typename T>
+cudaError_t launch_cache_append(T* kv, long long stride, int dc, int dR, int batch, const T* c_t, const T* k_rope,
+                                const int64_t* offs, int* seq_lens, int max_len, int* status, cudaStream_t s);
 // combine.cu
 template <typename T>
 cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const float* rec_o,

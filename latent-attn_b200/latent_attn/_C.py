@@ -377,3 +377,37 @@ def mla_combine_partials(part_ml: torch.Tensor, part_o: torch.Tensor, W_UV: torc
                                         C.c_void_p(part_o.data_ptr()), C.c_void_p(W_UV.data_ptr()),
                                         C.c_void_p(out.data_ptr()), C.c_void_p(_stream(part_ml.device))))
     return out
+
+
+def mla_cache_append(kv_cache: torch.Tensor, c_t: torch.Tensor, k_rope: torch.Tensor, seq_lens: torch.Tensor,
+                     max_seq_len: int, d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads,
+                     v_head_dim, *, kv_offsets: Optional[torch.Tensor] = None,
+                     status: Optional[torch.Tensor] = None) -> None:
+    """Append one row per sequence on the device: row ``kv_offsets[b]`` (or ``b * max_seq_len``)
+    ``+ seq_lens[b]`` of ``kv_cache`` receives ``[c_t[b] | k_rope[b]]`` (k_rope unrotated) and
+    ``seq_lens[b]`` advances by one; nothing waits for the device. ``c_t`` (B, d_c) and ``k_rope``
+    (B, d_R) have the cache's dtype. A full sequence (``max_seq_len`` rows) is left unchanged and
+    sets bit 0 of ``status`` (a CUDA int32 tensor), if given."""
+    if kv_cache.dtype not in _DT or not kv_cache.is_cuda or kv_cache.stride(-1) != 1:
+        raise RuntimeError("kv_cache must be a CUDA fp16/bf16 tensor with unit inner stride")
+    for t, name in ((c_t, "c_t"), (k_rope, "k_rope")):
+        _check_half(t, name)
+        if t.dtype != kv_cache.dtype:
+            raise RuntimeError(f"{name} dtype must match kv_cache dtype")
+    B = c_t.size(0)
+    if tuple(c_t.shape) != (B, kv_lora_rank) or tuple(k_rope.shape) != (B, qk_rope_head_dim):
+        raise RuntimeError("c_t must be (batch, kv_lora_rank) and k_rope (batch, qk_rope_head_dim)")
+    if seq_lens.dtype != torch.int32 or not seq_lens.is_cuda or seq_lens.numel() != B:
+        raise RuntimeError("seq_lens must be a CUDA int32 tensor of shape (batch,)")
+    if kv_offsets is not None and (kv_offsets.dtype != torch.int64 or not kv_offsets.is_cuda or kv_offsets.numel() != B):
+        raise RuntimeError("kv_offsets must be a CUDA int64 tensor of shape (batch,)")
+    if status is not None and (status.dtype != torch.int32 or not status.is_cuda):
+        raise RuntimeError("status must be a CUDA int32 tensor")
+    cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    stride = kv_cache.stride(0) if kv_cache.dim() == 2 else 0
+    lib = _lib.load()
+    _lib.check(lib.mla_cache_append(C.byref(cfg), _DT[kv_cache.dtype], C.c_void_p(kv_cache.data_ptr()),
+                                    C.c_int64(stride), B, C.c_void_p(c_t.data_ptr()),
+                                    C.c_void_p(k_rope.data_ptr()), C.c_void_p(_ptr(kv_offsets)),
+                                    C.c_void_p(seq_lens.data_ptr()), int(max_seq_len),
+                                    C.c_void_p(_ptr(status)), C.c_void_p(_stream(kv_cache.device))))

@@ -96,6 +96,14 @@ def test_validation_without_gpu():
     p = _lib.MlaFusedParams()
     p.cfg = C.pointer(ok)
     assert lib.mla_launch_fused(C.byref(p), _lib.DTYPE_F16, None) == _lib.MLA_ERR_INVALID_ARGUMENT
+    # cache append: null pointers, a bad batch and a bad dtype are rejected before any launch
+    fake = C.c_void_p(256)
+    assert lib.mla_cache_append(C.byref(ok), _lib.DTYPE_BF16, None, 0, 1, fake, fake, None, fake, 8, None,
+                                None) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert lib.mla_cache_append(C.byref(ok), _lib.DTYPE_BF16, fake, 0, 0, fake, fake, None, fake, 8, None,
+                                None) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert lib.mla_cache_append(C.byref(ok), _lib.DTYPE_F32, fake, 0, 1, fake, fake, None, fake, 8, None,
+                                None) == _lib.MLA_ERR_UNSUPPORTED
     assert lib.mla_version().startswith(b"latent-attn-b200")
 
 
