@@ -167,6 +167,14 @@ typedef struct mla_decode_args {
   float* output;                /* (B, H, dv) fp32 */
   int kernel;                   /* MLA_KERNEL_AUTO (0), MLA_KERNEL_TENSOR_CORE (1), MLA_KERNEL_CUDA_CORE (2) */
   mla_timer_t timer;            /* optional: CUDA events are recorded around the decode kernel */
+  /* Paged cache (block table), optional. With page_table, position p of sequence b is row
+   * page_table[b * max_pages + p / page_rows] * page_rows + p % page_rows of kv_cache, and
+   * kv_total_rows (the page pool's rows) is required; kv_offsets and shared_cache must be unset.
+   * A page id outside the pool reads no memory: the tile reads as zeros, the status word
+   * records the error and the output becomes NaN. */
+  const int* page_table;        /* device (B, max_pages) int32 page ids, or NULL (contiguous layout) */
+  int page_rows;                /* rows per page, a positive multiple of 64 */
+  int max_pages;                /* page-table entries per sequence, >= ceil(max_seq_len / page_rows) */
 } mla_decode_args_t;
 
 enum { MLA_KERNEL_AUTO = 0, MLA_KERNEL_TENSOR_CORE = 1, MLA_KERNEL_CUDA_CORE = 2 };
@@ -192,22 +200,27 @@ MLA_API mla_status_t mla_combine_partials(const mla_config_t* cfg, mla_dtype_t d
                                   int num_parts, const float* partial_ml, const float* partial_o,
                                   const void* W_UV, float* output, mla_stream_t stream);
 
-/* Device-side cache append, one new row per sequence: for each b, row
- * (kv_offsets ? kv_offsets[b] : b * max_seq_len) + seq_lens[b] of kv_cache receives
- * [c_t[b] (d_c) | k_rope[b] (d_R)] (k_rope unrotated, as the cache stores it) and
- * seq_lens[b] advances by one. Everything happens on the stream: no host copy, no
- * synchronisation, so a decode step can append and attend without the host.
+/* Device-side cache append, one new row per sequence: for each b, the row of position
+ * p = seq_lens[b] receives [c_t[b] (d_c) | k_rope[b] (d_R)] (k_rope unrotated, as the cache
+ * stores it) and seq_lens[b] advances by one. The row is (kv_offsets ? kv_offsets[b] :
+ * b * max_seq_len) + p, or, with page_table, page_table[b * max_pages + p / page_rows] *
+ * page_rows + p % page_rows (the layout mla_decode reads with the same table). Everything
+ * happens on the stream: no host copy, no synchronisation, so a decode step can append and
+ * attend without the host.
  * Replaces LatentKVCache::append_host (src/mla_config.cuh:58-72), which copies one
  * position from host memory and synchronises the stream per token.
  * - c_t (batch, d_c) and k_rope (batch, d_R): device, element type `dtype`.
- * - seq_lens (batch,) int32 device, read and advanced; kv_offsets (batch,) int64
- *   device or NULL (sequence b starts at row b * max_seq_len).
- * - A sequence that already holds max_seq_len rows is left unchanged; if status is
- *   non-NULL (a device int), bit 0 of *status is set for it.
+ * - seq_lens (batch,) int32 device, read and advanced; kv_offsets (batch,) int64 device or
+ *   NULL; page_table (batch, max_pages) int32 device or NULL (page_rows > 0 with it).
+ * - kv_total_rows: rows of kv_cache; required with page_table (a page outside it is not
+ *   written), 0 otherwise allowed.
+ * - A sequence that already holds max_seq_len rows is left unchanged and sets bit 0 of
+ *   *status; a page id outside the cache sets bit 1 (status: a device int, or NULL).
  * - kv_row_stride: elements between rows, 0 meaning d_c + d_R. */
 MLA_API mla_status_t mla_cache_append(const mla_config_t* cfg, mla_dtype_t dtype, void* kv_cache,
-                              int64_t kv_row_stride, int batch, const void* c_t, const void* k_rope,
-                              const int64_t* kv_offsets, int* seq_lens, int max_seq_len, int* status,
+                              int64_t kv_row_stride, int64_t kv_total_rows, int batch, const void* c_t,
+                              const void* k_rope, const int64_t* kv_offsets, const int* page_table,
+                              int page_rows, int max_pages, int* seq_lens, int max_seq_len, int* status,
                               mla_stream_t stream);
 
 /* Kernel timing for benchmarks: a timer passed in mla_decode_args_t.timer gets

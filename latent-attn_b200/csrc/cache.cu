@@ -14,14 +14,15 @@ namespace mla {
 
 namespace {
 
-// One CTA per sequence b: row (kv_offsets[b] or b * max_len) + seq_lens[b] receives the new
-// values, then seq_lens[b] advances. A sequence already holding max_len rows is left as it is
-// and reported through *status (bit 0).
+// One CTA per sequence b: the row of position seq_lens[b] (contiguous: kv_offsets[b] or
+// b * max_len plus the position; paged: through the page table) receives the new values, then
+// seq_lens[b] advances. A sequence already holding max_len rows is left as it is and reported
+// through *status (bit 0); so is a page outside the cache (bit 1).
 template <typename T>
-__global__ void cache_append_kernel(T* __restrict__ kv, long long stride, int dc, int dR,
+__global__ void cache_append_kernel(T* __restrict__ kv, long long stride, long long kv_rows, int dc, int dR,
                                     const T* __restrict__ c_t, const T* __restrict__ k_rope,
-                                    const int64_t* __restrict__ offs, int* seq_lens, int max_len, int* status,
-                                    bool vec16) {
+                                    const int64_t* __restrict__ offs, const int* __restrict__ pages, int page_rows,
+                                    int max_pages, int* seq_lens, int max_len, int* status, bool vec16) {
     const int b = blockIdx.x;
     const int pos = seq_lens[b];
     __syncthreads();  // every thread has read the length before thread 0 advances it
@@ -29,7 +30,17 @@ __global__ void cache_append_kernel(T* __restrict__ kv, long long stride, int dc
         if (threadIdx.x == 0 && status) atomicOr(status, 1);
         return;
     }
-    const long long row = (offs ? offs[b] : static_cast<long long>(b) * max_len) + pos;
+    long long row;
+    if (pages) {
+        const int pg = pages[static_cast<long long>(b) * max_pages + pos / page_rows];
+        row = static_cast<long long>(pg) * page_rows + pos % page_rows;
+        if (pg < 0 || static_cast<long long>(pg + 1) * page_rows > kv_rows) {
+            if (threadIdx.x == 0 && status) atomicOr(status, 2);
+            return;
+        }
+    } else {
+        row = (offs ? offs[b] : static_cast<long long>(b) * max_len) + pos;
+    }
     T* dst = kv + row * stride;
     const T* src_c = c_t + static_cast<long long>(b) * dc;
     const T* src_r = k_rope + static_cast<long long>(b) * dR;
@@ -50,20 +61,22 @@ __global__ void cache_append_kernel(T* __restrict__ kv, long long stride, int dc
 }  // namespace
 
 template <typename T>
-cudaError_t launch_cache_append(T* kv, long long stride, int dc, int dR, int batch, const T* c_t, const T* k_rope,
-                                const int64_t* offs, int* seq_lens, int max_len, int* status, cudaStream_t s) {
+cudaError_t launch_cache_append(T* kv, long long stride, long long kv_rows, int dc, int dR, int batch, const T* c_t,
+                                const T* k_rope, const int64_t* offs, const int* pages, int page_rows, int max_pages,
+                                int* seq_lens, int max_len, int* status, cudaStream_t s) {
     auto a16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
     const bool vec16 = dc % 8 == 0 && dR % 8 == 0 && stride % 8 == 0 && a16(kv) && a16(c_t) && a16(k_rope);
-    cache_append_kernel<T><<<batch, 128, 0, s>>>(kv, stride, dc, dR, c_t, k_rope, offs, seq_lens, max_len, status,
-                                                 vec16);
+    cache_append_kernel<T><<<batch, 128, 0, s>>>(kv, stride, kv_rows, dc, dR, c_t, k_rope, offs, pages, page_rows,
+                                                 max_pages, seq_lens, max_len, status, vec16);
     count_launches(1);
     return cudaGetLastError();
 }
 
-template cudaError_t launch_cache_append<__half>(__half*, long long, int, int, int, const __half*, const __half*,
-                                                 const int64_t*, int*, int, int*, cudaStream_t);
-template cudaError_t launch_cache_append<__nv_bfloat16>(__nv_bfloat16*, long long, int, int, int,
+template cudaError_t launch_cache_append<__half>(__half*, long long, long long, int, int, int, const __half*,
+                                                 const __half*, const int64_t*, const int*, int, int, int*, int, int*,
+                                                 cudaStream_t);
+template cudaError_t launch_cache_append<__nv_bfloat16>(__nv_bfloat16*, long long, long long, int, int, int,
                                                         const __nv_bfloat16*, const __nv_bfloat16*, const int64_t*,
-                                                        int*, int, int*, cudaStream_t);
+                                                        const int*, int, int, int*, int, int*, cudaStream_t);
 
 }  // namespace mla

@@ -69,15 +69,17 @@ decode_simt_kernel(DecodePlan P, const T* __restrict__ kv, const T* __restrict__
         for (int lt = lt0; lt < lt1 && active_block; ++lt) {
             const int p0 = lt * kTile;
             const int np = (len - p0) < kTile ? (len - p0) : kTile;
+            const int64_t kvr = tile_kv_row(P, g, row0, p0);   // -1: page outside the cache, read nothing
+            if (kvr < 0 && threadIdx.x == 0) atomicCAS(P.status, 0, kStatusBadPage);
             __syncthreads();
             // stage the packed rows (32-bit words; K is even)
             const int wpr = K / 2;
             for (int i = threadIdx.x; i < kTile * wpr; i += blockDim.x) {
                 int j = i / wpr, c = i % wpr;
                 uint32_t v = 0;
-                if (j < np) {
+                if (j < np && kvr >= 0) {
                     const uint32_t* src = reinterpret_cast<const uint32_t*>(
-                        kv + (row0 + p0 + j) * static_cast<int64_t>(P.row_stride));
+                        kv + (kvr + j) * static_cast<int64_t>(P.row_stride));
                     v = src[c];
                 }
                 tile_w[j * ldt + c] = v;

@@ -313,6 +313,9 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             int issued = 0;
             for (int i = 0; it.valid(); ++i, it.next(P)) {
                 const int st = i % kStages;
+                // the tile's cache row (a page-table read in the paged layout, issued before the
+                // stage wait so its latency overlaps it)
+                const long long kvr = tile_kv_row(P, it.g, it.row0, it.pos0());
                 if (i >= kStages &&
                     !mbar_wait(smem_u32(&bars->kv_empty[st]), ((i / kStages) - 1) & 1, err, code(kWaitProducer))) {
                     note_fail(err, kWaitProducer, i);
@@ -320,7 +323,9 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                 }
                 const uint32_t full = smem_u32(&bars->kv_full[st]);
                 mbar_arrive_expect_tx(full, kStageBytes);
-                const int y = static_cast<int>(it.row0 + it.pos0());
+                // a page outside the cache: the loads start below row 0 and read zeros
+                if (kvr < 0) atomicCAS(const_cast<int*>(err), 0, kStatusBadPage);
+                const int y = kvr < 0 ? -2 * kTileN : static_cast<int>(kvr);
                 const uint32_t dst = stages_u32 + st * kStageBytes;
                 // rope boxes: columns 16 r + {0, 8} and 32 + 16 r + {0, 8} of k_rope
                 for (int b = 0; b < 4; ++b)

@@ -174,6 +174,20 @@ mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan
     d.kv_offsets = a->kv_offsets;
     d.kv_pos_offset = a->kv_pos_offset;
     if (a->kv_total_rows < 0) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_total_rows must be >= 0");
+    if (a->page_table) {
+        if (a->shared_cache || a->kv_offsets)
+            return fail(MLA_ERR_INVALID_ARGUMENT, "page_table excludes shared_cache and kv_offsets");
+        if (a->page_rows <= 0 || a->page_rows % 64 != 0)
+            return fail(MLA_ERR_UNSUPPORTED, "page_rows must be a positive multiple of 64, got %d", a->page_rows);
+        if (static_cast<long long>(a->max_pages) * a->page_rows < a->max_seq_len)
+            return fail(MLA_ERR_INVALID_ARGUMENT, "max_pages %d x page_rows %d < max_seq_len %d", a->max_pages,
+                        a->page_rows, a->max_seq_len);
+        if (a->kv_total_rows <= 0)
+            return fail(MLA_ERR_INVALID_ARGUMENT, "kv_total_rows (rows of the page pool) is required with page_table");
+        d.page_table = a->page_table;
+        d.page_rows = a->page_rows;
+        d.max_pages = a->max_pages;
+    }
     if (a->kv_total_rows > 0) d.kv_rows = a->kv_total_rows;
     else if (a->kv_offsets) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_total_rows is required with kv_offsets");
     else d.kv_rows = d.shared ? a->max_seq_len : static_cast<long long>(a->batch) * a->max_seq_len;
@@ -435,7 +449,8 @@ mla_status_t mla_combine_partials(const mla_config_t* cfg, mla_dtype_t dtype, in
 }
 
 mla_status_t mla_cache_append(const mla_config_t* cfg, mla_dtype_t dtype, void* kv_cache, int64_t kv_row_stride,
-                              int batch, const void* c_t, const void* k_rope, const int64_t* kv_offsets,
+                              int64_t kv_total_rows, int batch, const void* c_t, const void* k_rope,
+                              const int64_t* kv_offsets, const int* page_table, int page_rows, int max_pages,
                               int* seq_lens, int max_seq_len, int* status, mla_stream_t stream) {
     mla_status_t st = validate_cfg(cfg);
     if (st != MLA_OK) return st;
@@ -445,17 +460,28 @@ mla_status_t mla_cache_append(const mla_config_t* cfg, mla_dtype_t dtype, void* 
     const int dc = cfg->kv_lora_rank, dR = cfg->qk_rope_head_dim;
     const int64_t stride = kv_row_stride ? kv_row_stride : (dc + dR);
     if (stride < dc + dR) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_row_stride %lld < d_c + d_R", (long long)stride);
+    if (kv_total_rows < 0) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_total_rows must be >= 0");
+    if (page_table) {
+        if (kv_offsets) return fail(MLA_ERR_INVALID_ARGUMENT, "page_table excludes kv_offsets");
+        if (page_rows <= 0) return fail(MLA_ERR_INVALID_ARGUMENT, "page_rows must be positive, got %d", page_rows);
+        if (static_cast<long long>(max_pages) * page_rows < max_seq_len)
+            return fail(MLA_ERR_INVALID_ARGUMENT, "max_pages %d x page_rows %d < max_seq_len %d", max_pages, page_rows,
+                        max_seq_len);
+        if (kv_total_rows <= 0)
+            return fail(MLA_ERR_INVALID_ARGUMENT, "kv_total_rows (rows of the page pool) is required with page_table");
+    }
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     cudaError_t e;
     if (dtype == MLA_DTYPE_BF16)
-        e = mla::launch_cache_append<__nv_bfloat16>(static_cast<__nv_bfloat16*>(kv_cache), stride, dc, dR, batch,
-                                                    static_cast<const __nv_bfloat16*>(c_t),
-                                                    static_cast<const __nv_bfloat16*>(k_rope), kv_offsets, seq_lens,
-                                                    max_seq_len, status, s);
+        e = mla::launch_cache_append<__nv_bfloat16>(static_cast<__nv_bfloat16*>(kv_cache), stride, kv_total_rows, dc,
+                                                    dR, batch, static_cast<const __nv_bfloat16*>(c_t),
+                                                    static_cast<const __nv_bfloat16*>(k_rope), kv_offsets, page_table,
+                                                    page_rows, max_pages, seq_lens, max_seq_len, status, s);
     else if (dtype == MLA_DTYPE_F16)
-        e = mla::launch_cache_append<__half>(static_cast<__half*>(kv_cache), stride, dc, dR, batch,
+        e = mla::launch_cache_append<__half>(static_cast<__half*>(kv_cache), stride, kv_total_rows, dc, dR, batch,
                                              static_cast<const __half*>(c_t), static_cast<const __half*>(k_rope),
-                                             kv_offsets, seq_lens, max_seq_len, status, s);
+                                             kv_offsets, page_table, page_rows, max_pages, seq_lens, max_seq_len,
+                                             status, s);
     else
         return fail(MLA_ERR_UNSUPPORTED, "dtype must be F16 or BF16");
     if (e == cudaErrorNoKernelImageForDevice || e == cudaErrorInvalidDeviceFunction)

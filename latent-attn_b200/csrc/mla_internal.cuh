@@ -47,6 +47,10 @@ struct DecodePlan {
     int W;                   // workers
     const int* tile_prefix;  // device (G + 1,) when !uniform (written by the pack kernel)
     int* status;             // device error word (0 = ok)
+    // paged layout (page_table != nullptr): position p of sequence b is row
+    // page_table[b * max_pages + p / page_rows] * page_rows + p % page_rows; page_rows % 64 == 0
+    const int* page_table;
+    int page_rows, max_pages;
 };
 
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
@@ -57,6 +61,19 @@ __device__ inline int group_seq(const DecodePlan& P, int g) { return P.shared ? 
 __device__ inline int group_len(const DecodePlan& P, int g) {
     if (P.uniform_len > 0) return P.uniform_len;
     return P.seq_lens[group_seq(P, g)];
+}
+
+// Cache row of position pos of group g, for the first position of a tile (pos a multiple of the
+// tile size; a tile never crosses a page since page_rows is a multiple of 64). Contiguous layout:
+// row0 + pos. Paged layout: the page id from the sequence's page-table row; an id whose page
+// lies outside the cache's kv_rows rows gives -1 (the caller reads nothing and reports it).
+__device__ inline int64_t tile_kv_row(const DecodePlan& P, int g, int64_t row0, int pos) {
+    if (!P.page_table) return row0 + pos;
+    const int b = P.shared ? 0 : g / P.head_blocks;
+    const int pg = P.page_table[static_cast<int64_t>(b) * P.max_pages + pos / P.page_rows];
+    const int64_t r = static_cast<int64_t>(pg) * P.page_rows;
+    if (pg < 0 || r + P.page_rows > P.kv_rows) return -1;
+    return r + pos % P.page_rows;
 }
 
 __device__ inline int64_t group_kv_row0(const DecodePlan& P, int g) {
@@ -172,7 +189,7 @@ template <> struct ElemTraits<__nv_bfloat16> {
 };
 
 // Device error codes written to DecodePlan::status.
-enum : int { kStatusOk = 0, kStatusTimeout = 1, kStatusBadPlan = 2 };
+enum : int { kStatusOk = 0, kStatusTimeout = 1, kStatusBadPlan = 2, kStatusBadPage = 3 };
 
 // Process-wide count of kernels launched by this library (mla_kernel_launch_count).
 void count_launches(int n);
@@ -213,8 +230,9 @@ cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack
 bool decode_sm100_available();
 // cache.cu
 template <typename T>
-cudaError_t launch_cache_append(T* kv, long long stride, int dc, int dR, int batch, const T* c_t, const T* k_rope,
-                                const int64_t* offs, int* seq_lens, int max_len, int* status, cudaStream_t s);
+cudaError_t launch_cache_append(T* kv, long long stride, long long kv_rows, int dc, int dR, int batch, const T* c_t,
+                                const T* k_rope, const int64_t* offs, const int* pages, int page_rows, int max_pages,
+                                int* seq_lens, int max_len, int* status, cudaStream_t s);
 // combine.cu
 template <typename T>
 cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const float* rec_o,

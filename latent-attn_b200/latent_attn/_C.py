@@ -80,7 +80,7 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 def _decode_args(dtype, batch, shared, kv_cache, max_seq_len, q_rope, W_UV, rope_cos, rope_sin, out,
                  q_absorbed=None, q_nope=None, W_UK=None, seq_lens=None, kv_offsets=None,
                  seq_lens_host=None, kv_pos_offset=0, softmax_scale=0.0, kv_row_stride=0, kernel=0,
-                 timer=None):
+                 timer=None, page_table=None, page_rows=0):
     a = _lib.MlaDecodeArgs()
     a.dtype = _DT[dtype]
     a.batch = int(batch)
@@ -104,6 +104,10 @@ def _decode_args(dtype, batch, shared, kv_cache, max_seq_len, q_rope, W_UV, rope
     a.output = _ptr(out)
     a.kernel = int(kernel)
     a.timer = timer.handle if timer is not None else None
+    if page_table is not None:
+        a.page_table = page_table.data_ptr()
+        a.page_rows = int(page_rows)
+        a.max_pages = int(page_table.size(-1))
     return a
 
 
@@ -277,13 +281,16 @@ def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
                seq_lens_host: Optional[Sequence[int]] = None, shared_cache: bool = False,
                kv_pos_offset: int = 0, softmax_scale: float = 0.0, kv_row_stride: int = 0,
                kernel: int = 0, out: Optional[torch.Tensor] = None,
-               workspace: Optional[torch.Tensor] = None, timer=None) -> torch.Tensor:
+               workspace: Optional[torch.Tensor] = None, timer=None,
+               page_table: Optional[torch.Tensor] = None, page_rows: int = 0) -> torch.Tensor:
     """General decode: (B, H, dv) fp32 for B sequences (or B tokens over one shared cache).
 
     Give ``q_absorbed`` (B, H, d_c) fp32, or ``q_nope`` (B, H, dn) fp32 with ``W_UK``
     (H*dn, d_c) for in-op absorption. ``seq_lens`` (B,) int32 and ``kv_offsets`` (B,)
     int64 (device) describe a variable-length batch packed in ``kv_cache``; without
-    them every sequence has ``max_seq_len`` rows at ``b * max_seq_len``.
+    them every sequence has ``max_seq_len`` rows at ``b * max_seq_len``. With ``page_table``
+    (B, max_pages) int32 (device) the cache is paged: position p of sequence b is row
+    ``page_table[b, p // page_rows] * page_rows + p % page_rows`` (``page_rows`` a multiple of 64).
     """
     if kv_row_stride:
         if kv_cache.dtype not in _DT or not kv_cache.is_cuda or kv_cache.stride(-1) != 1:
@@ -322,6 +329,10 @@ def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
     if kv_offsets is not None:
         if kv_offsets.dtype != torch.int64 or not kv_offsets.is_cuda or kv_offsets.numel() != B:
             raise RuntimeError("kv_offsets must be a CUDA int64 tensor of shape (batch,)")
+    if page_table is not None:
+        if page_table.dtype != torch.int32 or not page_table.is_cuda or page_table.dim() != 2 \
+                or page_table.size(0) != B or not page_table.is_contiguous():
+            raise RuntimeError("page_table must be a contiguous CUDA int32 tensor of shape (batch, max_pages)")
     host_arr = None
     if seq_lens_host is not None:
         host_arr = (C.c_int * B)(*[int(x) for x in seq_lens_host])
@@ -331,7 +342,7 @@ def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
                 rope_sin, out, workspace=workspace, q_absorbed=q_absorbed, q_nope=q_nope, W_UK=W_UK,
                 seq_lens=seq_lens, kv_offsets=kv_offsets, seq_lens_host=host_arr,
                 kv_pos_offset=kv_pos_offset, softmax_scale=softmax_scale, kv_row_stride=kv_row_stride,
-                kernel=kernel, timer=timer)
+                kernel=kernel, timer=timer, page_table=page_table, page_rows=page_rows)
     return out
 
 
@@ -382,12 +393,15 @@ def mla_combine_partials(part_ml: torch.Tensor, part_o: torch.Tensor, W_UV: torc
 def mla_cache_append(kv_cache: torch.Tensor, c_t: torch.Tensor, k_rope: torch.Tensor, seq_lens: torch.Tensor,
                      max_seq_len: int, d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads,
                      v_head_dim, *, kv_offsets: Optional[torch.Tensor] = None,
+                     page_table: Optional[torch.Tensor] = None, page_rows: int = 0,
                      status: Optional[torch.Tensor] = None) -> None:
-    """Append one row per sequence on the device: row ``kv_offsets[b]`` (or ``b * max_seq_len``)
-    ``+ seq_lens[b]`` of ``kv_cache`` receives ``[c_t[b] | k_rope[b]]`` (k_rope unrotated) and
-    ``seq_lens[b]`` advances by one; nothing waits for the device. ``c_t`` (B, d_c) and ``k_rope``
-    (B, d_R) have the cache's dtype. A full sequence (``max_seq_len`` rows) is left unchanged and
-    sets bit 0 of ``status`` (a CUDA int32 tensor), if given."""
+    """Append one row per sequence on the device: the row of position ``seq_lens[b]`` (at
+    ``kv_offsets[b]`` or ``b * max_seq_len`` plus the position, or through ``page_table`` (B,
+    max_pages) int32 with ``page_rows`` rows a page) receives ``[c_t[b] | k_rope[b]]`` (k_rope
+    unrotated) and ``seq_lens[b]`` advances by one; nothing waits for the device. ``c_t`` (B, d_c)
+    and ``k_rope`` (B, d_R) have the cache's dtype. A full sequence (``max_seq_len`` rows) is left
+    unchanged and sets bit 0 of ``status`` (a CUDA int32 tensor), if given; a page outside the
+    cache sets bit 1."""
     if kv_cache.dtype not in _DT or not kv_cache.is_cuda or kv_cache.stride(-1) != 1:
         raise RuntimeError("kv_cache must be a CUDA fp16/bf16 tensor with unit inner stride")
     for t, name in ((c_t, "c_t"), (k_rope, "k_rope")):
@@ -403,11 +417,17 @@ def mla_cache_append(kv_cache: torch.Tensor, c_t: torch.Tensor, k_rope: torch.Te
         raise RuntimeError("kv_offsets must be a CUDA int64 tensor of shape (batch,)")
     if status is not None and (status.dtype != torch.int32 or not status.is_cuda):
         raise RuntimeError("status must be a CUDA int32 tensor")
+    if page_table is not None and (page_table.dtype != torch.int32 or not page_table.is_cuda
+                                   or page_table.dim() != 2 or page_table.size(0) != B
+                                   or not page_table.is_contiguous()):
+        raise RuntimeError("page_table must be a contiguous CUDA int32 tensor of shape (batch, max_pages)")
     cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
     stride = kv_cache.stride(0) if kv_cache.dim() == 2 else 0
     lib = _lib.load()
+    max_pages = int(page_table.size(1)) if page_table is not None else 0
     _lib.check(lib.mla_cache_append(C.byref(cfg), _DT[kv_cache.dtype], C.c_void_p(kv_cache.data_ptr()),
-                                    C.c_int64(stride), B, C.c_void_p(c_t.data_ptr()),
+                                    C.c_int64(stride), C.c_int64(kv_cache.size(0)), B, C.c_void_p(c_t.data_ptr()),
                                     C.c_void_p(k_rope.data_ptr()), C.c_void_p(_ptr(kv_offsets)),
+                                    C.c_void_p(_ptr(page_table)), int(page_rows), max_pages,
                                     C.c_void_p(seq_lens.data_ptr()), int(max_seq_len),
                                     C.c_void_p(_ptr(status)), C.c_void_p(_stream(kv_cache.device))))

@@ -59,7 +59,8 @@ class MlaDecodeArgs(C.Structure):
                 ("kv_pos_offset", C.c_int), ("q_absorbed", C.c_void_p), ("q_nope", C.c_void_p),
                 ("W_UK", C.c_void_p), ("q_rope", C.c_void_p), ("W_UV", C.c_void_p),
                 ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p), ("softmax_scale", C.c_float),
-                ("output", C.c_void_p), ("kernel", C.c_int), ("timer", C.c_void_p)]
+                ("output", C.c_void_p), ("kernel", C.c_int), ("timer", C.c_void_p),
+                ("page_table", C.c_void_p), ("page_rows", C.c_int), ("max_pages", C.c_int)]
 
 KERNEL_AUTO = 0
 KERNEL_TENSOR_CORE = 1
@@ -80,8 +81,9 @@ SIGNATURES = {
                                      C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "mla_combine_partials": (C.c_int, [C.POINTER(MlaConfig), C.c_int, C.c_int, C.c_int, C.c_void_p,
                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
-    "mla_cache_append": (C.c_int, [C.POINTER(MlaConfig), C.c_int, C.c_void_p, C.c_int64, C.c_int, C.c_void_p,
-                                   C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    "mla_cache_append": (C.c_int, [C.POINTER(MlaConfig), C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_int,
+                                   C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                   C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "mla_timer_create": (C.c_int, [C.POINTER(C.c_void_p)]),
     "mla_timer_destroy": (C.c_int, [C.c_void_p]),
     "mla_timer_decode_ms": (C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),

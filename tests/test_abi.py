@@ -47,7 +47,7 @@ int main(void) {
   printf("mla_decode_args_t %zu\n", sizeof(mla_decode_args_t));
   P(mla_decode_args_t, kv_total_rows) P(mla_decode_args_t, seq_lens_host) P(mla_decode_args_t, softmax_scale)
   P(mla_decode_args_t, output) P(mla_decode_args_t, kernel) P(mla_fused_params_t, cfg)
-  P(mla_batched_fused_params_t, output)
+  P(mla_batched_fused_params_t, output) P(mla_decode_args_t, page_table) P(mla_decode_args_t, max_pages)
   return 0;
 }
 '''
@@ -70,6 +70,8 @@ int main(void) {
         "mla_decode_args_t.kernel": _lib.MlaDecodeArgs.kernel.offset,
         "mla_fused_params_t.cfg": _lib.MlaFusedParams.cfg.offset,
         "mla_batched_fused_params_t.output": _lib.MlaBatchedFusedParams.output.offset,
+        "mla_decode_args_t.page_table": _lib.MlaDecodeArgs.page_table.offset,
+        "mla_decode_args_t.max_pages": _lib.MlaDecodeArgs.max_pages.offset,
     }
     for k, v in want.items():
         assert int(got[k]) == v, (k, got[k], v)
@@ -98,12 +100,14 @@ def test_validation_without_gpu():
     assert lib.mla_launch_fused(C.byref(p), _lib.DTYPE_F16, None) == _lib.MLA_ERR_INVALID_ARGUMENT
     # cache append: null pointers, a bad batch and a bad dtype are rejected before any launch
     fake = C.c_void_p(256)
-    assert lib.mla_cache_append(C.byref(ok), _lib.DTYPE_BF16, None, 0, 1, fake, fake, None, fake, 8, None,
-                                None) == _lib.MLA_ERR_INVALID_ARGUMENT
-    assert lib.mla_cache_append(C.byref(ok), _lib.DTYPE_BF16, fake, 0, 0, fake, fake, None, fake, 8, None,
-                                None) == _lib.MLA_ERR_INVALID_ARGUMENT
-    assert lib.mla_cache_append(C.byref(ok), _lib.DTYPE_F32, fake, 0, 1, fake, fake, None, fake, 8, None,
-                                None) == _lib.MLA_ERR_UNSUPPORTED
+    def append(dtype=_lib.DTYPE_BF16, kv=fake, total=0, batch=1, pages=None, page_rows=0, max_pages=0):
+        return lib.mla_cache_append(C.byref(ok), dtype, kv, 0, total, batch, fake, fake, None, pages, page_rows,
+                                    max_pages, fake, 8, None, None)
+    assert append(kv=None) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert append(batch=0) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert append(dtype=_lib.DTYPE_F32) == _lib.MLA_ERR_UNSUPPORTED
+    assert append(pages=fake, page_rows=64, max_pages=1) == _lib.MLA_ERR_INVALID_ARGUMENT    # no kv_total_rows
+    assert append(pages=fake, page_rows=4, max_pages=1, total=64) == _lib.MLA_ERR_INVALID_ARGUMENT  # 4 < 8 rows
     assert lib.mla_version().startswith(b"latent-attn-b200")
 
 

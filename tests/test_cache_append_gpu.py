@@ -101,3 +101,90 @@ def test_decode_after_device_appends_equals_direct_cache():
     out_b = mla_decode(direct, qr, W_UV, cos, sin, cfg,
                        seq_lens=torch.tensor(final, dtype=torch.int32, device=dev), **args)
     assert torch.equal(out_a, out_b)
+
+
+def _paged_copy(kv, offs, lens, page_rows, max_pages, n_pool_pages, seed):
+    """Scatter each sequence's rows into shuffled pages of a pool pre-filled with noise; unused
+    page-table entries are -1 (never read for positions below the sequence length)."""
+    g = torch.Generator().manual_seed(seed)
+    pool = torch.randn(n_pool_pages * page_rows, kv.size(1), generator=g).to(kv.dtype).to(kv.device)
+    perm = torch.randperm(n_pool_pages, generator=g).tolist()
+    table = torch.full((len(lens), max_pages), -1, dtype=torch.int32)
+    nxt = 0
+    for b, n in enumerate(lens):
+        for k in range((n + page_rows - 1) // page_rows):
+            pid = perm[nxt]
+            nxt += 1
+            table[b, k] = pid
+            m = min(page_rows, n - k * page_rows)
+            pool[pid * page_rows:pid * page_rows + m] = kv[offs[b] + k * page_rows:offs[b] + k * page_rows + m]
+    return pool, table.to(kv.device)
+
+
+@pytest.mark.parametrize("page_rows", [64, 128])
+@pytest.mark.parametrize("kernel", [1, 2])          # tensor-core, CUDA-core decode
+def test_paged_decode_equals_contiguous(page_rows, kernel):
+    dev = torch.device("cuda")
+    cfg = MLAConfig.deepseek_v2()
+    lens, cap = [300, 1000, 327], 1024
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=lens, seed=31)
+    kv = inp.kv_cache.to(dev)
+    max_pages = cap // page_rows
+    need = sum((n + page_rows - 1) // page_rows for n in lens)
+    pool, table = _paged_copy(kv, inp.kv_offsets, lens, page_rows, max_pages, need + 5, seed=page_rows)
+    cos, sin = synthetic.build_rope_tables(cap, 64, device=dev)
+    lens_d = torch.tensor(lens, dtype=torch.int32, device=dev)
+    common = dict(q_nope=inp.q_nope.float().to(dev), W_UK=inp.W_UK.to(dev), seq_lens=lens_d, max_seq_len=cap,
+                  kernel=kernel)
+    qr, W_UV = inp.q_rope.float().to(dev), inp.W_UV.to(dev)
+    contig = mla_decode(kv, qr, W_UV, cos, sin, cfg,
+                        kv_offsets=torch.tensor(inp.kv_offsets, dtype=torch.int64, device=dev), **common)
+    paged = mla_decode(pool, qr, W_UV, cos, sin, cfg, page_table=table, page_rows=page_rows, **common)
+    assert torch.isfinite(paged).all()
+    assert torch.equal(paged, contig)
+
+    # a page id outside the pool reads nothing and makes the output NaN
+    bad = table.clone()
+    bad[1, 3] = 1 << 20
+    broken = mla_decode(pool, qr, W_UV, cos, sin, cfg, page_table=bad, page_rows=page_rows, **common)
+    assert torch.isnan(broken).any()
+
+
+def test_paged_append_then_decode():
+    """Device appends through a page table cross a page boundary and land in the mapped pages;
+    the decode over the pool then equals the contiguous decode of the same rows."""
+    dev = torch.device("cuda")
+    cfg = MLAConfig.deepseek_v2()
+    page_rows, cap, pre, steps = 64, 256, [70, 62], 4
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[cap, cap], seed=41)
+    rows = inp.kv_cache.to(dev)                                       # (2 * cap, 576)
+    offs = [0, cap]
+    pool, table = _paged_copy(rows, offs, pre, page_rows, cap // page_rows, 12, seed=5)
+    for b in range(2):                                                # pages for the rows still to come
+        used = set(table[b].tolist()) | set(table[1 - b].tolist())
+        free = [p for p in range(12) if p not in used]
+        for k in range(cap // page_rows):
+            if int(table[b, k]) < 0:
+                table[b, k] = free.pop(0)
+                used.add(int(table[b, k]))
+    lens = torch.tensor(pre, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    for s in range(steps):
+        new = torch.stack([rows[offs[b] + pre[b] + s] for b in range(2)])
+        _C.mla_cache_append(pool, new[:, :512].contiguous(), new[:, 512:].contiguous(), lens, cap,
+                            cfg.d_model, 512, 128, 64, 128, 128, page_table=table, page_rows=page_rows,
+                            status=status)
+    final = [n + steps for n in pre]
+    torch.cuda.synchronize()
+    assert lens.cpu().tolist() == final and int(status.item()) == 0
+    for b in range(2):
+        for p in range(pre[b], final[b]):
+            r = int(table[b, p // page_rows]) * page_rows + p % page_rows
+            assert torch.equal(pool[r], rows[offs[b] + p])
+    cos, sin = synthetic.build_rope_tables(cap, 64, device=dev)
+    common = dict(q_nope=inp.q_nope.float().to(dev), W_UK=inp.W_UK.to(dev), seq_lens=lens, max_seq_len=cap)
+    qr, W_UV = inp.q_rope.float().to(dev), inp.W_UV.to(dev)
+    paged = mla_decode(pool, qr, W_UV, cos, sin, cfg, page_table=table, page_rows=page_rows, **common)
+    contig = mla_decode(rows, qr, W_UV, cos, sin, cfg,
+                        kv_offsets=torch.tensor(offs, dtype=torch.int64, device=dev), **common)
+    assert torch.equal(paged, contig)
