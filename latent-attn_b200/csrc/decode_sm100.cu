@@ -230,7 +230,10 @@ __device__ __forceinline__ float2 f2_sub(float2 a, float2 b) {
 
 }  // namespace
 
-template <typename T>
+// kPaged: the cache is paged (the tile's row comes from the page table). A separate instantiation,
+// so the contiguous layout runs without the lookup: the kernel is sensitive to its instruction
+// footprint, and the lookup alone cost 3.6% at B = 256.
+template <typename T, bool kPaged>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_rope,
                     const DecodePlan P, const T* __restrict__ qpack, const float* __restrict__ cos_tab,
@@ -313,9 +316,10 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             int issued = 0;
             for (int i = 0; it.valid(); ++i, it.next(P)) {
                 const int st = i % kStages;
-                // the tile's cache row (a page-table read in the paged layout, issued before the
-                // stage wait so its latency overlaps it)
-                const long long kvr = tile_kv_row(P, it.g, it.row0, it.pos0());
+                // paged: the tile's cache row from the page table, read before the stage wait so its
+                // latency overlaps it
+                long long kvr = 0;
+                if constexpr (kPaged) kvr = tile_kv_row(P, it.g, it.row0, it.pos0());
                 if (i >= kStages &&
                     !mbar_wait(smem_u32(&bars->kv_empty[st]), ((i / kStages) - 1) & 1, err, code(kWaitProducer))) {
                     note_fail(err, kWaitProducer, i);
@@ -323,9 +327,12 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                 }
                 const uint32_t full = smem_u32(&bars->kv_full[st]);
                 mbar_arrive_expect_tx(full, kStageBytes);
-                // a page outside the cache: the loads start below row 0 and read zeros
-                if (kvr < 0) atomicCAS(const_cast<int*>(err), 0, kStatusBadPage);
-                const int y = kvr < 0 ? -2 * kTileN : static_cast<int>(kvr);
+                int y = static_cast<int>(it.row0 + it.pos0());
+                if constexpr (kPaged) {
+                    // a page outside the cache: the loads start below row 0 and read zeros
+                    if (kvr < 0) atomicCAS(const_cast<int*>(err), 0, kStatusBadPage);
+                    y = kvr < 0 ? -2 * kTileN : static_cast<int>(kvr);
+                }
                 const uint32_t dst = stages_u32 + st * kStageBytes;
                 // rope boxes: columns 16 r + {0, 8} and 32 + 16 r + {0, 8} of k_rope
                 for (int b = 0; b < 4; ++b)
@@ -853,8 +860,10 @@ cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack
     if (!make_tmap_2d_16b(&tmap, kv, rows, 576, stride, 64, 64) ||
         !make_tmap_2d_16b(&tmap_rope, kv, rows, 576, stride, 64, 8, CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
-    cudaError_t e =
-        ensure_dynamic_smem(reinterpret_cast<const void*>(decode_sm100_kernel<T>), static_cast<int>(kSmemBytes));
+    const bool paged = P.page_table != nullptr;
+    const void* kernel = paged ? reinterpret_cast<const void*>(decode_sm100_kernel<T, true>)
+                               : reinterpret_cast<const void*>(decode_sm100_kernel<T, false>);
+    cudaError_t e = ensure_dynamic_smem(kernel, static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * P.W);
@@ -866,7 +875,10 @@ cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    e = cudaLaunchKernelEx(&cfg, decode_sm100_kernel<T>, tmap, tmap_rope, P, qpack, cos, sin, rec_ml, rec_o);
+    if (paged)
+        e = cudaLaunchKernelEx(&cfg, decode_sm100_kernel<T, true>, tmap, tmap_rope, P, qpack, cos, sin, rec_ml, rec_o);
+    else
+        e = cudaLaunchKernelEx(&cfg, decode_sm100_kernel<T, false>, tmap, tmap_rope, P, qpack, cos, sin, rec_ml, rec_o);
     count_launches(1);
     return e != cudaSuccess ? e : cudaGetLastError();
 }
