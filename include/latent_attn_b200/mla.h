@@ -161,7 +161,7 @@ typedef struct mla_decode_args {
   const void* W_UK;             /* (H * dn, d_c), required with q_nope */
   const float* q_rope;          /* (B, H, d_R) fp32, already rotated to the query position */
   const void* W_UV;             /* (H * dv, d_c) */
-  const float* rope_cos;        /* (kv_pos_offset + max_seq_len, d_R/2) fp32 */
+  const float* rope_cos;        /* (kv_pos_offset + max_seq_len, d_R/2) fp32, or NULL (see rope_theta) */
   const float* rope_sin;
   float softmax_scale;          /* 0: 1 / sqrt(dn + d_R) */
   float* output;                /* (B, H, dv) fp32 */
@@ -175,6 +175,13 @@ typedef struct mla_decode_args {
   const int* page_table;        /* device (B, max_pages) int32 page ids, or NULL (contiguous layout) */
   int page_rows;                /* rows per page, a positive multiple of 64 */
   int max_pages;                /* page-table entries per sequence, >= ceil(max_seq_len / page_rows) */
+  /* On-the-fly RoPE. With rope_cos and rope_sin both NULL the decode kernels compute the
+   * rotation of each cache row themselves, as the reference's table builder defines it
+   * (latent_attn/__init__.py:31-38): freq_i = rope_theta^(-2i / d_R) (a double-precision power
+   * rounded to fp32), angle = (float)pos * freq_i in fp32, then cos / sin of the angle after an
+   * exact double-precision reduction to [-pi, pi]. No table is read. 0 means 10000. Ignored
+   * when tables are given; needs qk_rope_head_dim <= 128. */
+  float rope_theta;
 } mla_decode_args_t;
 
 enum { MLA_KERNEL_AUTO = 0, MLA_KERNEL_TENSOR_CORE = 1, MLA_KERNEL_CUDA_CORE = 2 };
@@ -212,10 +219,11 @@ MLA_API mla_status_t mla_combine_partials(const mla_config_t* cfg, mla_dtype_t d
  * - c_t (batch, d_c) and k_rope (batch, d_R): device, element type `dtype`.
  * - seq_lens (batch,) int32 device, read and advanced; kv_offsets (batch,) int64 device or
  *   NULL; page_table (batch, max_pages) int32 device or NULL (page_rows > 0 with it).
- * - kv_total_rows: rows of kv_cache; required with page_table (a page outside it is not
- *   written), 0 otherwise allowed.
+ * - kv_total_rows: rows of kv_cache; required with page_table or kv_offsets (a row outside
+ *   it is not written), 0 allowed only without both.
  * - A sequence that already holds max_seq_len rows is left unchanged and sets bit 0 of
- *   *status; a page id outside the cache sets bit 1 (status: a device int, or NULL).
+ *   *status; a row outside the cache (a bad page id or offset) is not written and sets
+ *   bit 1 (status: a device int, or NULL).
  * - kv_row_stride: elements between rows, 0 meaning d_c + d_R. */
 MLA_API mla_status_t mla_cache_append(const mla_config_t* cfg, mla_dtype_t dtype, void* kv_cache,
                               int64_t kv_row_stride, int64_t kv_total_rows, int batch, const void* c_t,

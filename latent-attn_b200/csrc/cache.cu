@@ -17,7 +17,8 @@ namespace {
 // One CTA per sequence b: the row of position seq_lens[b] (contiguous: kv_offsets[b] or
 // b * max_len plus the position; paged: through the page table) receives the new values, then
 // seq_lens[b] advances. A sequence already holding max_len rows is left as it is and reported
-// through *status (bit 0); so is a page outside the cache (bit 1).
+// through *status (bit 0); so is a row outside the cache's kv_rows rows, from a bad page id or
+// offset (bit 1).
 template <typename T>
 __global__ void cache_append_kernel(T* __restrict__ kv, long long stride, long long kv_rows, int dc, int dR,
                                     const T* __restrict__ c_t, const T* __restrict__ k_rope,
@@ -34,12 +35,18 @@ __global__ void cache_append_kernel(T* __restrict__ kv, long long stride, long l
     if (pages) {
         const int pg = pages[static_cast<long long>(b) * max_pages + pos / page_rows];
         row = static_cast<long long>(pg) * page_rows + pos % page_rows;
-        if (pg < 0 || static_cast<long long>(pg + 1) * page_rows > kv_rows) {
+        // 64-bit arithmetic: pg + 1 must not wrap for a page id near INT_MAX
+        if (pg < 0 || (static_cast<long long>(pg) + 1) * page_rows > kv_rows) {
             if (threadIdx.x == 0 && status) atomicOr(status, 2);
             return;
         }
     } else {
         row = (offs ? offs[b] : static_cast<long long>(b) * max_len) + pos;
+        // a row outside the cache (a bad offset) is not written
+        if (row < 0 || (kv_rows > 0 && row >= kv_rows)) {
+            if (threadIdx.x == 0 && status) atomicOr(status, 2);
+            return;
+        }
     }
     T* dst = kv + row * stride;
     const T* src_c = c_t + static_cast<long long>(b) * dc;

@@ -6,8 +6,8 @@
 // Block = (worker w, row block of 8 rows); warp i owns row 8*blockIdx.y + i.
 // Per tile of 32 positions the block stages the packed rows in shared memory
 // (row stride padded by one 32-bit word so "lane = position" reads are
-// conflict-free), rotates the tile's k_rope in fp32 with the caller's tables
-// (the rotation of src/fused_mla.cu:34-54), then every warp scores its row
+// conflict-free), rotates the tile's k_rope in fp32 with the caller's tables or
+// on-the-fly cos / sin (the rotation of src/fused_mla.cu:34-54), then every warp scores its row
 // against the 32 positions (lane j <-> position j), does an online-softmax
 // update in log2 units, and accumulates o += 2^(s-m) * c_t with lane l owning
 // latent columns l, l+32, ... .
@@ -93,7 +93,8 @@ decode_simt_kernel(DecodePlan P, const T* __restrict__ kv, const T* __restrict__
                     const T* kr = reinterpret_cast<const T*>(tile_w + j * ldt) + dc;
                     float k0 = ElemTraits<T>::to_f(kr[d]), k1 = ElemTraits<T>::to_f(kr[d + half]);
                     long long pos = static_cast<long long>(P.kv_pos_offset) + p0 + j;
-                    float c = rope_cos[pos * half + d], s = rope_sin[pos * half + d];
+                    float c, s;
+                    rope_cs(P, rope_cos, rope_sin, pos, d, &c, &s);
                     r0 = k0 * c - k1 * s;
                     r1 = k0 * s + k1 * c;
                 }

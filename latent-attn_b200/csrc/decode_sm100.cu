@@ -27,8 +27,8 @@
 //               their inputs are ready, in tile order per kind
 //   warps 2-3   tile transform: zero rows past the sequence end, rotate the CTA's
 //               k_rope pairs in place with the caller's cos/sin tables, read from global
-//               memory one tile ahead (the rotation of src/fused_mla.cu:34-54 of the
-//               reference)
+//               memory one tile ahead, or with cos/sin computed on the fly (the rotation of
+//               src/fused_mla.cu:34-54 of the reference)
 //   warps 4-7   softmax set 0: the even tiles of the worker
 //   warps 8-11  softmax set 1: the odd tiles (thread = query row = TMEM lane)
 // The two softmax sets work on consecutive tiles at the same time: while one waits
@@ -311,6 +311,10 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
+            // a paged producer may record kStatusBadPage: the previous kernel clears the status
+            // words, so wait for it first (with variable lengths every role waited already)
+            if constexpr (kPaged)
+                if (uniform) pdl_wait();
             TileIter it;
             it.init(P, tb, te);
             int issued = 0;
@@ -471,14 +475,27 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             for (int u = 0; u < kItems; ++u) {
                 const int item = tt + kTransformThreads * u, p = item >> 1, h = item & 1;
                 if (p < tnp) {
-                    const long long off = (static_cast<long long>(P.kv_pos_offset) + ti.pos0() + p) * 32 +
-                                          16 * static_cast<int>(rank) + 8 * h;
-                    const float4* c4 = reinterpret_cast<const float4*>(cos_tab + off);
-                    const float4* s4 = reinterpret_cast<const float4*>(sin_tab + off);
-                    tab_next[u][0] = __ldg(c4);
-                    tab_next[u][1] = __ldg(c4 + 1);
-                    tab_next[u][2] = __ldg(s4);
-                    tab_next[u][3] = __ldg(s4 + 1);
+                    const long long pos = static_cast<long long>(P.kv_pos_offset) + ti.pos0() + p;
+                    const int f0 = 16 * static_cast<int>(rank) + 8 * h;
+                    if (P.rope_otf) {
+                        // computed, not read: no table traffic and no load latency
+                        float cs[8], sn[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            rope_sincos(static_cast<float>(pos) * P.rope_freq[f0 + e], &sn[e], &cs[e]);
+                        tab_next[u][0] = make_float4(cs[0], cs[1], cs[2], cs[3]);
+                        tab_next[u][1] = make_float4(cs[4], cs[5], cs[6], cs[7]);
+                        tab_next[u][2] = make_float4(sn[0], sn[1], sn[2], sn[3]);
+                        tab_next[u][3] = make_float4(sn[4], sn[5], sn[6], sn[7]);
+                    } else {
+                        const long long off = pos * 32 + f0;
+                        const float4* c4 = reinterpret_cast<const float4*>(cos_tab + off);
+                        const float4* s4 = reinterpret_cast<const float4*>(sin_tab + off);
+                        tab_next[u][0] = __ldg(c4);
+                        tab_next[u][1] = __ldg(c4 + 1);
+                        tab_next[u][2] = __ldg(s4);
+                        tab_next[u][3] = __ldg(s4 + 1);
+                    }
                 }
             }
         };
@@ -856,7 +873,8 @@ cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack
     CUtensorMap tmap, tmap_rope;
     const uint64_t rows = static_cast<uint64_t>(P.kv_rows), stride = static_cast<uint64_t>(P.row_stride);
     // the tables (kv_pos_offset + max_len rows of d_R / 2 = 32 floats) are read as float4
-    if ((reinterpret_cast<uintptr_t>(cos) | reinterpret_cast<uintptr_t>(sin)) & 15u) return cudaErrorInvalidValue;
+    if (!P.rope_otf && ((reinterpret_cast<uintptr_t>(cos) | reinterpret_cast<uintptr_t>(sin)) & 15u))
+        return cudaErrorInvalidValue;
     if (!make_tmap_2d_16b(&tmap, kv, rows, 576, stride, 64, 64) ||
         !make_tmap_2d_16b(&tmap_rope, kv, rows, 576, stride, 64, 8, CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;

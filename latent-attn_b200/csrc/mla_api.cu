@@ -143,7 +143,13 @@ mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan
     if (!a->kv_cache) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_cache is null");
     if (!a->q_rope) return fail(MLA_ERR_INVALID_ARGUMENT, "q_rope is null");
     if (!a->W_UV) return fail(MLA_ERR_INVALID_ARGUMENT, "W_UV is null");
-    if (!a->rope_cos || !a->rope_sin) return fail(MLA_ERR_INVALID_ARGUMENT, "rope_cos / rope_sin are null");
+    if ((a->rope_cos == nullptr) != (a->rope_sin == nullptr))
+        return fail(MLA_ERR_INVALID_ARGUMENT, "give both rope_cos and rope_sin, or neither (on-the-fly RoPE)");
+    const bool rope_otf = a->rope_cos == nullptr;
+    if (rope_otf && dR > 2 * mla::kMaxRopeHalf)
+        return fail(MLA_ERR_UNSUPPORTED, "on-the-fly RoPE needs qk_rope_head_dim <= %d (got %d)",
+                    2 * mla::kMaxRopeHalf, dR);
+    if (rope_otf && a->rope_theta < 0.f) return fail(MLA_ERR_INVALID_ARGUMENT, "rope_theta must be >= 0");
     if (!a->q_absorbed && !(a->q_nope && a->W_UK))
         return fail(MLA_ERR_INVALID_ARGUMENT, "give q_absorbed, or q_nope together with W_UK");
     const int64_t stride = a->kv_row_stride ? a->kv_row_stride : (dc + dR);
@@ -173,6 +179,14 @@ mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan
     d.max_len = a->max_seq_len;
     d.kv_offsets = a->kv_offsets;
     d.kv_pos_offset = a->kv_pos_offset;
+    if (rope_otf) {
+        // freq_i = theta^(-2i/d_R) (latent_attn/__init__.py:34-36 of the reference), the
+        // double-precision power rounded once to fp32
+        const double theta = a->rope_theta > 0.f ? static_cast<double>(a->rope_theta) : 10000.0;
+        d.rope_otf = 1;
+        for (int i = 0; i < dR / 2; ++i)
+            d.rope_freq[i] = static_cast<float>(std::pow(theta, -2.0 * i / static_cast<double>(dR)));
+    }
     if (a->kv_total_rows < 0) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_total_rows must be >= 0");
     if (a->page_table) {
         if (a->shared_cache || a->kv_offsets)
@@ -461,6 +475,9 @@ mla_status_t mla_cache_append(const mla_config_t* cfg, mla_dtype_t dtype, void* 
     const int64_t stride = kv_row_stride ? kv_row_stride : (dc + dR);
     if (stride < dc + dR) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_row_stride %lld < d_c + d_R", (long long)stride);
     if (kv_total_rows < 0) return fail(MLA_ERR_INVALID_ARGUMENT, "kv_total_rows must be >= 0");
+    // as for mla_decode: rows addressed through offsets are checked against the cache's rows
+    if (kv_offsets && kv_total_rows <= 0)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "kv_total_rows is required with kv_offsets");
     if (page_table) {
         if (kv_offsets) return fail(MLA_ERR_INVALID_ARGUMENT, "page_table excludes kv_offsets");
         if (page_rows <= 0) return fail(MLA_ERR_INVALID_ARGUMENT, "page_rows must be positive, got %d", page_rows);
@@ -589,22 +606,25 @@ mla_status_t mla_launch_fused_noalloc(const mla_fused_params_t* p, mla_dtype_t d
     a.rope_cos = p->rope_cos;
     a.rope_sin = p->rope_sin;
     a.output = p->output;
-    // Largest worker count whose workspace fits the static array (fewer workers,
-    // fewer partial records); a problem that does not fit even with one worker is
-    // rejected before anything is launched.
+    // Largest worker count whose workspace fits the static array (fewer workers, fewer
+    // partial records). Each worker beyond the first adds one record of kGroupRows rows of
+    // (m, l, o[d_c]) fp32, a multiple of the 256-byte alignment, so the scratch grows by
+    // exactly that much per worker and the cap follows from the one-worker size. A problem
+    // that does not fit even with one worker is rejected before anything is launched.
     Plan pl;
-    st = make_plan(p->cfg, &a, &pl);
+    st = make_plan(p->cfg, &a, &pl, 1);
     if (st != MLA_OK) return st;
-    int workers = pl.dp.W;
-    while (workers > 1 && pl.total > MLA_NOALLOC_SCRATCH_BYTES) {
-        --workers;
-        st = make_plan(p->cfg, &a, &pl, workers);
-        if (st != MLA_OK) return st;
-    }
     if (pl.total > MLA_NOALLOC_SCRATCH_BYTES)
         return fail(MLA_ERR_UNSUPPORTED,
                     "problem needs %zu bytes of scratch; the static scratch of mla_launch_fused_noalloc holds %u",
                     pl.total, static_cast<unsigned>(MLA_NOALLOC_SCRATCH_BYTES));
+    const size_t per_worker = static_cast<size_t>(mla::kGroupRows) * (2 + p->cfg->kv_lora_rank) * sizeof(float);
+    const size_t extra = (MLA_NOALLOC_SCRATCH_BYTES - pl.total) / per_worker;
+    const int workers = static_cast<int>(extra > 4096 ? 4097 : extra + 1);
+    st = make_plan(p->cfg, &a, &pl, workers);
+    if (st != MLA_OK) return st;
+    if (pl.total > MLA_NOALLOC_SCRATCH_BYTES)  // the per-worker step above is exact; kept as a guard
+        return fail(MLA_ERR_UNSUPPORTED, "static scratch plan does not fit (%zu bytes)", pl.total);
     void* scratch = nullptr;
     st = noalloc_scratch(&scratch);
     if (st != MLA_OK) return st;

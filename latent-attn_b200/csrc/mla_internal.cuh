@@ -26,6 +26,7 @@
 namespace mla {
 
 constexpr int kGroupRows = 128;  // query rows per group (the tcgen05 M tile)
+constexpr int kMaxRopeHalf = 64;  // on-the-fly RoPE: d_R <= 128
 
 struct DecodePlan {
     // dims
@@ -51,6 +52,10 @@ struct DecodePlan {
     // page_table[b * max_pages + p / page_rows] * page_rows + p % page_rows; page_rows % 64 == 0
     const int* page_table;
     int page_rows, max_pages;
+    // RoPE computed in the kernels instead of read from tables (the caller passed none):
+    // rope_freq[i] = theta^(-2i/d_R) rounded to fp32, i < d_R / 2 <= kMaxRopeHalf
+    int rope_otf;
+    float rope_freq[kMaxRopeHalf];
 };
 
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
@@ -133,8 +138,9 @@ __device__ inline int group_of_tile(const DecodePlan& P, int t) {
     return lo;
 }
 
-// The first kernel of a decode call clears the status words (the decode kernel writes
-// them only after a wait has failed, at least a millisecond after it starts).
+// The first kernel of a decode call clears the status words. The decode kernel writes them
+// only after its programmatic-dependency wait on that kernel (a bad page id), or after one of
+// its own waits has failed, at least a millisecond after it starts.
 __device__ inline void clear_status(const DecodePlan& P) {
     if (P.status && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x < 4)
         P.status[threadIdx.x] = 0;
@@ -173,6 +179,32 @@ __device__ inline void write_tile_prefix(const DecodePlan& P, int* prefix) {
 }
 
 __device__ inline int num_records(const DecodePlan& P) { return P.G + P.W - 1; }
+
+// cos and sin of an on-the-fly RoPE angle. The angle is an fp32 value of up to ~1.3e5 rad
+// (position x frequency, formed in fp32 as the reference's table builder forms it). It is
+// reduced to r in [-pi, pi] in double precision: with k <= 2^21 and a 53-bit 2 pi the reduced
+// value is exact to ~1e-10 rad before its rounding to fp32 (1.2e-7 rad). On [-pi, pi] the
+// hardware approximations have an absolute error below 4e-7, so cos and sin are within 5e-7 of
+// the exact values; the rotated key is then rounded to 16 bits (relative 4e-3 for bf16).
+__device__ __forceinline__ void rope_sincos(float angle, float* s, float* c) {
+    const double a = static_cast<double>(angle);
+    const double k = rint(a * 0.15915494309189535);  // 1 / (2 pi)
+    const float r = static_cast<float>(fma(-k, 6.283185307179586, a));
+    __sincosf(r, s, c);
+}
+
+// cos and sin of RoPE frequency i at absolute position pos: from the caller's tables
+// ((pos, d_R / 2) fp32) or, with P.rope_otf, computed.
+__device__ __forceinline__ void rope_cs(const DecodePlan& P, const float* cos_tab, const float* sin_tab,
+                                        long long pos, int i, float* c, float* s) {
+    if (P.rope_otf) {
+        rope_sincos(static_cast<float>(pos) * P.rope_freq[i], s, c);
+    } else {
+        const long long off = pos * (P.dR / 2) + i;
+        *c = cos_tab[off];
+        *s = sin_tab[off];
+    }
+}
 
 template <typename T> struct ElemTraits;
 template <> struct ElemTraits<__half> {

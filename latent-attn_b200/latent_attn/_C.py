@@ -80,7 +80,7 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 def _decode_args(dtype, batch, shared, kv_cache, max_seq_len, q_rope, W_UV, rope_cos, rope_sin, out,
                  q_absorbed=None, q_nope=None, W_UK=None, seq_lens=None, kv_offsets=None,
                  seq_lens_host=None, kv_pos_offset=0, softmax_scale=0.0, kv_row_stride=0, kernel=0,
-                 timer=None, page_table=None, page_rows=0):
+                 timer=None, page_table=None, page_rows=0, rope_theta=0.0):
     a = _lib.MlaDecodeArgs()
     a.dtype = _DT[dtype]
     a.batch = int(batch)
@@ -98,8 +98,10 @@ def _decode_args(dtype, batch, shared, kv_cache, max_seq_len, q_rope, W_UV, rope
     a.W_UK = _ptr(W_UK)
     a.q_rope = q_rope.data_ptr()
     a.W_UV = W_UV.data_ptr()
-    a.rope_cos = rope_cos.data_ptr()
-    a.rope_sin = rope_sin.data_ptr()
+    # no tables: the kernels compute cos / sin from rope_theta (on-the-fly RoPE)
+    a.rope_cos = _ptr(rope_cos)
+    a.rope_sin = _ptr(rope_sin)
+    a.rope_theta = float(rope_theta)
     a.softmax_scale = float(softmax_scale)
     a.output = _ptr(out)
     a.kernel = int(kernel)
@@ -236,6 +238,15 @@ def naive_mla_forward(kv_cache, W_UK, W_UV, q_nope, q_rope, rope_cos, rope_sin,
     return torch.einsum("hs,shv->hv", p, V).contiguous()
 
 
+def _check_tables(rope_cos, rope_sin):
+    """Both RoPE tables (fp32, contiguous, CUDA), or neither (on-the-fly RoPE)."""
+    if (rope_cos is None) != (rope_sin is None):
+        raise RuntimeError("give both rope_cos and rope_sin, or neither (on-the-fly RoPE)")
+    if rope_cos is not None:
+        _check_f32(rope_cos, "rope_cos")
+        _check_f32(rope_sin, "rope_sin")
+
+
 def _check_common(kv_cache, W_UV, rope_cos, rope_sin, seq_len, H, dv, dc, dR):
     if W_UV.dtype != kv_cache.dtype:
         raise RuntimeError(f"W_UV dtype {W_UV.dtype} must match kv_cache dtype {kv_cache.dtype}")
@@ -272,8 +283,9 @@ def _run_decode(cfg, dtype, batch, shared, kv_cache, max_seq_len, q_rope, W_UV, 
 # general decode (no reference counterpart)
 # ---------------------------------------------------------------------------
 
-def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor, rope_cos: torch.Tensor,
-               rope_sin: torch.Tensor, d_model: int, kv_lora_rank: int, qk_nope_head_dim: int,
+def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
+               rope_cos: Optional[torch.Tensor], rope_sin: Optional[torch.Tensor], d_model: int,
+               kv_lora_rank: int, qk_nope_head_dim: int,
                qk_rope_head_dim: int, num_heads: int, v_head_dim: int, *,
                q_absorbed: Optional[torch.Tensor] = None, q_nope: Optional[torch.Tensor] = None,
                W_UK: Optional[torch.Tensor] = None, seq_lens: Optional[torch.Tensor] = None,
@@ -282,7 +294,8 @@ def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
                kv_pos_offset: int = 0, softmax_scale: float = 0.0, kv_row_stride: int = 0,
                kernel: int = 0, out: Optional[torch.Tensor] = None,
                workspace: Optional[torch.Tensor] = None, timer=None,
-               page_table: Optional[torch.Tensor] = None, page_rows: int = 0) -> torch.Tensor:
+               page_table: Optional[torch.Tensor] = None, page_rows: int = 0,
+               rope_theta: float = 0.0) -> torch.Tensor:
     """General decode: (B, H, dv) fp32 for B sequences (or B tokens over one shared cache).
 
     Give ``q_absorbed`` (B, H, d_c) fp32, or ``q_nope`` (B, H, dn) fp32 with ``W_UK``
@@ -291,6 +304,9 @@ def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
     them every sequence has ``max_seq_len`` rows at ``b * max_seq_len``. With ``page_table``
     (B, max_pages) int32 (device) the cache is paged: position p of sequence b is row
     ``page_table[b, p // page_rows] * page_rows + p % page_rows`` (``page_rows`` a multiple of 64).
+    With ``rope_cos`` and ``rope_sin`` both ``None`` the kernels compute the RoPE rotation
+    themselves from ``rope_theta`` (0: 10000), as the reference's table builder defines it,
+    and read no table.
     """
     if kv_row_stride:
         if kv_cache.dtype not in _DT or not kv_cache.is_cuda or kv_cache.stride(-1) != 1:
@@ -299,8 +315,7 @@ def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
         _check_half(kv_cache, "kv_cache")
     _check_half(W_UV, "W_UV")
     _check_f32(q_rope, "q_rope")
-    _check_f32(rope_cos, "rope_cos")
-    _check_f32(rope_sin, "rope_sin")
+    _check_tables(rope_cos, rope_sin)
     cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
     if q_absorbed is not None:
         _check_f32(q_absorbed, "q_absorbed")
@@ -342,19 +357,22 @@ def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
                 rope_sin, out, workspace=workspace, q_absorbed=q_absorbed, q_nope=q_nope, W_UK=W_UK,
                 seq_lens=seq_lens, kv_offsets=kv_offsets, seq_lens_host=host_arr,
                 kv_pos_offset=kv_pos_offset, softmax_scale=softmax_scale, kv_row_stride=kv_row_stride,
-                kernel=kernel, timer=timer, page_table=page_table, page_rows=page_rows)
+                kernel=kernel, timer=timer, page_table=page_table, page_rows=page_rows, rope_theta=rope_theta)
     return out
 
 
 def mla_decode_partial(kv_cache, q_rope, W_UV, rope_cos, rope_sin, d_model, kv_lora_rank,
                        qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim, *,
                        q_absorbed=None, q_nope=None, W_UK=None, kv_pos_offset: int = 0,
-                       softmax_scale: float = 0.0, workspace=None, kernel: int = 0, timer=None):
+                       softmax_scale: float = 0.0, workspace=None, kernel: int = 0, timer=None,
+                       rope_theta: float = 0.0):
     """One KV-range shard of a single-token-per-sequence decode over all rows of
     ``kv_cache`` (B sequences of ``kv_cache.size(0) // B`` rows). Returns
     (ml (B, H, 2), o (B, H, d_c)): natural-log max, sum of exponentials, and the
-    unnormalised latent sum, ready for ``mla_combine_partials``."""
+    unnormalised latent sum, ready for ``mla_combine_partials``. ``rope_cos`` / ``rope_sin``
+    ``None``: on-the-fly RoPE from ``rope_theta``."""
     _check_half(kv_cache, "kv_cache")
+    _check_tables(rope_cos, rope_sin)
     cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
     B = q_rope.size(0)
     L = kv_cache.size(0) // B
@@ -363,7 +381,7 @@ def mla_decode_partial(kv_cache, q_rope, W_UV, rope_cos, rope_sin, d_model, kv_l
     args = _decode_args(kv_cache.dtype, B, False, kv_cache, L, q_rope, W_UV, rope_cos, rope_sin, None,
                         q_absorbed=q_absorbed, q_nope=None if q_absorbed is not None else q_nope,
                         W_UK=None if q_absorbed is not None else W_UK, kv_pos_offset=kv_pos_offset,
-                        softmax_scale=softmax_scale, kernel=kernel, timer=timer)
+                        softmax_scale=softmax_scale, kernel=kernel, timer=timer, rope_theta=rope_theta)
     ws = _workspace(cfg, args, kv_cache.device, workspace)
     lib = _lib.load()
     _lib.check(lib.mla_decode_partial(C.byref(cfg), C.byref(args), C.c_void_p(ml.data_ptr()),

@@ -60,7 +60,8 @@ class MlaDecodeArgs(C.Structure):
                 ("W_UK", C.c_void_p), ("q_rope", C.c_void_p), ("W_UV", C.c_void_p),
                 ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p), ("softmax_scale", C.c_float),
                 ("output", C.c_void_p), ("kernel", C.c_int), ("timer", C.c_void_p),
-                ("page_table", C.c_void_p), ("page_rows", C.c_int), ("max_pages", C.c_int)]
+                ("page_table", C.c_void_p), ("page_rows", C.c_int), ("max_pages", C.c_int),
+                ("rope_theta", C.c_float)]
 
 KERNEL_AUTO = 0
 KERNEL_TENSOR_CORE = 1

@@ -67,7 +67,7 @@ def batched_fused_mla(kv_cache: torch.Tensor, q_absorbed: torch.Tensor, q_rope: 
 
 
 def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
-               rope_cos: torch.Tensor, rope_sin: torch.Tensor, cfg: "MLAConfig", *,
+               rope_cos: Optional[torch.Tensor], rope_sin: Optional[torch.Tensor], cfg: "MLAConfig", *,
                q_absorbed: Optional[torch.Tensor] = None, q_nope: Optional[torch.Tensor] = None,
                W_UK: Optional[torch.Tensor] = None, seq_lens: Optional[torch.Tensor] = None,
                kv_offsets: Optional[torch.Tensor] = None, max_seq_len: Optional[int] = None,
@@ -75,13 +75,16 @@ def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
                kv_pos_offset: int = 0, softmax_scale: float = 0.0, kv_row_stride: int = 0,
                kernel: int = 0, out: Optional[torch.Tensor] = None,
                workspace: Optional[torch.Tensor] = None, timer=None,
-               page_table: Optional[torch.Tensor] = None, page_rows: int = 0) -> torch.Tensor:
+               page_table: Optional[torch.Tensor] = None, page_rows: int = 0,
+               rope_theta: float = 0.0) -> torch.Tensor:
     """General decode over a (variable-length, optionally paged) batch; see ``_C.mla_decode``.
-    Returns (B, H, dv) fp32."""
+    ``rope_cos`` / ``rope_sin`` may both be ``None``: the kernels then compute the RoPE rotation
+    from ``rope_theta`` (0: 10000). Returns (B, H, dv) fp32."""
     return _load_ext().mla_decode(kv_cache, q_rope, W_UV, rope_cos, rope_sin, *_dims(cfg),
                                   q_absorbed=q_absorbed, q_nope=q_nope, W_UK=W_UK, seq_lens=seq_lens,
                                   kv_offsets=kv_offsets, max_seq_len=max_seq_len,
                                   seq_lens_host=seq_lens_host, shared_cache=shared_cache,
                                   kv_pos_offset=kv_pos_offset, softmax_scale=softmax_scale,
                                   kv_row_stride=kv_row_stride, kernel=kernel, out=out, workspace=workspace,
-                                  timer=timer, page_table=page_table, page_rows=page_rows)
+                                  timer=timer, page_table=page_table, page_rows=page_rows,
+                                  rope_theta=rope_theta)

@@ -1,6 +1,6 @@
 """Compile the reference's own fused decode kernels into oracle/_ref/ (test oracle only).
 
-    python oracle/build_ref.py            # needs the reference checkout at $LATENT_ATTN_REF
+    LATENT_ATTN_REF=<reference checkout> python oracle/build_ref.py [--force]
 
 The sources are compiled where they lie (src/fused_mla.cu, src/fused_mla_batched.cu
 of anishesg/latent-attn) with the reference's own flags (setup.py:26-32: -O3
@@ -24,7 +24,11 @@ OUT = os.path.join(OUT_DIR, "libref_mla.so")
 
 
 def build(ref: str | None = None, force: bool = False) -> str | None:
-    ref = ref or os.environ.get("LATENT_ATTN_REF", "/root/reference")
+    """Build from the reference checkout `ref` (or $LATENT_ATTN_REF). Without a checkout the
+    previously built library is returned if there is one (the GPU box only uses that), else None."""
+    ref = ref or os.environ.get("LATENT_ATTN_REF")
+    if not ref:
+        return OUT if os.path.exists(OUT) else None
     src = os.path.join(ref, "src")
     files = [os.path.join(src, "fused_mla.cu"), os.path.join(src, "fused_mla_batched.cu")]
     if not all(os.path.exists(f) for f in files):

@@ -1,9 +1,9 @@
 """Generate the golden MLA decode fixtures from the reference's own oracle.
 
-Run in a container that has the reference checkout (read-only) at
-``$LATENT_ATTN_REF`` (default ``/root/reference``):
+Run in a container that has the reference checkout (read-only), named by
+``$LATENT_ATTN_REF``:
 
-    python tests/golden/make_golden.py
+    LATENT_ATTN_REF=<reference checkout> python tests/golden/make_golden.py
 
 For every case it draws seeded inputs with ``latent_attn/synthetic.py`` (loaded
 by file path, so the reference's own ``latent_attn`` package is the one on
@@ -36,7 +36,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("LATENT_ATTN_REF", "/root/reference")
+REF = os.environ.get("LATENT_ATTN_REF")  # the reference checkout; required (see main())
 
 
 def _load_synthetic():
@@ -122,6 +122,8 @@ def run_case(syn, ref_tests, RefCfg, name, recipe, kw):
 
 
 def main():
+    if not REF or not os.path.isdir(REF):
+        raise SystemExit("set LATENT_ATTN_REF to the reference checkout")
     sys.path.insert(0, os.path.join(REF, "tests"))
     sys.path.insert(0, REF)
     import latent_attn as ref_pkg  # the reference's package (torch only; _C is imported lazily)

@@ -188,3 +188,31 @@ def test_paged_append_then_decode():
     contig = mla_decode(rows, qr, W_UV, cos, sin, cfg,
                         kv_offsets=torch.tensor(offs, dtype=torch.int64, device=dev), **common)
     assert torch.equal(paged, contig)
+
+
+def test_append_rejects_rows_outside_the_cache():
+    """A page id near INT_MAX (whose page end would overflow 32-bit arithmetic) and an offset
+    past the cache's rows are not written: the cache stays untouched, the length does not
+    advance, and bit 1 of the status word is set."""
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(13)
+    kv = torch.randn(256, 576, generator=g).to(torch.bfloat16).to(dev)
+    before = kv.clone()
+    c_t = torch.randn(1, 512, generator=g).to(torch.bfloat16).to(dev)
+    k_r = torch.randn(1, 64, generator=g).to(torch.bfloat16).to(dev)
+    # paged: the sequence's only page id is INT_MAX
+    table = torch.full((1, 2), 2 ** 31 - 1, dtype=torch.int32, device=dev)
+    lens = torch.tensor([3], dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    _C.mla_cache_append(kv, c_t, k_r, lens, 128, *DIMS, page_table=table, page_rows=64, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 2 and int(lens.item()) == 3
+    assert torch.equal(kv, before)
+    # contiguous: an offset whose row lies past the cache's 256 rows
+    offs = torch.tensor([250], dtype=torch.int64, device=dev)
+    lens = torch.tensor([10], dtype=torch.int32, device=dev)
+    status.zero_()
+    _C.mla_cache_append(kv, c_t, k_r, lens, 64, *DIMS, kv_offsets=offs, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 2 and int(lens.item()) == 10
+    assert torch.equal(kv, before)

@@ -353,3 +353,123 @@ def test_decode_timer_eager_and_graph():
     del g
     t_eager.close()
     t_graph.close()
+
+
+def _oracle_single_otf(inp, b, H=128, dc=512, dn=128, dR=64, dv=128, pos_offset=0):
+    """Oracle of sequence b with the on-the-fly RoPE mode's cos / sin."""
+    L, off = inp.seq_lens[b], inp.kv_offsets[b]
+    cos, sin = O.rope_tables_otf(L, dR, pos_offset=pos_offset)
+    kv = inp.kv_cache[off:off + L].float().numpy()
+    q_abs = O.absorb_query(inp.q_nope[b].float().numpy(), inp.W_UK.float().numpy(), H, dc)
+    return O.absorbed_decode(kv, q_abs, inp.q_rope[b].float().numpy(), inp.W_UV.float().numpy(), cos, sin,
+                             H, dc, dn, dR, dv)
+
+
+@pytest.mark.parametrize("L", [8192, 131072])
+def test_on_the_fly_rope_vs_oracle_and_tables(L):
+    """No RoPE tables (rope_cos = rope_sin = None): the kernels compute cos / sin themselves.
+    BASELINE configs 1 and 3 on both decode kernels, against the fp64 oracle with the same
+    angles, and against the table path (the reference's tables) within the same bound."""
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[L], seed=0)
+    cfg = MLAConfig.deepseek_v2()
+    dev = torch.device("cuda")
+    kv, W_UV, W_UK = inp.kv_cache.to(dev), inp.W_UV.to(dev), inp.W_UK.to(dev)
+    qn, qr = inp.q_nope.float().to(dev), inp.q_rope.float().to(dev)
+    cos, sin = synthetic.build_rope_tables(L, 64, device=dev)
+    ref = _oracle_single_otf(inp, 0)
+    for kern in kernels_for(cfg):
+        otf = mla_decode(kv, qr, W_UV, None, None, cfg, q_nope=qn, W_UK=W_UK, kernel=kern).cpu().numpy()[0]
+        tab = mla_decode(kv, qr, W_UV, cos, sin, cfg, q_nope=qn, W_UK=W_UK, kernel=kern).cpu().numpy()[0]
+        assert_close(otf, ref, f"on-the-fly L={L} kernel={kern}")
+        assert_close(otf, tab, f"on-the-fly vs tables L={L} kernel={kern}")
+
+
+def test_on_the_fly_rope_offset_theta_and_varlen():
+    """On-the-fly RoPE with a KV-range position offset, a non-default theta, a variable-length
+    batch with a partial last tile, and the reference-shaped op given no tables."""
+    dev = torch.device("cuda")
+    cfg = MLAConfig.deepseek_v2()
+    lens = [77, 640, 1]
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=lens, seed=21)
+    kv = inp.kv_cache.to(dev)
+    qn, qr, W_UK, W_UV = inp.q_nope.float().to(dev), inp.q_rope.float().to(dev), inp.W_UK.to(dev), inp.W_UV.to(dev)
+    for kern in kernels_for(cfg):
+        out = mla_decode(kv, qr, W_UV, None, None, cfg, q_nope=qn, W_UK=W_UK,
+                         seq_lens=torch.tensor(lens, dtype=torch.int32, device=dev),
+                         kv_offsets=torch.tensor(inp.kv_offsets, dtype=torch.int64, device=dev),
+                         max_seq_len=max(lens), kernel=kern).cpu().numpy()
+        for b in range(len(lens)):
+            assert_close(out[b], _oracle_single_otf(inp, b), f"varlen b={b} kernel={kern}")
+        # one sequence's rows at absolute positions 1000.., theta 50000
+        b, off, theta = 1, 1000, 50000.0
+        L, r0 = lens[b], inp.kv_offsets[b]
+        kvb = kv[r0:r0 + L].contiguous()
+        got = mla_decode(kvb, qr[b:b + 1].contiguous(), W_UV, None, None, cfg, q_nope=qn[b:b + 1].contiguous(),
+                         W_UK=W_UK, kv_pos_offset=off, rope_theta=theta, kernel=kern).cpu().numpy()[0]
+        cos, sin = O.rope_tables_otf(L, 64, theta=theta, pos_offset=off)
+        q_abs = O.absorb_query(inp.q_nope[b].float().numpy(), inp.W_UK.float().numpy(), 128, 512)
+        ref = O.absorbed_decode(kvb.cpu().float().numpy(), q_abs, inp.q_rope[b].float().numpy(),
+                                inp.W_UV.float().numpy(), cos, sin, 128, 512, 128, 64, 128)
+        assert_close(got, ref, f"offset + theta kernel={kern}")
+    with pytest.raises(RuntimeError, match="both rope_cos and rope_sin"):
+        mla_decode(kv, qr, W_UV, synthetic.build_rope_tables(640, 64, device=dev)[0], None, cfg, q_nope=qn,
+                   W_UK=W_UK, seq_lens=torch.tensor(lens, dtype=torch.int32, device=dev),
+                   kv_offsets=torch.tensor(inp.kv_offsets, dtype=torch.int64, device=dev), max_seq_len=640)
+
+
+def _per_token_cosine(a, b):
+    """The reference's batched-vs-loop criterion (tests/test_batched.py:82-86)."""
+    a = np.asarray(a, dtype=np.float64).ravel()
+    b = np.asarray(b, dtype=np.float64).ravel()
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def test_config4_batch256_vs_oracle():
+    """BASELINE config 4 (B=256, L=4096, H=128, bf16, in-op absorption): the absorption GEMM's
+    full 256-token block and the projection's four 64-token blocks. Six sequences against the
+    fp64 oracle and two against single-sequence decodes, on both decode kernels."""
+    L, B = 4096, 256
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[L] * B, seed=4)
+    cfg = MLAConfig.deepseek_v3()
+    dev = torch.device("cuda")
+    kv, W_UV, W_UK = inp.kv_cache.to(dev), inp.W_UV.to(dev), inp.W_UK.to(dev)
+    qn, qr = inp.q_nope.float().to(dev), inp.q_rope.float().to(dev)
+    cos, sin = synthetic.build_rope_tables(L, 64, device=dev)
+    cos_np, sin_np = cos.cpu().numpy(), sin.cpu().numpy()
+    refs = {b: _oracle_single(inp, b, cos_np, sin_np) for b in (0, 1, 63, 64, 200, 255)}
+    for kern in kernels_for(cfg):
+        out = mla_decode(kv, qr, W_UV, cos, sin, cfg, q_nope=qn, W_UK=W_UK, max_seq_len=L,
+                         kernel=kern).cpu().numpy()
+        assert np.isfinite(out).all()
+        for b, ref in refs.items():
+            assert_close(out[b], ref, f"cfg4 seq {b} kernel={kern}")
+        for b in (7, 130):
+            single = mla_decode(kv[b * L:(b + 1) * L], qr[b:b + 1].contiguous(), W_UV, cos, sin, cfg,
+                                q_nope=qn[b:b + 1].contiguous(), W_UK=W_UK, kernel=kern).cpu().numpy()[0]
+            assert_close(out[b], single, f"cfg4 batched vs single seq {b} kernel={kern}")
+            assert _per_token_cosine(out[b], single) > 0.998
+
+
+@pytest.mark.parametrize("B", [65, 257, 300])
+def test_batches_crossing_gemm_blocks(B):
+    """Batches that cross the absorption GEMM's 256-token block (257, 300: two z-blocks) and the
+    projection's 64-token blocks (65: a one-token tail block), with short variable lengths
+    (partial tiles, single-position sequences), every sequence against the oracle, on both
+    decode kernels."""
+    lens = [1 + (37 * b) % 200 for b in range(B)]
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=lens, seed=B)
+    cfg = MLAConfig.deepseek_v2()
+    dev = torch.device("cuda")
+    Lmax = max(lens)
+    cos, sin = synthetic.build_rope_tables(Lmax, 64, device=dev)
+    cos_np, sin_np = cos.cpu().numpy(), sin.cpu().numpy()
+    kv, W_UV, W_UK = inp.kv_cache.to(dev), inp.W_UV.to(dev), inp.W_UK.to(dev)
+    qn, qr = inp.q_nope.float().to(dev), inp.q_rope.float().to(dev)
+    seq = torch.tensor(lens, dtype=torch.int32, device=dev)
+    offs = torch.tensor(inp.kv_offsets, dtype=torch.int64, device=dev)
+    refs = [_oracle_single(inp, b, cos_np, sin_np) for b in range(B)]
+    for kern in kernels_for(cfg):
+        out = mla_decode(kv, qr, W_UV, cos, sin, cfg, q_nope=qn, W_UK=W_UK, seq_lens=seq, kv_offsets=offs,
+                         max_seq_len=Lmax, kernel=kern).cpu().numpy()
+        for b in range(B):
+            assert_close(out[b], refs[b], f"B={B} seq {b} (L={lens[b]}) kernel={kern}")
