@@ -176,11 +176,12 @@ typedef struct mla_decode_args {
   int page_rows;                /* rows per page, a positive multiple of 64 */
   int max_pages;                /* page-table entries per sequence, >= ceil(max_seq_len / page_rows) */
   /* On-the-fly RoPE. With rope_cos and rope_sin both NULL the decode kernels compute the
-   * rotation of each cache row themselves, as the reference's table builder defines it
-   * (latent_attn/__init__.py:31-38): freq_i = rope_theta^(-2i / d_R) (a double-precision power
-   * rounded to fp32), angle = (float)pos * freq_i in fp32, then cos / sin of the angle after an
-   * exact double-precision reduction to [-pi, pi]. No table is read. 0 means 10000. Ignored
-   * when tables are given; needs qk_rope_head_dim <= 128. */
+   * rotation of each cache row themselves, with the reference table builder's rotate-half
+   * convention (latent_attn/__init__.py:31-38): freq_i = rope_theta^(-2i / d_R) (a
+   * double-precision power rounded to fp32) and angle = pos * freq_i taken exactly (the table
+   * builder rounds it to fp32, a difference of at most half an fp32 ulp of the angle); cos / sin
+   * are within 6e-7 of their exact values. No table is read. 0 means 10000. Ignored when tables
+   * are given; needs qk_rope_head_dim <= 128 and positions below 2^29. */
   float rope_theta;
 } mla_decode_args_t;
 

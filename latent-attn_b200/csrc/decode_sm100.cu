@@ -469,33 +469,58 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
         // from global memory one tile ahead, so the loads overlap the tile before.
         constexpr int kItems = 128 / kTransformThreads;
         float4 tab_next[kItems][4];  // per item: cos[0:4], cos[4:8], sin[0:4], sin[4:8]
+        // Both items of a thread have the same half h = tt & 1, i.e. the same 8 frequencies.
+        // On-the-fly RoPE: the angle (P0 + p) f of the tile's base position P0 and the item's
+        // offset p is rotated as base(P0 f) x step(p f): the 16 base rotations of a tile are
+        // computed by lanes 0-15 and shuffled; each thread's 2 x 8 step rotations once per CTA.
+        const int hsel = tt & 1;
+        const int f0 = 16 * static_cast<int>(rank) + 8 * hsel;
+        float stc[kItems][8], sts[kItems][8];
+        if (P.rope_otf) {
+#pragma unroll
+            for (int u = 0; u < kItems; ++u)
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    rope_sincos_exact((tt + kTransformThreads * u) >> 1, P.rope_freq[f0 + e], &sts[u][e], &stc[u][e]);
+        }
         auto load_tabs = [&](const TileIter& ti) {
             const int tnp = ti.np();
+            const long long pos0 = static_cast<long long>(P.kv_pos_offset) + ti.pos0();
+            if (P.rope_otf) {
+                // computed, not read: no table traffic and no load latency (warp-collective)
+                float cb = 1.f, sb = 0.f;
+                if (lane < 16) rope_sincos_exact(pos0, P.rope_freq[16 * static_cast<int>(rank) + lane], &sb, &cb);
+                float cs[kItems][8], sn[kItems][8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float c0 = __shfl_sync(0xffffffffu, cb, 8 * hsel + e);
+                    const float s0 = __shfl_sync(0xffffffffu, sb, 8 * hsel + e);
+#pragma unroll
+                    for (int u = 0; u < kItems; ++u) {
+                        cs[u][e] = c0 * stc[u][e] - s0 * sts[u][e];
+                        sn[u][e] = s0 * stc[u][e] + c0 * sts[u][e];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < kItems; ++u) {
+                    tab_next[u][0] = make_float4(cs[u][0], cs[u][1], cs[u][2], cs[u][3]);
+                    tab_next[u][1] = make_float4(cs[u][4], cs[u][5], cs[u][6], cs[u][7]);
+                    tab_next[u][2] = make_float4(sn[u][0], sn[u][1], sn[u][2], sn[u][3]);
+                    tab_next[u][3] = make_float4(sn[u][4], sn[u][5], sn[u][6], sn[u][7]);
+                }
+                return;
+            }
 #pragma unroll
             for (int u = 0; u < kItems; ++u) {
-                const int item = tt + kTransformThreads * u, p = item >> 1, h = item & 1;
+                const int item = tt + kTransformThreads * u, p = item >> 1;
                 if (p < tnp) {
-                    const long long pos = static_cast<long long>(P.kv_pos_offset) + ti.pos0() + p;
-                    const int f0 = 16 * static_cast<int>(rank) + 8 * h;
-                    if (P.rope_otf) {
-                        // computed, not read: no table traffic and no load latency
-                        float cs[8], sn[8];
-#pragma unroll
-                        for (int e = 0; e < 8; ++e)
-                            rope_sincos(static_cast<float>(pos) * P.rope_freq[f0 + e], &sn[e], &cs[e]);
-                        tab_next[u][0] = make_float4(cs[0], cs[1], cs[2], cs[3]);
-                        tab_next[u][1] = make_float4(cs[4], cs[5], cs[6], cs[7]);
-                        tab_next[u][2] = make_float4(sn[0], sn[1], sn[2], sn[3]);
-                        tab_next[u][3] = make_float4(sn[4], sn[5], sn[6], sn[7]);
-                    } else {
-                        const long long off = pos * 32 + f0;
-                        const float4* c4 = reinterpret_cast<const float4*>(cos_tab + off);
-                        const float4* s4 = reinterpret_cast<const float4*>(sin_tab + off);
-                        tab_next[u][0] = __ldg(c4);
-                        tab_next[u][1] = __ldg(c4 + 1);
-                        tab_next[u][2] = __ldg(s4);
-                        tab_next[u][3] = __ldg(s4 + 1);
-                    }
+                    const long long off = (pos0 + p) * 32 + f0;
+                    const float4* c4 = reinterpret_cast<const float4*>(cos_tab + off);
+                    const float4* s4 = reinterpret_cast<const float4*>(sin_tab + off);
+                    tab_next[u][0] = __ldg(c4);
+                    tab_next[u][1] = __ldg(c4 + 1);
+                    tab_next[u][2] = __ldg(s4);
+                    tab_next[u][3] = __ldg(s4 + 1);
                 }
             }
         };

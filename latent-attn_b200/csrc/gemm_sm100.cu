@@ -8,8 +8,11 @@
 //    It runs transposed, D^T[d_c x tokens] = W_UK_h^T . q_nope_h^T, so the 128-row
 //    M tile is a slice of d_c and any token count (1 .. 256 per CTA) is the N side:
 //      A = W_UK_h^T, MN-major (d_c contiguous), 2 TMA boxes of 64 d_c x dn rows
-//      B = q_nope_h^T, K-major, converted from fp32 to the cache type on load.
-//    CTA = (d_c slice of 128, head, block of up to 256 tokens), 128 threads.
+//      B = q_nope_h^T, K-major, converted from fp32 on load into two 16-bit parts, hi =
+//          round(q) and lo = round(q - hi), and both are multiplied (two K passes into one
+//          accumulator): the product keeps q_nope to about 2^-17 instead of the 2^-9 of a
+//          single bf16 rounding, the largest error term of the whole decode for short sequences.
+//    CTA = (d_c slice of 128, head, block of up to 128 tokens), 128 threads.
 //
 // 2. Split-KV merge + output projection, per head h:
 //        o_lat[b, h, :] = sum_k w_k o_k     (log-sum-exp weights of the partial records)
@@ -78,7 +81,7 @@ __device__ __forceinline__ long long qpack_row(const DecodePlan& P, int b, int h
                     : static_cast<long long>(b) * P.head_blocks * kGroupRows + h;
 }
 
-constexpr int kAbsorbTok = 256;    // tokens per absorption CTA (MMA N <= 256)
+constexpr int kAbsorbTok = 128;    // tokens per absorption CTA (MMA N; two CTAs per SM with the hi/lo operand)
 constexpr int kProjTok = 64;       // tokens per projection CTA
 constexpr int kProjWarps = 16;     // projection CTA: 16 warps merge, warp 0 issues the MMA, warps 4-7 store
 // rows of split partial sums of the merge (S * ntok <= rows): 32 when the token operand is at most
@@ -87,9 +90,11 @@ constexpr int kProjWarps = 16;     // projection CTA: 16 warps merge, warp 0 iss
 __host__ __device__ constexpr int proj_red_rows(int ntp) { return ntp <= 16 ? 32 : 8; }
 constexpr int kProjRedMax = 32;    // the largest proj_red_rows
 
-// B operand (dn/64 chunks of ntp rows x 128 B), reused after the MMAs as ntp rows x 128 elements of staging
+// B operand hi and lo parts (each dn/64 chunks of ntp rows x 128 B), reused after the MMAs as ntp rows x
+// 128 elements of staging
+__host__ __device__ inline int absorb_b_part_bytes(int dn, int ntp) { return (dn / 64) * ntp * 128; }
 __host__ __device__ inline int absorb_b_bytes(int dn, int ntp) {
-    const int b = (dn / 64) * ntp * 128, st = ntp * 256;
+    const int b = 2 * absorb_b_part_bytes(dn, ntp), st = ntp * 256;
     return b > st ? b : st;
 }
 
@@ -142,10 +147,12 @@ absorb_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
         tma_load_2d(a_u32, &tmap_w, a_full, m0, h * dn);
         tma_load_2d(a_u32 + dn * 128, &tmap_w, a_full, m0 + 64, h * dn);
     }
-    // B operand: q_nope of the block's tokens, fp32 -> T, K-major 128-byte-swizzled rows.
-    // Eight 32-byte items per thread are loaded before any is stored, so the loads overlap.
+    // B operand: q_nope of the block's tokens, fp32 -> hi and lo parts in T, K-major
+    // 128-byte-swizzled rows. Eight 32-byte items per thread are loaded before any is stored,
+    // so the loads overlap.
     const int upr = dn / 8;  // 16-byte units (8 elements) per token row
     const int items = ntp * upr;
+    const uint32_t lo_off = static_cast<uint32_t>(absorb_b_part_bytes(dn, ntp));
     for (int i0 = threadIdx.x; i0 < items; i0 += 8 * 128) {
         float4 x[8], y[8];
 #pragma unroll
@@ -165,8 +172,16 @@ absorb_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
             const int i = i0 + q * 128, t = i / upr, u = i % upr;
             if (i < items) {
                 const uint32_t dst = b_u32 + (u >> 3) * (ntp * 128) + t * 128 + (((u & 7) ^ (t & 7)) << 4);
-                st_shared_v4(dst, pack_pair<T>(x[q].x, x[q].y), pack_pair<T>(x[q].z, x[q].w),
-                             pack_pair<T>(y[q].x, y[q].y), pack_pair<T>(y[q].z, y[q].w));
+                const float v[8] = {x[q].x, x[q].y, x[q].z, x[q].w, y[q].x, y[q].y, y[q].z, y[q].w};
+                uint32_t hi[4], lo[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    hi[e] = pack_pair<T>(v[2 * e], v[2 * e + 1]);
+                    const float2 h = ElemTraits<T>::to_f2(*reinterpret_cast<const typename ElemTraits<T>::T2*>(&hi[e]));
+                    lo[e] = pack_pair<T>(v[2 * e] - h.x, v[2 * e + 1] - h.y);
+                }
+                st_shared_v4(dst, hi[0], hi[1], hi[2], hi[3]);
+                st_shared_v4(dst + lo_off, lo[0], lo[1], lo[2], lo[3]);
             }
         }
     }
@@ -178,11 +193,13 @@ absorb_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
         if (issued) {
             tc_fence_after();
             const uint32_t idesc = idesc_f16(128, ntp, GemmFmt<T>::v, true, false);
-            for (int k = 0; k < dn / 16; ++k) {
-                const uint64_t ad = smem_desc_sw128(a_u32 + k * 2048, dn * 128, 1024);
-                const uint64_t bd = smem_desc_sw128(b_u32 + (k >> 2) * (ntp * 128) + (k & 3) * 32, 16, 1024);
-                mma_ss(tbase, ad, bd, idesc, k > 0 ? 1u : 0u);
-            }
+            for (int part = 0; part < 2; ++part)   // hi, then lo, into the same accumulator
+                for (int k = 0; k < dn / 16; ++k) {
+                    const uint64_t ad = smem_desc_sw128(a_u32 + k * 2048, dn * 128, 1024);
+                    const uint64_t bd = smem_desc_sw128(b_u32 + part * lo_off + (k >> 2) * (ntp * 128) + (k & 3) * 32,
+                                                        16, 1024);
+                    mma_ss(tbase, ad, bd, idesc, (part | k) > 0 ? 1u : 0u);
+                }
         }
         mma_commit(mma_done);  // also arrives when nothing was issued
     }

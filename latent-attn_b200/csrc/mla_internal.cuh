@@ -180,14 +180,14 @@ __device__ inline void write_tile_prefix(const DecodePlan& P, int* prefix) {
 
 __device__ inline int num_records(const DecodePlan& P) { return P.G + P.W - 1; }
 
-// cos and sin of an on-the-fly RoPE angle. The angle is an fp32 value of up to ~1.3e5 rad
-// (position x frequency, formed in fp32 as the reference's table builder forms it). It is
-// reduced to r in [-pi, pi] in double precision: with k <= 2^21 and a 53-bit 2 pi the reduced
-// value is exact to ~1e-10 rad before its rounding to fp32 (1.2e-7 rad). On [-pi, pi] the
-// hardware approximations have an absolute error below 4e-7, so cos and sin are within 5e-7 of
-// the exact values; the rotated key is then rounded to 16 bits (relative 4e-3 for bf16).
-__device__ __forceinline__ void rope_sincos(float angle, float* s, float* c) {
-    const double a = static_cast<double>(angle);
+// cos and sin of the on-the-fly RoPE angle pos * freq, taken as the exact product (pos below
+// 2^29 times an fp32 frequency fits the 53-bit double mantissa). The angle is reduced to
+// r = angle - k 2pi, |r| <= pi, in double precision (2pi's double rounding contributes below
+// 1e-9 rad for k < 2^22), rounded to fp32 (1.2e-7 rad), and the hardware approximations on
+// [-pi, pi] add below 4e-7: cos and sin are within 6e-7 of their exact values. The rotated key
+// is then rounded to 16 bits (relative 4e-3 for bf16).
+__device__ __forceinline__ void rope_sincos_exact(long long pos, float freq, float* s, float* c) {
+    const double a = static_cast<double>(pos) * static_cast<double>(freq);
     const double k = rint(a * 0.15915494309189535);  // 1 / (2 pi)
     const float r = static_cast<float>(fma(-k, 6.283185307179586, a));
     __sincosf(r, s, c);
@@ -198,7 +198,7 @@ __device__ __forceinline__ void rope_sincos(float angle, float* s, float* c) {
 __device__ __forceinline__ void rope_cs(const DecodePlan& P, const float* cos_tab, const float* sin_tab,
                                         long long pos, int i, float* c, float* s) {
     if (P.rope_otf) {
-        rope_sincos(static_cast<float>(pos) * P.rope_freq[i], s, c);
+        rope_sincos_exact(pos, P.rope_freq[i], s, c);
     } else {
         const long long off = pos * (P.dR / 2) + i;
         *c = cos_tab[off];
@@ -260,6 +260,12 @@ template <typename T>
 cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
                                 const float* sin, float* rec_ml, float* rec_o, bool pdl, cudaStream_t s);
 bool decode_sm100_available();
+// decode_2sm.cu: the CTA-pair (cta_group::2) decode kernel, 128-position tiles
+bool decode_2sm_supported(const DecodePlan& P);
+int decode_2sm_tile();
+template <typename T>
+cudaError_t launch_decode_2sm(const DecodePlan& P, const T* kv, const T* qpack, const float* cos, const float* sin,
+                              float* rec_ml, float* rec_o, bool pdl, cudaStream_t s);
 // cache.cu
 template <typename T>
 cudaError_t launch_cache_append(T* kv, long long stride, long long kv_rows, int dc, int dR, int batch, const T* c_t,

@@ -13,8 +13,8 @@ produced by importing the reference's own ``torch_mla_reference``
 Everything is plain numpy.
 
 * ``rope_tables`` restates ``_build_rope_tables`` (latent_attn/__init__.py:31-38);
-  ``rope_tables_otf`` gives the same angles with the frequencies of the library's
-  on-the-fly mode (a double-precision power rounded to fp32).
+  ``rope_tables_otf`` gives the rotation of the library's on-the-fly mode (fp32
+  frequencies from a double-precision power, exact angles).
 * ``naive_decode`` restates ``torch_mla_reference`` (tests/test_python.py:26-63):
   decompress ``K_nope = c @ W_UK^T`` and ``V = c @ W_UV^T``, rotate ``k_rope``,
   score with ``scale = 1/sqrt(dn + dR)`` and take a softmax, then ``out = P @ V``.
@@ -49,13 +49,14 @@ def rope_tables(seq_len: int, d_R: int, theta: float = 10000.0, pos_offset: int 
 def rope_tables_otf(seq_len: int, d_R: int, theta: float = 10000.0, pos_offset: int = 0
                     ) -> Tuple[np.ndarray, np.ndarray]:
     """(cos, sin) of the library's on-the-fly RoPE mode (no tables passed): the reference
-    builder's angles (latent_attn/__init__.py:31-38: ``angle = pos * freq_i`` in fp32) with
-    ``freq_i = theta^(-2i/d_R)`` taken as the double-precision power rounded once to fp32,
-    and cos / sin of each fp32 angle evaluated in float64, then rounded to fp32."""
+    builder's rotation (latent_attn/__init__.py:31-38) with ``freq_i = theta^(-2i/d_R)`` taken
+    as the double-precision power rounded once to fp32 and the angle ``pos * freq_i`` taken
+    exactly (in float64, not rounded to fp32 as the table builder rounds it); cos / sin
+    evaluated in float64, then rounded to fp32."""
     half = d_R // 2
-    freqs = np.array([np.float32(theta ** (-2.0 * i / d_R)) for i in range(half)], dtype=np.float32)
-    pos = np.arange(pos_offset, pos_offset + seq_len, dtype=np.float32)
-    ang = (pos[:, None] * freqs[None, :]).astype(np.float32).astype(np.float64)
+    freqs = np.array([np.float32(theta ** (-2.0 * i / d_R)) for i in range(half)], dtype=np.float64)
+    pos = np.arange(pos_offset, pos_offset + seq_len, dtype=np.float64)
+    ang = pos[:, None] * freqs[None, :]
     return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
 
 

@@ -425,9 +425,9 @@ def _per_token_cosine(a, b):
 
 
 def test_config4_batch256_vs_oracle():
-    """BASELINE config 4 (B=256, L=4096, H=128, bf16, in-op absorption): the absorption GEMM's
-    full 256-token block and the projection's four 64-token blocks. Six sequences against the
-    fp64 oracle and two against single-sequence decodes, on both decode kernels."""
+    """BASELINE config 4 (B=256, L=4096, H=128, bf16, in-op absorption): two full 128-token
+    blocks of the absorption GEMM and the projection's four 64-token blocks. Six sequences
+    against the fp64 oracle and two against single-sequence decodes, on both decode kernels."""
     L, B = 4096, 256
     inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[L] * B, seed=4)
     cfg = MLAConfig.deepseek_v3()
@@ -452,8 +452,9 @@ def test_config4_batch256_vs_oracle():
 
 @pytest.mark.parametrize("B", [65, 257, 300])
 def test_batches_crossing_gemm_blocks(B):
-    """Batches that cross the absorption GEMM's 256-token block (257, 300: two z-blocks) and the
-    projection's 64-token blocks (65: a one-token tail block), with short variable lengths
+    """Batches that cross the absorption GEMM's 128-token blocks (257, 300: a one-token and a
+    44-token tail block) and the projection's 64-token blocks (65: a one-token tail block), with
+    short variable lengths
     (partial tiles, single-position sequences), every sequence against the oracle, on both
     decode kernels."""
     lens = [1 + (37 * b) % 200 for b in range(B)]
