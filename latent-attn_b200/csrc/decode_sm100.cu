@@ -230,10 +230,11 @@ __device__ __forceinline__ float2 f2_sub(float2 a, float2 b) {
 
 }  // namespace
 
-// kPaged: the cache is paged (the tile's row comes from the page table). A separate instantiation,
-// so the contiguous layout runs without the lookup: the kernel is sensitive to its instruction
-// footprint, and the lookup alone cost 3.6% at B = 256.
-template <typename T, bool kPaged>
+// kPaged: the cache is paged (the tile's row comes from the page table). kOtf: RoPE computed on
+// the fly instead of read from the caller's tables. Separate instantiations, so each runs without
+// the other modes' code: the kernel is sensitive to its instruction footprint (the page lookup
+// alone cost 3.6% at B = 256).
+template <typename T, bool kPaged, bool kOtf>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_rope,
                     const DecodePlan P, const T* __restrict__ qpack, const float* __restrict__ cos_tab,
@@ -476,7 +477,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
         const int hsel = tt & 1;
         const int f0 = 16 * static_cast<int>(rank) + 8 * hsel;
         float stc[kItems][8], sts[kItems][8];
-        if (P.rope_otf) {
+        if constexpr (kOtf) {
 #pragma unroll
             for (int u = 0; u < kItems; ++u)
 #pragma unroll
@@ -486,7 +487,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
         auto load_tabs = [&](const TileIter& ti) {
             const int tnp = ti.np();
             const long long pos0 = static_cast<long long>(P.kv_pos_offset) + ti.pos0();
-            if (P.rope_otf) {
+            if constexpr (kOtf) {
                 // computed, not read: no table traffic and no load latency (warp-collective)
                 float cb = 1.f, sb = 0.f;
                 if (lane < 16) rope_sincos_exact(pos0, P.rope_freq[16 * static_cast<int>(rank) + lane], &sb, &cb);
@@ -508,8 +509,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                     tab_next[u][2] = make_float4(sn[u][0], sn[u][1], sn[u][2], sn[u][3]);
                     tab_next[u][3] = make_float4(sn[u][4], sn[u][5], sn[u][6], sn[u][7]);
                 }
-                return;
-            }
+            } else {
 #pragma unroll
             for (int u = 0; u < kItems; ++u) {
                 const int item = tt + kTransformThreads * u, p = item >> 1;
@@ -522,6 +522,7 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                     tab_next[u][2] = __ldg(s4);
                     tab_next[u][3] = __ldg(s4 + 1);
                 }
+            }
             }
         };
         TileIter it;
@@ -903,9 +904,11 @@ cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack
     if (!make_tmap_2d_16b(&tmap, kv, rows, 576, stride, 64, 64) ||
         !make_tmap_2d_16b(&tmap_rope, kv, rows, 576, stride, 64, 8, CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
-    const bool paged = P.page_table != nullptr;
-    const void* kernel = paged ? reinterpret_cast<const void*>(decode_sm100_kernel<T, true>)
-                               : reinterpret_cast<const void*>(decode_sm100_kernel<T, false>);
+    const bool paged = P.page_table != nullptr, otf = P.rope_otf != 0;
+    const void* kernel = paged ? (otf ? reinterpret_cast<const void*>(decode_sm100_kernel<T, true, true>)
+                                      : reinterpret_cast<const void*>(decode_sm100_kernel<T, true, false>))
+                               : (otf ? reinterpret_cast<const void*>(decode_sm100_kernel<T, false, true>)
+                                      : reinterpret_cast<const void*>(decode_sm100_kernel<T, false, false>));
     cudaError_t e = ensure_dynamic_smem(kernel, static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
@@ -918,10 +921,17 @@ cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    if (paged)
-        e = cudaLaunchKernelEx(&cfg, decode_sm100_kernel<T, true>, tmap, tmap_rope, P, qpack, cos, sin, rec_ml, rec_o);
+    if (paged && otf)
+        e = cudaLaunchKernelEx(&cfg, decode_sm100_kernel<T, true, true>, tmap, tmap_rope, P, qpack, cos, sin, rec_ml, rec_o);
+    else if (paged)
+        e = cudaLaunchKernelEx(&cfg, decode_sm100_kernel<T, true, false>, tmap, tmap_rope, P, qpack, cos, sin, rec_ml,
+                               rec_o);
+    else if (otf)
+        e = cudaLaunchKernelEx(&cfg, decode_sm100_kernel<T, false, true>, tmap, tmap_rope, P, qpack, cos, sin, rec_ml,
+                               rec_o);
     else
-        e = cudaLaunchKernelEx(&cfg, decode_sm100_kernel<T, false>, tmap, tmap_rope, P, qpack, cos, sin, rec_ml, rec_o);
+        e = cudaLaunchKernelEx(&cfg, decode_sm100_kernel<T, false, false>, tmap, tmap_rope, P, qpack, cos, sin, rec_ml,
+                               rec_o);
     count_launches(1);
     return e != cudaSuccess ? e : cudaGetLastError();
 }

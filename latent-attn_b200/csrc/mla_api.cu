@@ -92,17 +92,6 @@ int env_workers() {
     return v;
 }
 
-// LATENT_ATTN_B200_DECODE = "split" | "pair" picks the tensor-core decode kernel: the K-split
-// pair kernel with a score exchange (decode_sm100.cu, the default) or the CTA-pair MMA kernel
-// (decode_2sm.cu).
-int env_decode_kernel() {
-    static int v = [] {
-        const char* s = std::getenv("LATENT_ATTN_B200_DECODE");
-        return (s && !std::strcmp(s, "pair")) ? 2 : 1;
-    }();
-    return v;
-}
-
 bool env_gemm_enabled() {
     static bool v = [] {
         const char* s = std::getenv("LATENT_ATTN_B200_GEMM");
@@ -117,7 +106,6 @@ size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 struct Plan {
     mla::DecodePlan dp;
     bool use_tc = false;
-    int tc_kernel = 0;              // 2: CTA-pair kernel (decode_2sm.cu), 1: K-split kernel (decode_sm100.cu)
     bool use_gemm_absorb = false;   // tcgen05 absorption (gemm_sm100.cu) instead of the CUDA-core pack
     bool use_gemm_project = false;  // tcgen05 merge + W_UV projection instead of the CUDA-core combine
     size_t off_prefix = 0, off_qpack = 0, off_rec_ml = 0, off_rec_o = 0, off_status = 0, total = 0;
@@ -235,8 +223,7 @@ mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan
         use_tc = true;
     }
     p->use_tc = use_tc;
-    p->tc_kernel = use_tc ? env_decode_kernel() : 0;
-    d.tile = use_tc ? (p->tc_kernel == 2 ? mla::decode_2sm_tile() : 64) : 32;
+    d.tile = use_tc ? 64 : 32;
 
     // tiles, if known on the host
     long long T = -1;
@@ -326,9 +313,7 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
     }
     // with a timer the decode kernel must not overlap the packing kernel, so that the
     // events bracket it exactly
-    if (pl.tc_kernel == 2)
-        e = mla::launch_decode_2sm<T>(d, kv, qpack, a->rope_cos, a->rope_sin, rec_ml, rec_o, a->timer == nullptr, s);
-    else if (pl.use_tc)
+    if (pl.use_tc)
         e = mla::launch_decode_sm100<T>(d, kv, qpack, a->rope_cos, a->rope_sin, rec_ml, rec_o, a->timer == nullptr, s);
     else
         e = mla::launch_decode_simt<T>(d, kv, qpack, a->rope_cos, a->rope_sin, rec_ml, rec_o, s);

@@ -260,12 +260,6 @@ template <typename T>
 cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
                                 const float* sin, float* rec_ml, float* rec_o, bool pdl, cudaStream_t s);
 bool decode_sm100_available();
-// decode_2sm.cu: the CTA-pair (cta_group::2) decode kernel, 128-position tiles
-bool decode_2sm_supported(const DecodePlan& P);
-int decode_2sm_tile();
-template <typename T>
-cudaError_t launch_decode_2sm(const DecodePlan& P, const T* kv, const T* qpack, const float* cos, const float* sin,
-                              float* rec_ml, float* rec_o, bool pdl, cudaStream_t s);
 // cache.cu
 template <typename T>
 cudaError_t launch_cache_append(T* kv, long long stride, long long kv_rows, int dc, int dR, int batch, const T* c_t,

@@ -1,7 +1,6 @@
 // Thin inline-PTX wrappers for the sm_100a features the decode kernels use:
-// mbarriers, TMA tiled loads into the issuing CTA's own shared memory (no multicast anywhere),
-// tcgen05 MMA / TMEM for one CTA and for a CTA pair (cta_group::2), cluster shared memory
-// (mapa, st.async, remote mbarrier arrive).
+// mbarriers, TMA tiled loads into the issuing CTA's own shared memory only,
+// tcgen05 MMA / TMEM, cluster shared memory (mapa, st.async, remote mbarrier arrive).
 //
 // Descriptor encodings (PTX ISA, tcgen05 "matrix descriptors"):
 //   shared-memory descriptor (64 bit):
@@ -166,17 +165,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
         : "memory");
 }
 
-// 2-D tiled load by each CTA of a CTA pair into its own shared memory, with the completion
-// (transaction bytes) counted on an mbarrier of the pair's leader CTA (`leader_bar` from mapa):
-// the form the pair MMAs (cta_group::2) consume. No multicast: every CTA loads its own tile.
-__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap, uint32_t leader_bar, int x, int y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(leader_bar), "r"(x), "r"(y)
-        : "memory");
-}
-
 // ---------------- TMEM / tcgen05 ----------------
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
@@ -194,19 +182,6 @@ __device__ __forceinline__ void tc_fence_before() {
 }
 __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// CTA-pair forms: one warp of each CTA of the pair runs the allocation (same warp index, same
-// destination offset), and the pair's MMAs address both CTAs' tensor memory at the same offset.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
 __host__ __device__ constexpr uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -247,33 +222,6 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-// Pair MMA (cta_group::2), issued by one thread of the leader CTA: M = 128 rows split 64 / 64
-// between the CTAs (each CTA's A rows and D lanes), B's N columns split N/2 / N/2 (each CTA
-// supplies half from its own shared memory at the same offset); each CTA's D holds its 64 rows
-// for all N columns.
-__device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// Arrive once on the mbarrier at offset `bar` in BOTH CTAs of the pair when every pair MMA this
-// thread issued so far has completed (a completion signal, not a data load).
-__device__ __forceinline__ void mma_commit_pair_both(uint32_t bar) {
-    asm volatile(
-        "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
-            bar)
-        : "memory");
-}
-// The same, arriving only on this CTA's barrier.
-__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
 // Arrive (once) on `bar` when all previously issued MMAs of this thread complete.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
