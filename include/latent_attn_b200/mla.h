@@ -19,7 +19,7 @@
  *                             tests/test_python.py:98-99
  *   mla_decode_partial /      no reference counterpart: the two halves of the
  *   mla_combine_partials      KV-range-sharded multi-GPU decode (per-head partial
- *                             (m, l, o_latent) out of one shard; log-sum-exp merge of
+ *   (and their _packed forms) (m, l, o_latent) out of one shard; log-sum-exp merge of
  *                             G shards' partials + the W_UV projection of
  *                             src/fused_mla.cu:258-267)
  *   mla_cache_append          LatentKVCache::append_host (src/mla_config.cuh:58-72),
@@ -207,6 +207,27 @@ MLA_API mla_status_t mla_decode_partial(const mla_config_t* cfg, const mla_decod
 MLA_API mla_status_t mla_combine_partials(const mla_config_t* cfg, mla_dtype_t dtype, int batch,
                                   int num_parts, const float* partial_ml, const float* partial_o,
                                   const void* W_UV, float* output, mla_stream_t stream);
+
+/* KV-range sharding with a head-sliced exchange, step 1: as mla_decode_partial, but every
+ * (b, h) partial is one packed row of d_c + 4 floats [m (natural-log units), l, 0, 0,
+ * o[0 .. d_c)], and the rows are ordered by head slice: the heads are cut into num_slices
+ * equal slices (num_slices divides H; slice q holds heads [q H / num_slices, + H / num_slices)),
+ * and head h of token b is row (q * B + b) * (H / num_slices) + h % (H / num_slices). Slice q is
+ * thus one contiguous block, ready for an all-to-all that sends it to the rank merging those
+ * heads. packed: (num_slices, B, H / num_slices, d_c + 4) fp32, 16-byte aligned. No reference
+ * counterpart (the reference has no multi-GPU path). */
+MLA_API mla_status_t mla_decode_partial_packed(const mla_config_t* cfg, const mla_decode_args_t* a, int num_slices,
+                                       float* packed, void* workspace, size_t workspace_bytes,
+                                       mla_stream_t stream);
+
+/* KV-range sharding with a head-sliced exchange, step 2: merge num_parts packed partial sets
+ * (num_parts, B, heads, d_c + 4) of one head slice (the rows of mla_decode_partial_packed that
+ * all ranks sent for it) and project through that slice's W_UV rows (heads * dv, d_c): output
+ * (B, heads, dv) fp32. The log-sum-exp merge of mla_combine_partials and the projection of
+ * src/fused_mla.cu:258-267, for a subset of the heads. */
+MLA_API mla_status_t mla_combine_partials_packed(const mla_config_t* cfg, mla_dtype_t dtype, int batch,
+                                         int num_parts, int heads, const float* packed, const void* W_UV,
+                                         float* output, mla_stream_t stream);
 
 /* Device-side cache append, one new row per sequence: for each b, the row of position
  * p = seq_lens[b] receives [c_t[b] (d_c) | k_rope[b] (d_R)] (k_rope unrotated, as the cache

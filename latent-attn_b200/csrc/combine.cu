@@ -177,10 +177,26 @@ __device__ void project_rows(int h, int b0, int ntok, int H, int dc, int dv, con
     }
 }
 
+// Row of (b, h) in the partial-set export: (B, H, .) rows of part_ml (2 floats) and part_o (d_c
+// floats), or, with packed_slices > 0, one packed row of d_c + 4 floats [m, l, 0, 0, o] at
+// part_o, rows ordered (head slice q, b, head within the slice) for packed_slices equal slices.
+struct PartOut {
+    float* ml;
+    float* o;
+    int slices;  // 0: separate arrays
+    __device__ long long row(int b, int h, int B, int H) const {
+        if (!slices) return static_cast<long long>(b) * H + h;
+        const int hs = H / slices;
+        return (static_cast<long long>(h / hs) * B + b) * hs + h % hs;
+    }
+    __device__ float* ml_at(long long r, int dc) const { return slices ? o + r * (dc + 4) : ml + r * 2; }
+    __device__ float* o_at(long long r, int dc) const { return slices ? o + r * (dc + 4) + 4 : o + r * dc; }
+};
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
 combine_kernel(DecodePlan P, const float* __restrict__ rec_ml, const float* __restrict__ rec_o,
-               const T* __restrict__ W_UV, float* __restrict__ out, float* part_ml, float* part_o) {
+               const T* __restrict__ W_UV, float* __restrict__ out, PartOut part) {
     extern __shared__ float o_s[];  // kTok * dc
     __shared__ MergeList ml;
     const int h = blockIdx.x, b0 = blockIdx.y * kTok;
@@ -191,8 +207,8 @@ combine_kernel(DecodePlan P, const float* __restrict__ rec_ml, const float* __re
         const float nan = __int_as_float(0x7fc00000);
         for (int i = threadIdx.x; i < ntok * P.dv; i += kThreads)
             if (out) out[(static_cast<long long>(b0 + i / P.dv) * P.H + h) * P.dv + i % P.dv] = nan;
-        if (part_ml && static_cast<int>(threadIdx.x) < ntok)
-            part_ml[(static_cast<long long>(b0 + threadIdx.x) * P.H + h) * 2 + 1] = nan;
+        if (!out && static_cast<int>(threadIdx.x) < ntok)
+            part.ml_at(part.row(b0 + threadIdx.x, h, P.B, P.H), P.dc)[1] = nan;
         return;
     }
     const bool partial = out == nullptr;
@@ -207,15 +223,16 @@ combine_kernel(DecodePlan P, const float* __restrict__ rec_ml, const float* __re
             const int rec = ml.rec[t][k];
             if (rec >= 0) a = fmaf(ml.wgt[t][k], rec_o[(static_cast<long long>(rec) * kGroupRows + r) * P.dc + c], a);
         }
-        if (partial) part_o[(static_cast<long long>(b0 + t) * P.H + h) * P.dc + c] = a;
+        if (partial) part.o_at(part.row(b0 + t, h, P.B, P.H), P.dc)[c] = a;
         else o_s[t * P.dc + c] = a;
     }
     if (partial) {
         if (static_cast<int>(threadIdx.x) < ntok) {
             const int t = threadIdx.x;
-            float* pm = part_ml + (static_cast<long long>(b0 + t) * P.H + h) * 2;
+            float* pm = part.ml_at(part.row(b0 + t, h, P.B, P.H), P.dc);
             pm[0] = ml.l[t] > 0.f ? ml.m[t] * kLn2 : -INFINITY;  // natural-log units for the caller
             pm[1] = ml.l[t];
+            if (part.slices) pm[2] = pm[3] = 0.f;
         }
         return;
     }
@@ -226,7 +243,8 @@ combine_kernel(DecodePlan P, const float* __restrict__ rec_ml, const float* __re
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
 combine_parts_kernel(int B, int H, int dc, int dv, int parts, const float* __restrict__ part_ml,
-                     const float* __restrict__ part_o, const T* __restrict__ W_UV, float* __restrict__ out) {
+                     const float* __restrict__ part_o, int ml_stride, int o_stride, const T* __restrict__ W_UV,
+                     float* __restrict__ out) {
     extern __shared__ float o_s[];
     __shared__ float wgt[kTok][64];
     const int h = blockIdx.x, b0 = blockIdx.y * kTok;
@@ -237,14 +255,14 @@ combine_parts_kernel(int B, int H, int dc, int dv, int parts, const float* __res
         const long long bh = static_cast<long long>(b0 + warp) * H + h;
         float M = -INFINITY;
         for (int p = lane; p < parts; p += 32) {
-            const float* pm = part_ml + (p * stride + bh) * 2;
+            const float* pm = part_ml + (p * stride + bh) * ml_stride;
             if (pm[1] > 0.f) M = fmaxf(M, pm[0]);
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
         float L = 0.f;
         for (int p = lane; p < parts; p += 32) {
-            const float* pm = part_ml + (p * stride + bh) * 2;
+            const float* pm = part_ml + (p * stride + bh) * ml_stride;
             const float a = pm[1] > 0.f ? expf(pm[0] - M) : 0.f;
             wgt[warp][p] = a;
             L += a * pm[1];
@@ -260,7 +278,7 @@ combine_parts_kernel(int B, int H, int dc, int dv, int parts, const float* __res
         const int t = i / dc, c = i % dc;
         const long long bh = static_cast<long long>(b0 + t) * H + h;
         float a = 0.f;
-        for (int p = 0; p < parts; ++p) a = fmaf(wgt[t][p], part_o[(p * stride + bh) * dc + c], a);
+        for (int p = 0; p < parts; ++p) a = fmaf(wgt[t][p], part_o[(p * stride + bh) * o_stride + c], a);
         o_s[t * dc + c] = a;
     }
     __syncthreads();
@@ -269,37 +287,40 @@ combine_parts_kernel(int B, int H, int dc, int dv, int parts, const float* __res
 
 template <typename T>
 cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
-                           float* out, float* part_ml, float* part_o, cudaStream_t s) {
+                           float* out, float* part_ml, float* part_o, int packed_slices, cudaStream_t s) {
     if (P.W > kMaxRec) return cudaErrorInvalidValue;
     const size_t smem = static_cast<size_t>(kTok) * P.dc * sizeof(float);
     cudaError_t e =
         ensure_dynamic_smem(reinterpret_cast<const void*>(combine_kernel<T>), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     dim3 grid(P.H, ceil_div(P.B, kTok));
-    combine_kernel<T><<<grid, kThreads, smem, s>>>(P, rec_ml, rec_o, W_UV, out, part_ml, part_o);
+    PartOut part{part_ml, part_o, packed_slices};
+    combine_kernel<T><<<grid, kThreads, smem, s>>>(P, rec_ml, rec_o, W_UV, out, part);
     count_launches(1);
     return cudaGetLastError();
 }
 
 template <typename T>
 cudaError_t launch_combine_parts(int B, int H, int dc, int dv, int parts, const float* part_ml,
-                                 const float* part_o, const T* W_UV, float* out, cudaStream_t s) {
+                                 const float* part_o, int ml_stride, int o_stride, const T* W_UV, float* out,
+                                 cudaStream_t s) {
     if (parts > 64) return cudaErrorInvalidValue;
     const size_t smem = static_cast<size_t>(kTok) * dc * sizeof(float);
     cudaError_t e =
         ensure_dynamic_smem(reinterpret_cast<const void*>(combine_parts_kernel<T>), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     dim3 grid(H, ceil_div(B, kTok));
-    combine_parts_kernel<T><<<grid, kThreads, smem, s>>>(B, H, dc, dv, parts, part_ml, part_o, W_UV, out);
+    combine_parts_kernel<T><<<grid, kThreads, smem, s>>>(B, H, dc, dv, parts, part_ml, part_o, ml_stride, o_stride,
+                                                         W_UV, out);
     count_launches(1);
     return cudaGetLastError();
 }
 
 #define MLA_INST(T)                                                                                   \
     template cudaError_t launch_combine<T>(const DecodePlan&, const float*, const float*, const T*,  \
-                                           float*, float*, float*, cudaStream_t);                    \
+                                           float*, float*, float*, int, cudaStream_t);               \
     template cudaError_t launch_combine_parts<T>(int, int, int, int, int, const float*, const float*, \
-                                                 const T*, float*, cudaStream_t);
+                                                 int, int, const T*, float*, cudaStream_t);
 MLA_INST(__half)
 MLA_INST(__nv_bfloat16)
 #undef MLA_INST

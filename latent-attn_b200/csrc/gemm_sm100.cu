@@ -263,9 +263,10 @@ template <typename T>
 __global__ void __launch_bounds__(32 * kProjWarps)
 project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
                      const float* __restrict__ rec_o, float* __restrict__ out, int ntp, uint32_t tmem_cols,
-                     int parts) {
+                     int parts, int ml_stride, int o_stride) {
     // parts == 0: the decode kernel's partial records (m in log2 units, record g + w of group g).
-    // parts > 0: that many partial sets in the layout of mla_decode_partial, [part][B][H] rows with
+    // parts > 0: that many partial sets of [part][B][H] rows (m, l at rec_ml + row * ml_stride, o at
+    // rec_o + row * o_stride: the separate arrays of mla_decode_partial or its packed rows), with
     // m in natural-log units and l = 0 for an empty part (the KV-range shards' merge).
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -411,13 +412,13 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                 for (int j = 0; j < 2; ++j)
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
-                        mlq[j][q] = vq[j][q] ? __ldg(reinterpret_cast<const float2*>(rec_ml + rq[j][q] * 2))
+                        mlq[j][q] = vq[j][q] ? __ldg(reinterpret_cast<const float2*>(rec_ml + rq[j][q] * ml_stride))
                                              : make_float2(-INFINITY, 0.f);
 #pragma unroll
                         for (int u4 = 0; u4 < 4; ++u4) {
                             const int u = lane + 32 * u4;
                             v[j][q][u4] = (vq[j][q] && u < U)
-                                              ? __ldg(reinterpret_cast<const float4*>(rec_o + rq[j][q] * dc) + u)
+                                              ? __ldg(reinterpret_cast<const float4*>(rec_o + rq[j][q] * o_stride) + u)
                                               : zero4;
                         }
                     }
@@ -625,7 +626,7 @@ cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const 
 
 template <typename T>
 cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
-                                float* out, bool pdl, int parts, cudaStream_t s) {
+                                float* out, bool pdl, int parts, int ml_stride, int o_stride, cudaStream_t s) {
     CUtensorMap tmap;
     if (!make_tmap_2d_16b(&tmap, W_UV, static_cast<uint64_t>(P.H) * P.dv, static_cast<uint64_t>(P.dc),
                           static_cast<uint64_t>(P.dc), static_cast<uint32_t>(P.dv), 64))
@@ -638,7 +639,7 @@ cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const 
     if (e != cudaSuccess) return e;
     dim3 grid(ceil_div(P.B, kProjTok), P.H);
     e = launch_ex(project_sm100_kernel<T>, grid, dim3(32 * kProjWarps), smem, s, pdl, tmap, P, rec_ml, rec_o, out, ntp,
-                  tmem_cols_for(ntp), parts);
+                  tmem_cols_for(ntp), parts, ml_stride, o_stride);
     count_launches(1);
     return e != cudaSuccess ? e : cudaGetLastError();
 }
@@ -647,7 +648,7 @@ template <typename T>
 cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
                                  float* out, bool pdl, cudaStream_t s) {
     if (!project_sm100_supported(P)) return cudaErrorInvalidValue;
-    return launch_project_impl<T>(P, rec_ml, rec_o, W_UV, out, pdl, 0, s);
+    return launch_project_impl<T>(P, rec_ml, rec_o, W_UV, out, pdl, 0, 2, P.dc, s);
 }
 
 // Status word of the partial-set merge: that path has no decode status to check, but the
@@ -660,7 +661,8 @@ bool project_parts_sm100_supported(int H, int dc, int dv, int parts) {
 
 template <typename T>
 cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, const float* part_ml,
-                                       const float* part_o, const T* W_UV, float* out, cudaStream_t s) {
+                                       const float* part_o, int ml_stride, int o_stride, const T* W_UV, float* out,
+                                       cudaStream_t s) {
     if (!project_parts_sm100_supported(H, dc, dv, parts)) return cudaErrorInvalidValue;
     static std::mutex mu;
     static std::vector<int*> status_addr;  // per device
@@ -686,7 +688,7 @@ cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, 
     P.B = B;
     P.head_blocks = ceil_div(H, kGroupRows);
     P.status = status;
-    return launch_project_impl<T>(P, part_ml, part_o, W_UV, out, false, parts, s);
+    return launch_project_impl<T>(P, part_ml, part_o, W_UV, out, false, parts, ml_stride, o_stride, s);
 }
 
 #define MLA_INST(T)                                                                                              \
@@ -694,7 +696,8 @@ cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, 
                                                 int*, cudaStream_t);                                             \
     template cudaError_t launch_project_sm100<T>(const DecodePlan&, const float*, const float*, const T*, float*,   \
                                                  bool, cudaStream_t);                                             \
-    template cudaError_t launch_project_parts_sm100<T>(int, int, int, int, int, const float*, const float*, const T*, \
+    template cudaError_t launch_project_parts_sm100<T>(int, int, int, int, int, const float*, const float*, int, int, \
+                                                       const T*, \
                                                        float*, cudaStream_t);
 MLA_INST(__half)
 MLA_INST(__nv_bfloat16)

@@ -284,7 +284,7 @@ cudaError_t timer_record(cudaEvent_t ev, cudaStream_t s) {
 
 template <typename T>
 mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned char* ws, float* out,
-                        float* part_ml, float* part_o, cudaStream_t s) {
+                        float* part_ml, float* part_o, int packed_slices, cudaStream_t s) {
     mla::DecodePlan d = pl.dp;
     int* prefix = reinterpret_cast<int*>(ws + pl.off_prefix);
     d.tile_prefix = d.uniform_len > 0 ? nullptr : prefix;
@@ -328,14 +328,15 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
     if (out && pl.use_gemm_project)
         e = mla::launch_project_sm100<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, true, s);
     else
-        e = mla::launch_combine<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, part_ml, part_o, s);
+        e = mla::launch_combine<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, part_ml, part_o,
+                                   packed_slices, s);
     if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
     return MLA_OK;
 }
 
 mla_status_t decode_impl(const mla_config_t* cfg, const mla_decode_args_t* a, void* workspace,
                          size_t ws_bytes, float* out, float* part_ml, float* part_o, cudaStream_t s,
-                         int max_workers = 0) {
+                         int max_workers = 0, int packed_slices = 0) {
     Plan pl;
     mla_status_t st = make_plan(cfg, a, &pl, max_workers);
     if (st != MLA_OK) return st;
@@ -345,8 +346,9 @@ mla_status_t decode_impl(const mla_config_t* cfg, const mla_decode_args_t* a, vo
     if (ws_bytes < pl.total)
         return fail(MLA_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", ws_bytes, pl.total);
     unsigned char* ws = static_cast<unsigned char*>(workspace);
-    if (a->dtype == MLA_DTYPE_BF16) return run_decode<__nv_bfloat16>(pl, a, ws, out, part_ml, part_o, s);
-    return run_decode<__half>(pl, a, ws, out, part_ml, part_o, s);
+    if (a->dtype == MLA_DTYPE_BF16)
+        return run_decode<__nv_bfloat16>(pl, a, ws, out, part_ml, part_o, packed_slices, s);
+    return run_decode<__half>(pl, a, ws, out, part_ml, part_o, packed_slices, s);
 }
 
 // Scratch for the reference-shaped launchers, whose signatures carry no workspace.
@@ -393,6 +395,41 @@ mla_status_t noalloc_scratch(void** out) {
     return MLA_OK;
 }
 
+// Merge `num_parts` partial sets of (B, heads) rows and project with W_UV (heads * dv, d_c):
+// m, l at part_ml + row * ml_stride, o at part_o + row * o_stride.
+mla_status_t combine_impl(const mla_config_t* cfg, mla_dtype_t dtype, int batch, int num_parts, int heads,
+                          const float* part_ml, const float* part_o, int ml_stride, int o_stride,
+                          const void* W_UV, float* output, cudaStream_t s) {
+    mla_status_t st = validate_cfg(cfg);
+    if (st != MLA_OK) return st;
+    if (batch <= 0 || num_parts <= 0 || heads <= 0)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "batch, num_parts and heads must be positive");
+    if (!part_ml || !part_o || !W_UV || !output) return fail(MLA_ERR_INVALID_ARGUMENT, "null pointer");
+    if (cfg->kv_lora_rank > 1024 || cfg->v_head_dim > 256)
+        return fail(MLA_ERR_UNSUPPORTED, "kv_lora_rank <= 1024 and v_head_dim <= 256 required");
+    if (dtype != MLA_DTYPE_BF16 && dtype != MLA_DTYPE_F16) return fail(MLA_ERR_UNSUPPORTED, "dtype must be F16 or BF16");
+    DeviceInfo di;
+    if (!device_info(&di)) return fail(MLA_ERR_CUDA, "no CUDA device");
+    const int dc = cfg->kv_lora_rank, dv = cfg->v_head_dim;
+    // tcgen05 merge + W_UV GEMM when the shape fits, else the CUDA-core combine
+    const bool gemm = di.major == 10 && env_gemm_enabled() && mla::project_parts_sm100_supported(heads, dc, dv, num_parts);
+    cudaError_t e;
+    if (gemm && dtype == MLA_DTYPE_BF16)
+        e = mla::launch_project_parts_sm100<__nv_bfloat16>(batch, heads, dc, dv, num_parts, part_ml, part_o, ml_stride,
+                                                          o_stride, static_cast<const __nv_bfloat16*>(W_UV), output, s);
+    else if (gemm)
+        e = mla::launch_project_parts_sm100<__half>(batch, heads, dc, dv, num_parts, part_ml, part_o, ml_stride, o_stride,
+                                                   static_cast<const __half*>(W_UV), output, s);
+    else if (dtype == MLA_DTYPE_BF16)
+        e = mla::launch_combine_parts<__nv_bfloat16>(batch, heads, dc, dv, num_parts, part_ml, part_o, ml_stride,
+                                                     o_stride, static_cast<const __nv_bfloat16*>(W_UV), output, s);
+    else
+        e = mla::launch_combine_parts<__half>(batch, heads, dc, dv, num_parts, part_ml, part_o, ml_stride, o_stride,
+                                              static_cast<const __half*>(W_UV), output, s);
+    if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
+    return MLA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -429,37 +466,32 @@ mla_status_t mla_combine_partials(const mla_config_t* cfg, mla_dtype_t dtype, in
                                   float* output, mla_stream_t stream) {
     mla_status_t st = validate_cfg(cfg);
     if (st != MLA_OK) return st;
-    if (batch <= 0 || num_parts <= 0) return fail(MLA_ERR_INVALID_ARGUMENT, "batch and num_parts must be positive");
-    if (!partial_ml || !partial_o || !W_UV || !output) return fail(MLA_ERR_INVALID_ARGUMENT, "null pointer");
-    if (cfg->kv_lora_rank > 1024 || cfg->v_head_dim > 256)
-        return fail(MLA_ERR_UNSUPPORTED, "kv_lora_rank <= 1024 and v_head_dim <= 256 required");
-    if (dtype != MLA_DTYPE_BF16 && dtype != MLA_DTYPE_F16) return fail(MLA_ERR_UNSUPPORTED, "dtype must be F16 or BF16");
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    DeviceInfo di;
-    if (!device_info(&di)) return fail(MLA_ERR_CUDA, "no CUDA device");
-    // tcgen05 merge + W_UV GEMM when the shape fits, else the CUDA-core combine
-    const bool gemm = di.major == 10 && env_gemm_enabled() &&
-                      mla::project_parts_sm100_supported(cfg->num_heads, cfg->kv_lora_rank, cfg->v_head_dim,
-                                                         num_parts);
-    cudaError_t e;
-    if (gemm && dtype == MLA_DTYPE_BF16)
-        e = mla::launch_project_parts_sm100<__nv_bfloat16>(batch, cfg->num_heads, cfg->kv_lora_rank,
-                                                          cfg->v_head_dim, num_parts, partial_ml, partial_o,
-                                                          static_cast<const __nv_bfloat16*>(W_UV), output, s);
-    else if (gemm)
-        e = mla::launch_project_parts_sm100<__half>(batch, cfg->num_heads, cfg->kv_lora_rank, cfg->v_head_dim,
-                                                   num_parts, partial_ml, partial_o,
-                                                   static_cast<const __half*>(W_UV), output, s);
-    else if (dtype == MLA_DTYPE_BF16)
-        e = mla::launch_combine_parts<__nv_bfloat16>(batch, cfg->num_heads, cfg->kv_lora_rank, cfg->v_head_dim,
-                                                     num_parts, partial_ml, partial_o,
-                                                     static_cast<const __nv_bfloat16*>(W_UV), output, s);
-    else if (dtype == MLA_DTYPE_F16)
-        e = mla::launch_combine_parts<__half>(batch, cfg->num_heads, cfg->kv_lora_rank, cfg->v_head_dim,
-                                              num_parts, partial_ml, partial_o,
-                                              static_cast<const __half*>(W_UV), output, s);
-    if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
-    return MLA_OK;
+    return combine_impl(cfg, dtype, batch, num_parts, cfg->num_heads, partial_ml, partial_o, 2, cfg->kv_lora_rank, W_UV,
+                        output, reinterpret_cast<cudaStream_t>(stream));
+}
+
+mla_status_t mla_decode_partial_packed(const mla_config_t* cfg, const mla_decode_args_t* a, int num_slices,
+                                       float* packed, void* workspace, size_t workspace_bytes, mla_stream_t stream) {
+    mla_status_t st = validate_cfg(cfg);
+    if (st != MLA_OK) return st;
+    if (!packed) return fail(MLA_ERR_INVALID_ARGUMENT, "packed output is null");
+    if (num_slices <= 0 || cfg->num_heads % num_slices != 0)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "num_slices (%d) must divide num_heads (%d)", num_slices, cfg->num_heads);
+    if (reinterpret_cast<uintptr_t>(packed) % 16 != 0) return fail(MLA_ERR_INVALID_ARGUMENT, "packed must be 16-byte aligned");
+    return decode_impl(cfg, a, workspace, workspace_bytes, nullptr, nullptr, packed,
+                       reinterpret_cast<cudaStream_t>(stream), 0, num_slices);
+}
+
+mla_status_t mla_combine_partials_packed(const mla_config_t* cfg, mla_dtype_t dtype, int batch, int num_parts,
+                                         int heads, const float* packed, const void* W_UV, float* output,
+                                         mla_stream_t stream) {
+    mla_status_t st = validate_cfg(cfg);
+    if (st != MLA_OK) return st;
+    if (!packed) return fail(MLA_ERR_INVALID_ARGUMENT, "packed input is null");
+    if (reinterpret_cast<uintptr_t>(packed) % 16 != 0) return fail(MLA_ERR_INVALID_ARGUMENT, "packed must be 16-byte aligned");
+    const int row = cfg->kv_lora_rank + 4;
+    return combine_impl(cfg, dtype, batch, num_parts, heads, packed, packed + 4, row, row, W_UV, output,
+                        reinterpret_cast<cudaStream_t>(stream));
 }
 
 mla_status_t mla_cache_append(const mla_config_t* cfg, mla_dtype_t dtype, void* kv_cache, int64_t kv_row_stride,

@@ -243,12 +243,13 @@ cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const 
 template <typename T>
 cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
                                  float* out, bool pdl, cudaStream_t s);
-// merge of gathered partial sets part_ml[parts][B][H][2] (natural-log max, sum; sum 0 = empty)
-// and part_o[parts][B][H][dc], followed by the W_UV projection
+// merge of gathered partial sets of [parts][B][H] rows -- (m natural-log max, l sum; l = 0 = empty)
+// at part_ml + row * ml_stride and o at part_o + row * o_stride -- followed by the W_UV projection
 bool project_parts_sm100_supported(int H, int dc, int dv, int parts);
 template <typename T>
 cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, const float* part_ml,
-                                       const float* part_o, const T* W_UV, float* out, cudaStream_t s);
+                                       const float* part_o, int ml_stride, int o_stride, const T* W_UV, float* out,
+                                       cudaStream_t s);
 // decode_simt.cu
 template <typename T>
 cudaError_t launch_decode_simt(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
@@ -266,12 +267,16 @@ cudaError_t launch_cache_append(T* kv, long long stride, long long kv_rows, int 
                                 const T* k_rope, const int64_t* offs, const int* pages, int page_rows, int max_pages,
                                 int* seq_lens, int max_len, int* status, cudaStream_t s);
 // combine.cu
+// out == nullptr: export one partial per (b, h) instead, to part_ml (B, H, 2) / part_o (B, H, dc),
+// or with packed_slices > 0 to packed rows of dc + 4 floats at part_o (see mla_decode_partial_packed)
 template <typename T>
 cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const float* rec_o,
-                           const T* W_UV, float* out, float* part_ml, float* part_o, cudaStream_t s);
+                           const T* W_UV, float* out, float* part_ml, float* part_o, int packed_slices,
+                           cudaStream_t s);
 template <typename T>
 cudaError_t launch_combine_parts(int B, int H, int dc, int dv, int parts, const float* part_ml,
-                                 const float* part_o, const T* W_UV, float* out, cudaStream_t s);
+                                 const float* part_o, int ml_stride, int o_stride, const T* W_UV, float* out,
+                                 cudaStream_t s);
 
 // Raises a kernel's dynamic shared-memory limit once per device: the attribute persists,
 // and setting it on every launch would cost host time in every decode call.

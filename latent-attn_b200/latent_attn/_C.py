@@ -390,6 +390,58 @@ def mla_decode_partial(kv_cache, q_rope, W_UV, rope_cos, rope_sin, d_model, kv_l
     return ml, o
 
 
+def mla_decode_partial_packed(kv_cache, q_rope, W_UV, rope_cos, rope_sin, d_model, kv_lora_rank,
+                              qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim, *, num_slices: int,
+                              q_absorbed=None, q_nope=None, W_UK=None, kv_pos_offset: int = 0,
+                              softmax_scale: float = 0.0, workspace=None, kernel: int = 0, timer=None,
+                              rope_theta: float = 0.0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``mla_decode_partial`` with the partials packed for a head-sliced exchange: returns
+    (num_slices, B, H / num_slices, d_c + 4) fp32 rows [m, l, 0, 0, o] (m in natural-log
+    units), slice q holding heads [q H / num_slices, (q + 1) H / num_slices)."""
+    _check_half(kv_cache, "kv_cache")
+    _check_tables(rope_cos, rope_sin)
+    cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    B = q_rope.size(0)
+    L = kv_cache.size(0) // B
+    if num_slices <= 0 or num_heads % num_slices:
+        raise RuntimeError(f"num_slices ({num_slices}) must divide num_heads ({num_heads})")
+    shape = (num_slices, B, num_heads // num_slices, kv_lora_rank + 4)
+    if out is None:
+        out = torch.empty(shape, dtype=torch.float32, device=kv_cache.device)
+    elif tuple(out.shape) != shape or out.dtype != torch.float32 or not out.is_contiguous():
+        raise RuntimeError(f"out must be a contiguous float32 tensor of shape {shape}")
+    args = _decode_args(kv_cache.dtype, B, False, kv_cache, L, q_rope, W_UV, rope_cos, rope_sin, None,
+                        q_absorbed=q_absorbed, q_nope=None if q_absorbed is not None else q_nope,
+                        W_UK=None if q_absorbed is not None else W_UK, kv_pos_offset=kv_pos_offset,
+                        softmax_scale=softmax_scale, kernel=kernel, timer=timer, rope_theta=rope_theta)
+    ws = _workspace(cfg, args, kv_cache.device, workspace)
+    _lib.check(_lib.load().mla_decode_partial_packed(C.byref(cfg), C.byref(args), int(num_slices),
+                                                     C.c_void_p(out.data_ptr()), C.c_void_p(ws.data_ptr()),
+                                                     C.c_size_t(ws.numel()), C.c_void_p(_stream(kv_cache.device))))
+    return out
+
+
+def mla_combine_partials_packed(packed: torch.Tensor, W_UV_slice: torch.Tensor, d_model, kv_lora_rank,
+                                qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim,
+                                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Merge packed partial sets (P, B, heads, d_c + 4) of one head slice and project with that
+    slice's W_UV rows (heads * dv, d_c) -> (B, heads, dv) fp32."""
+    _check_f32(packed, "packed")
+    _check_half(W_UV_slice, "W_UV_slice")
+    cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    if packed.dim() != 4 or packed.size(3) != kv_lora_rank + 4:
+        raise RuntimeError("packed must be (parts, batch, heads, kv_lora_rank + 4)")
+    P, B, heads = packed.size(0), packed.size(1), packed.size(2)
+    if W_UV_slice.dim() != 2 or W_UV_slice.size(0) != heads * v_head_dim or W_UV_slice.size(1) != kv_lora_rank:
+        raise RuntimeError("W_UV_slice must be (heads * v_head_dim, kv_lora_rank)")
+    if out is None:
+        out = torch.empty(B, heads, v_head_dim, dtype=torch.float32, device=packed.device)
+    _lib.check(_lib.load().mla_combine_partials_packed(C.byref(cfg), _DT[W_UV_slice.dtype], B, P, heads,
+                                                       C.c_void_p(packed.data_ptr()), C.c_void_p(W_UV_slice.data_ptr()),
+                                                       C.c_void_p(out.data_ptr()), C.c_void_p(_stream(packed.device))))
+    return out
+
+
 def mla_combine_partials(part_ml: torch.Tensor, part_o: torch.Tensor, W_UV: torch.Tensor, d_model,
                          kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim,
                          out: Optional[torch.Tensor] = None) -> torch.Tensor:

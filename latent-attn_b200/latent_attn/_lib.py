@@ -82,6 +82,10 @@ SIGNATURES = {
                                      C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "mla_combine_partials": (C.c_int, [C.POINTER(MlaConfig), C.c_int, C.c_int, C.c_int, C.c_void_p,
                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "mla_decode_partial_packed": (C.c_int, [C.POINTER(MlaConfig), C.POINTER(MlaDecodeArgs), C.c_int, C.c_void_p,
+                                            C.c_void_p, C.c_size_t, C.c_void_p]),
+    "mla_combine_partials_packed": (C.c_int, [C.POINTER(MlaConfig), C.c_int, C.c_int, C.c_int, C.c_int,
+                                              C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "mla_cache_append": (C.c_int, [C.POINTER(MlaConfig), C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_int,
                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                    C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),

@@ -8,16 +8,22 @@ the GPUs of one node are provided here:
   ``lpt_shard`` assigns sequences longest-first to the least-loaded rank, so
   the per-rank sums of cache rows (the work) are balanced.
 * **KV-range sharding** (one sequence too long for one GPU's share of the step).
-  Rank ``r`` holds rows ``kv_range(L, world, r)`` of the cache, decodes them
-  with ``mla_decode_partial`` (positions offset by the range start, so RoPE
-  angles match a single-GPU decode), and the per-head partials -- max ``m``,
-  sum of exponentials ``l`` and the unnormalised latent sum ``o`` (512 floats
-  per head) -- are exchanged with one all-gather. Every rank then merges all
-  ranks' partials with ``mla_combine_partials`` (log-sum-exp merge + W_UV), so
-  every rank ends with the full output.
+  Rank ``r`` holds rows ``kv_range(L, world, r)`` of the cache and decodes them
+  with positions offset by the range start (so RoPE angles match a single-GPU
+  decode) into per-head partials: max ``m``, sum of exponentials ``l`` and the
+  unnormalised latent sum ``o`` (512 floats per head). The heads are then split
+  over the ranks: ``mla_decode_partial_packed`` writes the partials as packed
+  rows grouped by head slice, one all-to-all (``exchange_head_slices``) brings
+  every rank the partials of its own ``H / world`` heads from all ranks, the rank
+  merges them and projects through its slice of W_UV
+  (``mla_combine_partials_packed``), and an all-gather of the 128-wide outputs
+  (``gather_head_slices``) gives every rank the full output.
 
-The all-gather moves ``world * B * H * (2 + d_c) * 4`` bytes (1 MiB for one
-DeepSeek-V2 token on 4 GPUs), small next to the cache each rank streams.
+The all-to-all moves ``B * H * (d_c + 4) * 4 * (world - 1) / world`` bytes per
+rank (about 0.25 MiB for one DeepSeek-V2 token), the output all-gather
+``B * H * dv * 4`` bytes, and each rank merges and projects only its slice of
+the heads. With a head count the ranks do not divide, the partials are
+all-gathered instead and every rank merges all of them (``gather_partials``).
 """
 
 from __future__ import annotations
@@ -83,38 +89,98 @@ def gather_partials(ml: torch.Tensor, o: torch.Tensor, group=None,
     return out_ml, out_o
 
 
+def packed_row(b: int, h: int, batch: int, heads: int, slices: int) -> int:
+    """Row of (token b, head h) in the packed partial layout of ``mla_decode_partial_packed``:
+    rows ordered (head slice, token, head within the slice), ``heads / slices`` heads a slice."""
+    hs = heads // slices
+    return ((h // hs) * batch + b) * hs + h % hs
+
+
+def exchange_head_slices(packed: torch.Tensor, group=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """All-to-all of packed partials: ``packed`` is (world, B, H / world, R) with block q holding the
+    heads of rank q; the result is (world, B, H / world, R) with block p holding rank p's partials
+    of this rank's heads. A collective: every rank calls it in the same order."""
+    world = dist.get_world_size(group)
+    if packed.shape[0] != world:
+        raise ValueError("packed partials must have world_size head slices as their leading dimension")
+    if out is None:
+        out = torch.empty_like(packed)
+    dist.all_to_all_single(out, packed, group=group)
+    return out
+
+
+def gather_head_slices(o_slice: torch.Tensor, group=None, out: Optional[torch.Tensor] = None,
+                       staging: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """All-gather every rank's output slice (B, H / world, dv), in rank (= head) order, into the full
+    (B, H, dv) output. With one token the slices land in place; otherwise through ``staging``
+    (world, B, H / world, dv) and one reordering copy."""
+    world = dist.get_world_size(group)
+    B, hs, dv = o_slice.shape
+    if out is None:
+        out = torch.empty(B, world * hs, dv, dtype=o_slice.dtype, device=o_slice.device)
+    if B == 1:
+        dist.all_gather_into_tensor(out.view(world * hs, dv), o_slice.view(hs, dv), group=group)
+        return out
+    if staging is None:
+        staging = torch.empty((world,) + tuple(o_slice.shape), dtype=o_slice.dtype, device=o_slice.device)
+    dist.all_gather_into_tensor(staging.view(world * B, hs, dv), o_slice.contiguous(), group=group)
+    out.copy_(staging.permute(1, 0, 2, 3).reshape(B, world * hs, dv))
+    return out
+
+
 class KVRangeDecoder:
     """Decode one token per sequence over a cache whose rows are split across ranks.
 
     ``kv_local`` holds this rank's rows ``[pos_offset, pos_offset + n)`` of every
     sequence (B sequences of ``n`` rows each, packed). ``rope_cos`` / ``rope_sin``
-    are the full tables (they are indexed by absolute position). The gather
-    buffers are allocated on the first call and reused.
+    are the full tables (they are indexed by absolute position), or both None for
+    on-the-fly RoPE. Exchange buffers are allocated on the first call and reused.
+    When the ranks divide the heads, each rank merges and projects its slice of the
+    heads (one all-to-all, one output all-gather); otherwise every rank merges all
+    partials after an all-gather.
     """
 
     def __init__(self, cfg, group=None):
         self.cfg = cfg
         self.group = group
-        self._ml = None
-        self._o = None
+        self._buf = {}
+
+    def _get(self, name, shape, like):
+        t = self._buf.get(name)
+        if t is None or tuple(t.shape) != tuple(shape) or t.device != like.device:
+            t = torch.empty(shape, dtype=torch.float32, device=like.device)
+            self._buf[name] = t
+        return t
 
     def __call__(self, kv_local: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
-                 rope_cos: torch.Tensor, rope_sin: torch.Tensor, *, pos_offset: int,
+                 rope_cos: Optional[torch.Tensor], rope_sin: Optional[torch.Tensor], *, pos_offset: int,
                  q_absorbed: Optional[torch.Tensor] = None, q_nope: Optional[torch.Tensor] = None,
                  W_UK: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
                  workspace: Optional[torch.Tensor] = None, timer=None) -> torch.Tensor:
         from latent_attn import _C
         c = self.cfg
         dims = (c.d_model, c.kv_lora_rank, c.qk_nope_head_dim, c.qk_rope_head_dim, c.num_heads, c.v_head_dim)
+        world = dist.get_world_size(self.group)
+        rank = dist.get_rank(self.group)
+        B, H, dc, dv = q_rope.size(0), c.num_heads, c.kv_lora_rank, c.v_head_dim
+        if H % world == 0:
+            hs = H // world
+            send = self._get("send", (world, B, hs, dc + 4), q_rope)
+            _C.mla_decode_partial_packed(kv_local, q_rope, W_UV, rope_cos, rope_sin, *dims, num_slices=world,
+                                         q_absorbed=q_absorbed, q_nope=q_nope, W_UK=W_UK,
+                                         kv_pos_offset=pos_offset, workspace=workspace, timer=timer, out=send)
+            recv = exchange_head_slices(send, self.group, out=self._get("recv", send.shape, q_rope))
+            o_slice = _C.mla_combine_partials_packed(recv, W_UV[rank * hs * dv:(rank + 1) * hs * dv], *dims,
+                                                     out=self._get("slice", (B, hs, dv), q_rope))
+            staging = self._get("stage", (world, B, hs, dv), q_rope) if B > 1 else None
+            return gather_head_slices(o_slice, self.group, out=out, staging=staging)
         ml, o = _C.mla_decode_partial(kv_local, q_rope, W_UV, rope_cos, rope_sin, *dims,
                                       q_absorbed=q_absorbed, q_nope=q_nope, W_UK=W_UK,
                                       kv_pos_offset=pos_offset, workspace=workspace, timer=timer)
-        world = dist.get_world_size(self.group)
-        if self._ml is None or self._ml.shape[1:] != ml.shape or self._ml.device != ml.device:
-            self._ml = torch.empty((world,) + tuple(ml.shape), dtype=ml.dtype, device=ml.device)
-            self._o = torch.empty((world,) + tuple(o.shape), dtype=o.dtype, device=o.device)
-        gml, go = gather_partials(ml, o, self.group, self._ml, self._o)
+        gml, go = gather_partials(ml, o, self.group, self._get("gml", (world,) + tuple(ml.shape), ml),
+                                  self._get("go", (world,) + tuple(o.shape), o))
         return _C.mla_combine_partials(gml, go, W_UV, *dims, out=out)
 
 
-__all__ = ["lpt_shard", "kv_range", "gather_partials", "KVRangeDecoder"]
+__all__ = ["lpt_shard", "kv_range", "gather_partials", "packed_row", "exchange_head_slices", "gather_head_slices",
+           "KVRangeDecoder"]

@@ -150,3 +150,59 @@ def _batch_worker(rank, world, port, lens, seed):
 
 def test_batch_shards_reassemble_to_the_single_device_decode():
     _spawn(_batch_worker, 2, [300, 17, 129, 64, 1, 250], 11)
+
+
+def _kv_range_sliced_worker(rank, world, port, L, B, seed):
+    """Head-sliced exchange: packed partials (mla_decode_partial_packed's layout), one all-to-all,
+    a per-rank merge + W_UV of its heads (the oracle stands in for mla_combine_partials_packed),
+    and the output all-gather give the single-device decode on every rank."""
+    _init(rank, world, port)
+    try:
+        inp = synthetic.baseline_inputs(num_heads=H, seq_lens=[L] * B, seed=seed)
+        kv = inp.kv_cache.float().numpy()
+        q_abs = O.absorb_query(inp.q_nope.float().numpy(), inp.W_UK.float().numpy(), H, DC)
+        q_rope = inp.q_rope.float().numpy()
+        W_UV = inp.W_UV.float().numpy()
+        cos, sin = O.rope_tables(L, DR)
+        lo, hi = D.kv_range(L, world, rank)
+        hs = H // world
+        R = DC + 4
+        send = np.zeros((world * B * hs, R), dtype=np.float32)
+        for b in range(B):
+            rows = kv[b * L + lo:b * L + hi]
+            m, l, o = O.split_partials(rows, q_abs[b], q_rope[b], cos[lo:hi], sin[lo:hi], DC, SCALE, [0, hi - lo])
+            for h in range(H):
+                r = D.packed_row(b, h, B, H, world)
+                send[r, 0], send[r, 1] = m[0, h], l[0, h]
+                send[r, 4:] = o[0, h]
+        recv = D.exchange_head_slices(torch.from_numpy(send).view(world, B, hs, R))
+        assert recv.shape == (world, B, hs, R)
+        # this rank's heads: merge the partials every rank sent, project through its W_UV slice
+        o_slice = np.zeros((B, hs, DV), dtype=np.float32)
+        for b in range(B):
+            p = recv[:, b].double().numpy()                                     # (world, hs, R)
+            olat = O.combine_partials(p[:, :, 0], p[:, :, 1], p[:, :, 4:])      # (hs, dc)
+            Ws = W_UV[rank * hs * DV:(rank + 1) * hs * DV]
+            o_slice[b] = O.project_wuv(olat, Ws, hs, DV)
+        out = D.gather_head_slices(torch.from_numpy(o_slice))
+        assert out.shape == (B, H, DV)
+        for b in range(B):
+            want = O.absorbed_decode(kv[b * L:(b + 1) * L], q_abs[b], q_rope[b], W_UV, cos, sin, H, DC, DN, DR, DV)
+            np.testing.assert_allclose(out[b].numpy(), want, rtol=2e-5, atol=2e-6)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,B", [(2, 1), (4, 2)])
+def test_kv_range_head_sliced_exchange_matches_single_device(world, B):
+    _spawn(_kv_range_sliced_worker, world, 257, B, 13)
+
+
+def test_packed_row_layout():
+    B, Hh, S = 3, 16, 4
+    rows = sorted(D.packed_row(b, h, B, Hh, S) for b in range(B) for h in range(Hh))
+    assert rows == list(range(B * Hh))
+    # slice q is one contiguous block of B * H / S rows
+    for q in range(S):
+        block = [D.packed_row(b, h, B, Hh, S) for b in range(B) for h in range(q * Hh // S, (q + 1) * Hh // S)]
+        assert min(block) == q * B * Hh // S and max(block) == (q + 1) * B * Hh // S - 1

@@ -474,3 +474,43 @@ def test_batches_crossing_gemm_blocks(B):
                          max_seq_len=Lmax, kernel=kern).cpu().numpy()
         for b in range(B):
             assert_close(out[b], refs[b], f"B={B} seq {b} (L={lens[b]}) kernel={kern}")
+
+
+@pytest.mark.parametrize("B", [1, 2])
+def test_kv_range_packed_head_slices(B):
+    """The head-sliced KV-range path on one GPU: 4 KV-range shards each export packed partials
+    (mla_decode_partial_packed, 4 head slices); slice q's merge takes every shard's block q
+    (what the all-to-all delivers) and projects through W_UV's rows of those heads
+    (mla_combine_partials_packed); the slices side by side equal one whole decode and the oracle."""
+    dev = torch.device("cuda")
+    cfg = MLAConfig.deepseek_v2()
+    L, G = 3000, 4
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[L] * B, seed=19)
+    kv = inp.kv_cache.to(dev)
+    W_UV, W_UK = inp.W_UV.to(dev), inp.W_UK.to(dev)
+    qn, qr = inp.q_nope.float().to(dev), inp.q_rope.float().to(dev)
+    dims = (cfg.d_model, 512, 128, 64, 128, 128)
+    full = mla_decode(kv, qr, W_UV, None, None, cfg, q_nope=qn, W_UK=W_UK, max_seq_len=L).cpu().numpy()
+    bounds = [L * g // G for g in range(G + 1)]
+    packed = []
+    for g in range(G):
+        lo, hi = bounds[g], bounds[g + 1]
+        shard = torch.cat([kv[b * L + lo:b * L + hi] for b in range(B)]).contiguous()
+        packed.append(_C.mla_decode_partial_packed(shard, qr, W_UV, None, None, *dims, num_slices=G, q_nope=qn,
+                                                   W_UK=W_UK, kv_pos_offset=lo))
+    hs = 128 // G
+    slices = []
+    for q in range(G):
+        recv = torch.stack([packed[g][q] for g in range(G)]).contiguous()     # (G, B, hs, 516)
+        slices.append(_C.mla_combine_partials_packed(recv, W_UV[q * hs * 128:(q + 1) * hs * 128], *dims))
+    out = torch.cat(slices, dim=1).cpu().numpy()                               # (B, 128, 128)
+    for b in range(B):
+        assert_close(out[b], full[b], f"packed slices vs whole, b={b}")
+        cos, sin = O.rope_tables_otf(L, 64)
+        q_abs = O.absorb_query(inp.q_nope[b].float().numpy(), inp.W_UK.float().numpy(), 128, 512)
+        ref = O.absorbed_decode(inp.kv_cache[b * L:(b + 1) * L].float().numpy(), q_abs, inp.q_rope[b].float().numpy(),
+                                inp.W_UV.float().numpy(), cos, sin, 128, 512, 128, 64, 128)
+        assert_close(out[b], ref, f"packed slices vs oracle, b={b}")
+    # the layout: row (q * B + b) * hs + h % hs of slice q; m, l, then two zero floats, then o
+    p0 = packed[0].view(-1, 516).cpu()
+    assert torch.all(p0[:, 2:4] == 0) and torch.all(p0[:, 1] > 0)
