@@ -22,6 +22,8 @@
  *   (and their _packed forms) (m, l, o_latent) out of one shard; log-sum-exp merge of
  *                             G shards' partials + the W_UV projection of
  *                             src/fused_mla.cu:258-267)
+ *   mla_linear                the torch matmuls of LatentAttentionLayer.forward
+ *                             (latent_attn/__init__.py:126, :128, :145)
  *   mla_cache_append          LatentKVCache::append_host (src/mla_config.cuh:58-72),
  *                             moved to the device for a whole batch
  *   mla_config_validate       MLAConfig::validate() (src/mla_config.cuh:35-40)
@@ -228,6 +230,16 @@ MLA_API mla_status_t mla_decode_partial_packed(const mla_config_t* cfg, const ml
 MLA_API mla_status_t mla_combine_partials_packed(const mla_config_t* cfg, mla_dtype_t dtype, int batch,
                                          int num_parts, int heads, const float* packed, const void* W_UV,
                                          float* output, mla_stream_t stream);
+
+/* Projection GEMM for the layer-level caller: Y (M, N) fp32 = X (M, K) . W (N, K)^T, with X and W
+ * row-major fp16 or bf16 (both `dtype`), 1 <= M <= 256 tokens, K a multiple of 8. It replaces the
+ * torch matmuls of the reference's LatentAttentionLayer.forward (latent_attn/__init__.py:126,
+ * :128, :145: x @ W_Q_absorbed^T, x @ W_Q_rope^T and the W_O projection); no counterpart in the
+ * reference's kernels. Weight-streaming tcgen05 kernel: every weight byte is read once for all M
+ * tokens. When N is small for the GPU the K range is split over CTAs that add into Y (the call
+ * zeroes Y first, on the stream), so results can differ in the last bits from run to run. */
+MLA_API mla_status_t mla_linear(mla_dtype_t dtype, int M, int N, int K, const void* X, const void* W, float* Y,
+                                mla_stream_t stream);
 
 /* Device-side cache append, one new row per sequence: for each b, the row of position
  * p = seq_lens[b] receives [c_t[b] (d_c) | k_rope[b] (d_R)] (k_rope unrotated, as the cache

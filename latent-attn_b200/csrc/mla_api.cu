@@ -470,6 +470,31 @@ mla_status_t mla_combine_partials(const mla_config_t* cfg, mla_dtype_t dtype, in
                         output, reinterpret_cast<cudaStream_t>(stream));
 }
 
+mla_status_t mla_linear(mla_dtype_t dtype, int M, int N, int K, const void* X, const void* W, float* Y,
+                        mla_stream_t stream) {
+    if (!X || !W || !Y) return fail(MLA_ERR_INVALID_ARGUMENT, "null pointer");
+    if (M <= 0 || N <= 0 || K <= 0) return fail(MLA_ERR_INVALID_ARGUMENT, "M, N and K must be positive");
+    if (dtype != MLA_DTYPE_BF16 && dtype != MLA_DTYPE_F16) return fail(MLA_ERR_UNSUPPORTED, "dtype must be F16 or BF16");
+    if (!mla::linear_sm100_supported(M, N, K))
+        return fail(MLA_ERR_UNSUPPORTED, "mla_linear needs 1 <= M <= 256 and K a multiple of 8 (M=%d, K=%d)", M, K);
+    if ((reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(W)) % 16 != 0)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "X and W must be 16-byte aligned");
+    DeviceInfo di;
+    if (!device_info(&di)) return fail(MLA_ERR_CUDA, "no CUDA device");
+    if (di.major != 10) return fail(MLA_ERR_NO_DEVICE_CODE, "mla_linear needs an sm_100 GPU");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = dtype == MLA_DTYPE_BF16
+                        ? mla::launch_linear_sm100<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(X),
+                                                                  static_cast<const __nv_bfloat16*>(W), Y, M, N, K,
+                                                                  di.sms, s)
+                        : mla::launch_linear_sm100<__half>(static_cast<const __half*>(X), static_cast<const __half*>(W),
+                                                           Y, M, N, K, di.sms, s);
+    if (e == cudaErrorNoKernelImageForDevice || e == cudaErrorInvalidDeviceFunction)
+        return fail(MLA_ERR_NO_DEVICE_CODE, "linear kernel: %s (library is built for sm_100a)", cudaGetErrorString(e));
+    if (e != cudaSuccess) return cuda_fail(e, "linear kernel launch");
+    return MLA_OK;
+}
+
 mla_status_t mla_decode_partial_packed(const mla_config_t* cfg, const mla_decode_args_t* a, int num_slices,
                                        float* packed, void* workspace, size_t workspace_bytes, mla_stream_t stream) {
     mla_status_t st = validate_cfg(cfg);

@@ -250,6 +250,10 @@ template <typename T>
 cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, const float* part_ml,
                                        const float* part_o, int ml_stride, int o_stride, const T* W_UV, float* out,
                                        cudaStream_t s);
+// linear_sm100.cu: Y[M x N] fp32 = X[M x K] . W[N x K]^T (the layer's projections)
+bool linear_sm100_supported(int M, int N, int K);
+template <typename T>
+cudaError_t launch_linear_sm100(const T* X, const T* W, float* Y, int M, int N, int K, int sms, cudaStream_t s);
 // decode_simt.cu
 template <typename T>
 cudaError_t launch_decode_simt(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,

@@ -460,6 +460,26 @@ def mla_combine_partials(part_ml: torch.Tensor, part_o: torch.Tensor, W_UV: torc
     return out
 
 
+def linear(x: torch.Tensor, W: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``x (M, K) @ W (N, K)^T`` -> (M, N) fp32 on the tcgen05 projection kernel (``mla_linear``):
+    x and W fp16 or bf16 of the same dtype, contiguous, 1 <= M <= 256."""
+    _check_half(x, "x")
+    _check_half(W, "W")
+    if x.dtype != W.dtype:
+        raise RuntimeError("x and W must have the same dtype")
+    if x.dim() != 2 or W.dim() != 2 or x.size(1) != W.size(1):
+        raise RuntimeError(f"shape mismatch: x {tuple(x.shape)}, W {tuple(W.shape)}")
+    M, K = x.shape
+    N = W.size(0)
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.float32, device=x.device)
+    elif tuple(out.shape) != (M, N) or out.dtype != torch.float32 or not out.is_contiguous():
+        raise RuntimeError(f"out must be a contiguous float32 tensor of shape ({M}, {N})")
+    _lib.check(_lib.load().mla_linear(_DT[x.dtype], M, N, K, C.c_void_p(x.data_ptr()), C.c_void_p(W.data_ptr()),
+                                      C.c_void_p(out.data_ptr()), C.c_void_p(_stream(x.device))))
+    return out
+
+
 def mla_cache_append(kv_cache: torch.Tensor, c_t: torch.Tensor, k_rope: torch.Tensor, seq_lens: torch.Tensor,
                      max_seq_len: int, d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads,
                      v_head_dim, *, kv_offsets: Optional[torch.Tensor] = None,

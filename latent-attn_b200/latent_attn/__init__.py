@@ -38,4 +38,6 @@ def _build_rope_tables(seq_len: int, d_R: int, device: torch.device):
     return build_rope_tables(seq_len, d_R, device=device)
 
 
-__all__ = ["MLAConfig", "build_rope_tables", "_build_rope_tables"]
+from .layer import LatentAttentionLayer  # noqa: E402  (needs MLAConfig above)
+
+__all__ = ["MLAConfig", "LatentAttentionLayer", "build_rope_tables", "_build_rope_tables"]

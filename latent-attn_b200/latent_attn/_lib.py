@@ -89,6 +89,7 @@ SIGNATURES = {
     "mla_cache_append": (C.c_int, [C.POINTER(MlaConfig), C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_int,
                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                    C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    "mla_linear": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "mla_timer_create": (C.c_int, [C.POINTER(C.c_void_p)]),
     "mla_timer_destroy": (C.c_int, [C.c_void_p]),
     "mla_timer_decode_ms": (C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),

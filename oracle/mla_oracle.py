@@ -22,6 +22,8 @@ Everything is plain numpy.
   ``score = (q_abs . c_t + q_rope . RoPE(k_rope, pos)) * scale``, two-pass
   softmax, ``o_lat = sum_p w_p c_p / l``, then ``out[h, j] = o_lat . W_UV[h*dv + j]``
   (src/fused_mla.cu:258-267). It runs in float64 so it can check large shapes.
+* ``layer_forward`` restates the layer-level caller (latent_attn/__init__.py:110-145) around
+  ``absorbed_decode``, with the reference_forward's shape error corrected.
 * ``split_partials`` / ``combine_partials`` restate the split-KV log-sum-exp
   merge that the build adds (no reference counterpart; the merge identity is
   the standard flash-decoding one).
@@ -140,6 +142,22 @@ def absorbed_decode(kv_cache: np.ndarray, q_abs: np.ndarray, q_rope: np.ndarray,
     scale = 1.0 / math.sqrt(qk_nope_head_dim + qk_rope_head_dim)
     o = absorbed_latent(kv_cache, q_abs, q_rope, cos, sin, kv_lora_rank, scale)
     return project_wuv(o, W_UV, num_heads, v_head_dim)
+
+
+def layer_forward(x: np.ndarray, W_Q_absorbed: np.ndarray, W_Q_rope: np.ndarray, W_UV: np.ndarray,
+                  W_O: np.ndarray, kv_cache: np.ndarray, cos: np.ndarray, sin: np.ndarray, num_heads: int,
+                  kv_lora_rank: int, qk_nope_head_dim: int, qk_rope_head_dim: int, v_head_dim: int) -> np.ndarray:
+    """One token through the reference's LatentAttentionLayer (latent_attn/__init__.py:110-198), float64:
+    ``q_abs = x @ W_Q_absorbed^T``, ``q_rope = x @ W_Q_rope^T`` (unrotated, as the reference), the
+    absorbed decode, then ``@ W_O^T``. Its ``reference_forward`` multiplies shapes that cannot be
+    multiplied (``(H, d_c) @ (H * dn, d_c)`` at :183); the nope score is taken in the latent space
+    (``q_abs . c_t``), the identity the fused path computes. x (d_model,) -> (d_model,)."""
+    H, dc, dR = num_heads, kv_lora_rank, qk_rope_head_dim
+    xd = x.astype(np.float64)
+    q_abs = (W_Q_absorbed.astype(np.float64) @ xd).reshape(H, dc)
+    q_r = (W_Q_rope.astype(np.float64) @ xd).reshape(H, dR)
+    out = absorbed_decode(kv_cache, q_abs, q_r, W_UV, cos, sin, H, dc, qk_nope_head_dim, dR, v_head_dim)
+    return W_O.astype(np.float64) @ out.reshape(-1)
 
 
 def varlen_decode(kv_cache: np.ndarray, seq_lens: Sequence[int], kv_offsets: Sequence[int],
