@@ -68,7 +68,7 @@ def test_layer_forward_single_token(d_model):
     want = _oracle(layer, cfg, x, kv, torch.bfloat16)
     _close(y.cpu().numpy(), want, f"forward d_model={d_model}")
     # the corrected reference_forward (fp32 torch, unrounded weights) agrees too
-    ref = layer.reference_forward(x, kv).double().cpu().numpy()
+    ref = layer.reference_forward(x, kv).detach().double().cpu().numpy()
     _close(y.cpu().numpy(), ref, f"forward vs reference_forward d_model={d_model}")
 
 
