@@ -24,10 +24,15 @@
 //    CTA = (block of up to 64 tokens, head), 512 threads. The same kernel merges the gathered
 //    partial sets of KV-range shards (mla_combine_partials).
 //
-// Both launch W loads by TMA before waiting on the previous kernel
+// Batches of at most four tokens take fp32 CUDA-core kernels instead (absorb_gemv_kernel,
+// project_gemv_kernel): there both products are matrix-vector products bound by reading the
+// weights once, and fp32 operands need no hi/lo split.
+//
+// The projection kernels launch their W loads by TMA before waiting on the previous kernel
 // (programmatic dependent launch), so weight streaming overlaps its tail.
 // Every wait is bounded; on timeout the status word records it.
 #include <cfloat>
+#include <cstdlib>
 
 #include "mla_internal.cuh"
 #include "sm100_ptx.cuh"
@@ -244,6 +249,93 @@ absorb_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tbase, tmem_cols);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// absorption of a few tokens: fp32 CUDA-core GEMV
+// ------------------------------------------------------------------------------------------
+// For B <= kAbsorbGemvTok the absorption is a vector-matrix product per token and head (dn x d_c),
+// bound by reading W_UK once. The products are formed in fp32 from the fp32 q_nope (no rounding of
+// the query before the product). CTA = (slice of 256 d_c columns, head h), 256 threads: warp w takes
+// the W_UK rows i = 16 w .. 16 w + 15 and lane l the 8 columns 8 l .. 8 l + 7 of the slice, with all
+// 16 row loads in flight at once; the 8 warps' partial sums are added in warp order through shared
+// memory, scaled, rounded once to T and written as 16-byte rows of qpack.
+constexpr int kAbsorbGemvTok = 4;
+constexpr int kAbsorbGemvCols = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+absorb_gemv_kernel(const DecodePlan P, const float* __restrict__ q_nope, const T* __restrict__ W_UK,
+                   const float* __restrict__ q_rope, float q_scale, T* __restrict__ qpack, int* tile_prefix_out) {
+    clear_status(P);
+    __shared__ float red[8][kAbsorbGemvTok][kAbsorbGemvCols];   // 32 KB
+    const int dn = P.dn, dc = P.dc, K = P.dc + P.dR, B = P.B;   // dn == 128, dc % 256 == 0, B <= 4
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c0 = blockIdx.x * kAbsorbGemvCols, h = blockIdx.y;
+    pdl_launch_dependents();
+    if (tile_prefix_out && blockIdx.x == 0 && blockIdx.y == 0) write_tile_prefix(P, tile_prefix_out);
+    using T2 = typename ElemTraits<T>::T2;
+    {
+        uint4 wv[16];
+        const T* wrow = W_UK + (static_cast<long long>(h) * dn + 16 * warp) * dc + c0 + 8 * lane;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) wv[i] = __ldg(reinterpret_cast<const uint4*>(wrow + static_cast<long long>(i) * dc));
+        float acc[kAbsorbGemvTok][8];
+#pragma unroll
+        for (int t = 0; t < kAbsorbGemvTok; ++t)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[t][e] = 0.f;
+#pragma unroll
+        for (int t = 0; t < kAbsorbGemvTok; ++t) {
+            if (t < B) {
+                // lanes 0-15 hold this warp's 16 q_nope values of token t; broadcast by shuffle
+                const float qv = lane < 16 ? __ldg(q_nope + (static_cast<long long>(t) * P.H + h) * dn + 16 * warp + lane)
+                                           : 0.f;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float q = __shfl_sync(0xffffffffu, qv, i);
+                    const float2 a = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv[i].x));
+                    const float2 b = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv[i].y));
+                    const float2 c = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv[i].z));
+                    const float2 d = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv[i].w));
+                    acc[t][0] = fmaf(q, a.x, acc[t][0]); acc[t][1] = fmaf(q, a.y, acc[t][1]);
+                    acc[t][2] = fmaf(q, b.x, acc[t][2]); acc[t][3] = fmaf(q, b.y, acc[t][3]);
+                    acc[t][4] = fmaf(q, c.x, acc[t][4]); acc[t][5] = fmaf(q, c.y, acc[t][5]);
+                    acc[t][6] = fmaf(q, d.x, acc[t][6]); acc[t][7] = fmaf(q, d.y, acc[t][7]);
+                }
+                float4* dst = reinterpret_cast<float4*>(&red[warp][t][8 * lane]);
+                dst[0] = make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
+                dst[1] = make_float4(acc[t][4], acc[t][5], acc[t][6], acc[t][7]);
+            }
+        }
+    }
+    __syncthreads();
+    // (token, 8-column group) items: sum the 8 warps in order, scale, round, one 16-byte store
+    for (int i = threadIdx.x; i < B * (kAbsorbGemvCols / 8); i += blockDim.x) {
+        const int t = i / (kAbsorbGemvCols / 8), g = i % (kAbsorbGemvCols / 8);
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            float s = 0.f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) s += red[w][t][8 * g + e];
+            v[e] = s * q_scale;
+        }
+        const uint4 x = make_uint4(pack_pair<T>(v[0], v[1]), pack_pair<T>(v[2], v[3]), pack_pair<T>(v[4], v[5]),
+                                   pack_pair<T>(v[6], v[7]));
+        *reinterpret_cast<uint4*>(qpack + qpack_row(P, t, h) * K + c0 + 8 * g) = x;
+    }
+    if (blockIdx.x == 0) {
+        // rope columns, 4 at a time
+        const int q4 = P.dR / 4;
+        for (int i = threadIdx.x; i < B * q4; i += blockDim.x) {
+            const int t = i / q4, j = 4 * (i % q4);
+            const long long flat = static_cast<long long>(t) * P.H + h;
+            const float4 x = *reinterpret_cast<const float4*>(q_rope + flat * P.dR + j);
+            const uint2 y = make_uint2(pack_pair<T>(x.x * q_scale, x.y * q_scale), pack_pair<T>(x.z * q_scale, x.w * q_scale));
+            *reinterpret_cast<uint2*>(qpack + qpack_row(P, t, h) * K + dc + j) = y;
+        }
     }
 }
 
@@ -597,6 +689,221 @@ cudaError_t launch_ex(Kernel k, dim3 grid, dim3 block, size_t smem, cudaStream_t
 }
 }  // namespace
 
+// ------------------------------------------------------------------------------------------
+// merge + projection of a few tokens: fp32 CUDA-core GEMV
+// ------------------------------------------------------------------------------------------
+// For B <= kGemvMaxTok the W_UV product is a matrix-vector product per token (128 x d_c per
+// head), too small for the tensor cores to pay for their issue and TMEM round trip, and the merged
+// latent row can stay in fp32 (no rounding before the projection). One CTA per head h, 512 threads:
+//   0. thread 0 starts the TMA of W_UV[h] (dv x d_c, independent of the decode kernel) before the
+//      programmatic-dependent wait;
+//   1. warps are split over the tokens (16 / B warps each); a warp merges the records k = s, s + S, ...
+//      of its token, four per round trip, into a running log-sum-exp (max, row sum, rescaled sum);
+//   2. per token, the warp partials are rescaled to the common max and summed column by column into
+//      the fp32 latent row (shared memory);
+//   3. thread (q, j) dots W_UV row j with latent quarter q for every token (each W element read once
+//      from shared memory per CTA); the four quarters are summed in a fixed order.
+constexpr int kGemvWarps = 16;
+constexpr int kGemvRec = 4;      // records per warp per round trip
+constexpr int kGemvMaxTok = 4;   // batches up to this size take the GEMV kernel
+
+__host__ __device__ inline size_t gemv_smem_bytes(int dc, int dv) {
+    return static_cast<size_t>(dc / 64) * dv * 128 +             // W_UV[h] boxes
+           static_cast<size_t>(kGemvWarps) * dc * sizeof(float) + // warp partial sums
+           kGemvWarps * sizeof(float2) +                          // warp (max, row sum)
+           static_cast<size_t>(kGemvMaxTok) * dc * sizeof(float) +   // merged latent rows
+           static_cast<size_t>(4) * kGemvMaxTok * dv * sizeof(float) +  // quarter sums
+           16;                                                    // mbarrier
+}
+
+template <typename T>
+__global__ void __launch_bounds__(32 * kGemvWarps, 1)
+project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
+                    const float* __restrict__ rec_o, float* __restrict__ out, int parts, int ml_stride, int o_stride) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int dc = P.dc, dv = P.dv, B = P.B;   // dv == 128, dc % 64 == 0, dc <= 512, B <= kGemvMaxTok
+    const int nk = dc / 64;
+    unsigned char* wsm = smem;                                                    // nk x (dv rows x 128 B)
+    float* red = reinterpret_cast<float*>(smem + nk * dv * 128);                  // [warp][dc]
+    float2* wml = reinterpret_cast<float2*>(red + kGemvWarps * dc);               // [warp]
+    float* olat = reinterpret_cast<float*>(wml + kGemvWarps);                     // [token][dc]
+    float* qsum = olat + kGemvMaxTok * dc;                                        // [quarter][token][dv]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(qsum + 4 * kGemvMaxTok * dv);
+    const uint32_t w_full = smem_u32(bar);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.x;
+    volatile int* err = P.status;
+
+    if (threadIdx.x == 0) {
+        mbar_init(w_full, 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tmap_w);
+        mbar_arrive_expect_tx(w_full, static_cast<uint32_t>(nk * dv * 128));
+        for (int j = 0; j < nk; ++j) tma_load_2d(smem_u32(wsm) + j * dv * 128, &tmap_w, w_full, 64 * j, h * dv);
+    }
+    pdl_wait();  // records and status come from the decode kernel
+    const int status0 = *err;   // consumed after the merge
+    const int step = parts ? B * P.H : kGroupRows;
+    const float mscale = parts ? 1.4426950408889634f : 1.f;   // m in log2 units
+    const int U = dc / 4;                                      // float4 units per row, <= 128
+
+    // ---- 1. merge: warp w takes token t = w / wpt and records k = s, s + wpt, ... (s = w % wpt)
+    const int wpt = kGemvWarps / B;
+    const int t = warp / wpt, s = warp % wpt;
+    if (t < B) {
+        const int b = t;
+        int n = parts, w0 = 0, ntiles = 0;
+        long long base = static_cast<long long>(b) * P.H + h;
+        bool busy = true;
+        if (!parts) {
+            ntiles = total_tiles(P);
+            busy = ntiles >= P.W;   // every worker owns a tile: every record in the range exists
+            int g, r;
+            if (P.shared) {
+                const int f = b * P.H + h;
+                g = f / kGroupRows;
+                r = f % kGroupRows;
+            } else {
+                g = b * P.head_blocks + h / kGroupRows;
+                r = h % kGroupRows;
+            }
+            const int gt0 = tile_prefix(P, g), gt1 = tile_prefix(P, g + 1);
+            n = 0;
+            if (gt1 > gt0 && ntiles > 0) {
+                w0 = worker_of_tile(ntiles, P.W, gt0);
+                n = worker_of_tile(ntiles, P.W, gt1 - 1) - w0 + 1;
+            }
+            base = static_cast<long long>(g + w0) * kGroupRows + r;
+        }
+        const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        float mrun = -INFINITY, lrun = 0.f;
+        float4 acc[4] = {zero4, zero4, zero4, zero4};
+        for (int k0 = s; k0 < n; k0 += wpt * kGemvRec) {
+            float2 mlq[kGemvRec];
+            float4 v[kGemvRec][4];
+#pragma unroll
+            for (int q = 0; q < kGemvRec; ++q) {
+                const int k = k0 + q * wpt;
+                // a worker that owns no tile of the group wrote no record: it is never read
+                const bool in = k < n && (parts || busy ||
+                                          worker_begin(ntiles, P.W, w0 + k) != worker_begin(ntiles, P.W, w0 + k + 1));
+                const long long row = base + static_cast<long long>(k) * step;
+                mlq[q] = in ? __ldg(reinterpret_cast<const float2*>(rec_ml + row * ml_stride))
+                            : make_float2(-INFINITY, 0.f);
+#pragma unroll
+                for (int u4 = 0; u4 < 4; ++u4) {
+                    const int u = lane + 32 * u4;
+                    v[q][u4] = (in && u < U) ? __ldg(reinterpret_cast<const float4*>(rec_o + row * o_stride) + u)
+                                             : zero4;
+                }
+            }
+            float mq[kGemvRec];
+            float mnew = mrun;
+#pragma unroll
+            for (int q = 0; q < kGemvRec; ++q) {   // an empty part (l = 0) contributes nothing
+                mq[q] = mlq[q].y > 0.f ? mlq[q].x * mscale : -INFINITY;
+                mnew = fmaxf(mnew, mq[q]);
+            }
+            if (mnew == -INFINITY) continue;
+            const float sc = exp2f(mrun - mnew);
+            lrun *= sc;
+#pragma unroll
+            for (int u4 = 0; u4 < 4; ++u4) {
+                acc[u4].x *= sc; acc[u4].y *= sc; acc[u4].z *= sc; acc[u4].w *= sc;
+            }
+#pragma unroll
+            for (int q = 0; q < kGemvRec; ++q) {
+                const float wq = exp2f(mq[q] - mnew);
+                lrun = fmaf(wq, mlq[q].y, lrun);
+#pragma unroll
+                for (int u4 = 0; u4 < 4; ++u4) {
+                    acc[u4].x = fmaf(wq, v[q][u4].x, acc[u4].x);
+                    acc[u4].y = fmaf(wq, v[q][u4].y, acc[u4].y);
+                    acc[u4].z = fmaf(wq, v[q][u4].z, acc[u4].z);
+                    acc[u4].w = fmaf(wq, v[q][u4].w, acc[u4].w);
+                }
+            }
+            mrun = mnew;
+        }
+        if (lane == 0) wml[warp] = make_float2(mrun, lrun);
+#pragma unroll
+        for (int u4 = 0; u4 < 4; ++u4) {
+            const int u = lane + 32 * u4;
+            if (u < U) reinterpret_cast<float4*>(red + warp * dc)[u] = acc[u4];
+        }
+    }
+    __syncthreads();
+    // ---- 2. per token: the warps' partials at the common max, summed in warp order
+    for (int i = threadIdx.x; i < B * dc; i += blockDim.x) {
+        const int tt = i / dc, c = i % dc;
+        float M = -INFINITY;
+        for (int w = tt * wpt; w < (tt + 1) * wpt; ++w) M = fmaxf(M, wml[w].x);
+        float L = 0.f, o = 0.f;
+        if (M != -INFINITY) {
+            for (int w = tt * wpt; w < (tt + 1) * wpt; ++w) {
+                const float a = wml[w].x == -INFINITY ? 0.f : exp2f(wml[w].x - M);
+                L = fmaf(a, wml[w].y, L);
+                o = fmaf(a, red[w * dc + c], o);
+            }
+        }
+        olat[tt * dc + c] = L > 0.f ? o / L : 0.f;
+    }
+    // W_UV[h] must have landed (thread 0 waits; the block-wide AND carries the result)
+    bool ok = true;
+    // (a wait that ends only on completion or its time limit: the load never depends on another kernel)
+    if (threadIdx.x == 0) ok = mbar_wait_impl<false, false>(w_full, 0, err, gcode(kSiteProjA), kDefaultWaitNs);
+    ok = __syncthreads_and(ok);
+    const bool failed = (parts == 0 && status0 != kStatusOk) || !ok;
+    // ---- 3. thread (q, j): W_UV row j . latent quarter q, for every token
+    {
+        const int q = threadIdx.x / dv, j = threadIdx.x % dv;   // 4 quarters x 128 rows
+        const int kq = dc / 4;                                   // elements per quarter, a multiple of 16
+        float acc[kGemvMaxTok] = {0.f, 0.f, 0.f, 0.f};
+        if (ok) {
+            for (int c = 0; c < kq / 8; ++c) {
+                const int k = q * kq + 8 * c;
+                // 128-byte-swizzled box row: 16-byte chunk ((k % 64) / 8) ^ (j % 8)
+                const uint4 wv = *reinterpret_cast<const uint4*>(wsm + (k >> 6) * (dv * 128) + j * 128 +
+                                                                 ((((k & 63) >> 3) ^ (j & 7)) << 4));
+                using T2 = typename ElemTraits<T>::T2;
+                const float2 w01 = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv.x));
+                const float2 w23 = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv.y));
+                const float2 w45 = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv.z));
+                const float2 w67 = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv.w));
+#pragma unroll
+                for (int tt = 0; tt < kGemvMaxTok; ++tt) {
+                    if (tt < B) {
+                        const float4 o0 = *reinterpret_cast<const float4*>(olat + tt * dc + k);
+                        const float4 o1 = *reinterpret_cast<const float4*>(olat + tt * dc + k + 4);
+                        float a = acc[tt];
+                        a = fmaf(w01.x, o0.x, a); a = fmaf(w01.y, o0.y, a);
+                        a = fmaf(w23.x, o0.z, a); a = fmaf(w23.y, o0.w, a);
+                        a = fmaf(w45.x, o1.x, a); a = fmaf(w45.y, o1.y, a);
+                        a = fmaf(w67.x, o1.z, a); a = fmaf(w67.y, o1.w, a);
+                        acc[tt] = a;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int tt = 0; tt < kGemvMaxTok; ++tt)
+            if (tt < B) qsum[(q * kGemvMaxTok + tt) * dv + j] = acc[tt];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < B * dv; i += blockDim.x) {
+        const int tt = i / dv, j = i % dv;
+        float y = __int_as_float(0x7fc00000);   // a failed decode or wait shows in the output
+        if (!failed)
+            y = ((qsum[(0 * kGemvMaxTok + tt) * dv + j] + qsum[(1 * kGemvMaxTok + tt) * dv + j]) +
+                 qsum[(2 * kGemvMaxTok + tt) * dv + j]) + qsum[(3 * kGemvMaxTok + tt) * dv + j];
+        out[(static_cast<long long>(tt) * P.H + h) * dv + j] = y;
+    }
+    // shared memory is not released under a TMA write: if the wait gave up, wait (bounded) again
+    if (threadIdx.x == 0 && !ok) mbar_wait_impl<false, false>(w_full, 0, err, gcode(kSiteProjA), 100000000ull);
+}
+
 bool absorb_sm100_supported(const DecodePlan& P) {
     return P.dc % 128 == 0 && P.dn % 64 == 0 && P.dn <= 256 && P.dR % 8 == 0;
 }
@@ -605,10 +912,28 @@ bool project_sm100_supported(const DecodePlan& P) {
     return P.dv == 128 && P.dc % 64 == 0 && P.dc <= 512 && P.W <= 128;
 }
 
+// Largest batch absorbed, merged and projected by the fp32 GEMV kernels (LATENT_ATTN_B200_GEMV_TOKENS =
+// 0 .. 4 overrides; 0 sends every batch to the tensor-core kernels).
+int gemv_max_tokens() {
+    static int v = [] {
+        const char* s = std::getenv("LATENT_ATTN_B200_GEMV_TOKENS");
+        if (!s) return kGemvMaxTok;
+        const int n = std::atoi(s);
+        return n < 0 ? 0 : (n > kGemvMaxTok ? kGemvMaxTok : n);
+    }();
+    return v;
+}
+
 template <typename T>
 cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const T* W_UK, const float* q_rope,
                                 float q_scale, T* qpack, int* tile_prefix_out, cudaStream_t s) {
     if (!absorb_sm100_supported(P)) return cudaErrorInvalidValue;
+    if (P.B <= gemv_max_tokens() && P.dn == 128 && P.dc % kAbsorbGemvCols == 0) {
+        const cudaError_t e = launch_ex(absorb_gemv_kernel<T>, dim3(P.dc / kAbsorbGemvCols, P.H), dim3(256), 0, s, false,
+                                        P, q_nope, W_UK, q_rope, q_scale, qpack, tile_prefix_out);
+        count_launches(1);
+        return e != cudaSuccess ? e : cudaGetLastError();
+    }
     CUtensorMap tmap;
     if (!make_tmap_2d_16b(&tmap, W_UK, static_cast<uint64_t>(P.H) * P.dn, static_cast<uint64_t>(P.dc),
                           static_cast<uint64_t>(P.dc), static_cast<uint32_t>(P.dn), 64))
@@ -631,6 +956,15 @@ cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const 
     if (!make_tmap_2d_16b(&tmap, W_UV, static_cast<uint64_t>(P.H) * P.dv, static_cast<uint64_t>(P.dc),
                           static_cast<uint64_t>(P.dc), static_cast<uint32_t>(P.dv), 64))
         return cudaErrorInvalidValue;
+    if (P.B <= gemv_max_tokens()) {
+        const size_t smem = 1024 + gemv_smem_bytes(P.dc, P.dv);
+        cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(project_gemv_kernel<T>), static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        e = launch_ex(project_gemv_kernel<T>, dim3(P.H), dim3(32 * kGemvWarps), smem, s, pdl, tmap, P, rec_ml, rec_o,
+                      out, parts, ml_stride, o_stride);
+        count_launches(1);
+        return e != cudaSuccess ? e : cudaGetLastError();
+    }
     const int ntp = pad16(P.B < kProjTok ? P.B : kProjTok);
     const int nk = P.dc / 64;
     const size_t smem = 1024 + static_cast<size_t>(nk) * P.dv * 128 + static_cast<size_t>(nk) * ntp * 128 +

@@ -514,3 +514,28 @@ def test_kv_range_packed_head_slices(B):
     # the layout: row (q * B + b) * hs + h % hs of slice q; m, l, then two zero floats, then o
     p0 = packed[0].view(-1, 516).cpu()
     assert torch.all(p0[:, 2:4] == 0) and torch.all(p0[:, 1] > 0)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B", [1, 2, 3, 4, 5])
+def test_small_batches_gemv_and_tensor_core_gemms(B, dtype):
+    """Batches of 1-4 tokens take the fp32 CUDA-core absorption and merge/projection kernels, 5
+    tokens the tensor-core ones. Lengths from one position (a single record, no merge) to 20000
+    (records of every split-KV worker), every sequence against the oracle, on both decode kernels."""
+    lens = [1, 20000, 5, 777, 64][:B]
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=lens, seed=31 + B, dtype=dtype)
+    cfg = MLAConfig.deepseek_v2()
+    dev = torch.device("cuda")
+    Lmax = max(lens)
+    cos, sin = synthetic.build_rope_tables(Lmax, 64, device=dev)
+    cos_np, sin_np = cos.cpu().numpy(), sin.cpu().numpy()
+    kv, W_UV, W_UK = inp.kv_cache.to(dev), inp.W_UV.to(dev), inp.W_UK.to(dev)
+    qn, qr = inp.q_nope.float().to(dev), inp.q_rope.float().to(dev)
+    seq = torch.tensor(lens, dtype=torch.int32, device=dev)
+    offs = torch.tensor(inp.kv_offsets, dtype=torch.int64, device=dev)
+    refs = [_oracle_single(inp, b, cos_np, sin_np) for b in range(B)]
+    for kern in kernels_for(cfg):
+        out = mla_decode(kv, qr, W_UV, cos, sin, cfg, q_nope=qn, W_UK=W_UK, seq_lens=seq, kv_offsets=offs,
+                         max_seq_len=Lmax, kernel=kern).cpu().numpy()
+        for b in range(B):
+            assert_close(out[b], refs[b], f"B={B} {dtype} seq {b} (L={lens[b]}) kernel={kern}")
