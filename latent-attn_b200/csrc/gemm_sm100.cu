@@ -86,7 +86,8 @@ __device__ __forceinline__ long long qpack_row(const DecodePlan& P, int b, int h
                     : static_cast<long long>(b) * P.head_blocks * kGroupRows + h;
 }
 
-constexpr int kAbsorbTok = 128;    // tokens per absorption CTA (MMA N; two CTAs per SM with the hi/lo operand)
+constexpr int kAbsorbTok = 128;    // tokens per absorption CTA (MMA M)
+constexpr int kAbsorbThreads = 256;
 constexpr int kProjTok = 64;       // tokens per projection CTA
 constexpr int kProjWarps = 16;     // projection CTA: 16 warps merge, warp 0 issues the MMA, warps 4-7 store
 // rows of split partial sums of the merge (S * ntok <= rows): 32 when the token operand is at most
@@ -95,12 +96,9 @@ constexpr int kProjWarps = 16;     // projection CTA: 16 warps merge, warp 0 iss
 __host__ __device__ constexpr int proj_red_rows(int ntp) { return ntp <= 16 ? 32 : 8; }
 constexpr int kProjRedMax = 32;    // the largest proj_red_rows
 
-// B operand hi and lo parts (each dn/64 chunks of ntp rows x 128 B), reused after the MMAs as ntp rows x
-// 128 elements of staging
-__host__ __device__ inline int absorb_b_part_bytes(int dn, int ntp) { return (dn / 64) * ntp * 128; }
-__host__ __device__ inline int absorb_b_bytes(int dn, int ntp) {
-    const int b = 2 * absorb_b_part_bytes(dn, ntp), st = ntp * 256;
-    return b > st ? b : st;
+// absorption shared memory: W_UK_h (d_c / 64 boxes of dn rows x 128 B), the hi and lo A parts, barriers
+__host__ __device__ inline size_t absorb_smem_bytes(int dn, int dc) {
+    return static_cast<size_t>(dc / 64) * dn * 128 + 2 * static_cast<size_t>(dn / 64) * kAbsorbTok * 128 + 32;
 }
 
 enum : int { kSiteAbsorbA = 12, kSiteAbsorbMma = 13, kSiteProjA = 14, kSiteProjMma = 15 };
@@ -112,144 +110,160 @@ __device__ __forceinline__ int gcode(int site) { return kStatusTimeout | (site <
 // absorption
 // ------------------------------------------------------------------------------------------
 template <typename T>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(kAbsorbThreads, 1)
 absorb_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ q_nope,
-                    const float* __restrict__ q_rope, float q_scale, T* __restrict__ qpack, int* tile_prefix_out,
-                    int ntp, uint32_t tmem_cols) {
+                    const float* __restrict__ q_rope, float q_scale, T* __restrict__ qpack, int* tile_prefix_out) {
+    // CTA = (block of up to 128 tokens, head h), 256 threads. D[tokens x d_c] = q_nope_h . W_UK_h in TMEM
+    // (lane = token, column = d_c index), in N = 256 column halves:
+    //   A = q_nope_h rows, K-major (K = dn), 128-byte swizzle, hi and lo parts (dn / 64 chunks each)
+    //   B = W_UK_h, MN-major (d_c contiguous): d_c / 64 TMA boxes of 64 columns x dn rows
     clear_status(P);
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    const int dn = P.dn, dc = P.dc, K = P.dc + P.dR;
-    const uint32_t a_u32 = smem_u32(smem);                   // 2 x (dn rows x 128 B)
-    const uint32_t b_u32 = a_u32 + 2u * dn * 128u;            // dn/64 x (ntp rows x 128 B), then the staging rows
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * dn * 128 + absorb_b_bytes(dn, ntp));
+    const int dn = P.dn, dc = P.dc, dR = P.dR, K = P.dc + P.dR;   // dn == 128, dc % 256 == 0, dc <= 512
+    const int box_bytes = dn * 128;                                // one W box: 64 d_c x dn rows
+    const int nbox = dc / 64;
+    const uint32_t w_u32 = smem_u32(smem);
+    const uint32_t a_u32 = w_u32 + nbox * box_bytes;               // [part][dn / 64][128 rows x 128 B]
+    const uint32_t chunk_bytes = kAbsorbTok * 128;
+    const uint32_t part_bytes = (dn / 64) * chunk_bytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + nbox * box_bytes + 2 * part_bytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
-    const uint32_t a_full = smem_u32(&bars[0]), mma_done = smem_u32(&bars[1]);
+    const uint32_t w_full = smem_u32(&bars[0]), mma_done = smem_u32(&bars[1]);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * 128, h = blockIdx.y, b0 = blockIdx.z * kAbsorbTok;
+    const int b0 = blockIdx.x * kAbsorbTok, h = blockIdx.y;
     const int ntok = min(kAbsorbTok, P.B - b0);
     volatile int* err = P.status;
 
     pdl_launch_dependents();
-    if (tile_prefix_out && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) write_tile_prefix(P, tile_prefix_out);
+    if (tile_prefix_out && blockIdx.x == 0 && blockIdx.y == 0) write_tile_prefix(P, tile_prefix_out);
     if (threadIdx.x == 0) {
-        mbar_init(a_full, 1);
+        mbar_init(w_full, 1);
         mbar_init(mma_done, 1);
         fence_mbar_init();
         tma_prefetch_desc(&tmap_w);
+        mbar_arrive_expect_tx(w_full, static_cast<uint32_t>(nbox * box_bytes));
+        for (int j = 0; j < nbox; ++j) tma_load_2d(w_u32 + j * box_bytes, &tmap_w, w_full, 64 * j, h * dn);
     }
     if (warp == 0) {
-        tmem_alloc(smem_u32(tmem_slot), tmem_cols);
+        tmem_alloc(smem_u32(tmem_slot), 512);
         tmem_relinquish();
     }
+    // Thread (t, half): token t's q_nope elements [64 half, 64 half + 64) (A chunk `half`) and rope
+    // elements [dR/2 half, dR/2 (half + 1)); every load is issued before the first is used.
+    const int t = threadIdx.x & (kAbsorbTok - 1), half = threadIdx.x / kAbsorbTok;
+    const bool tok = t < ntok;
+    const long long flat = static_cast<long long>(b0 + t) * P.H + h;
+    float4 x[16];
+    float4 r[8];
+    const int rq = dR / 8;   // float4 units of a rope half (dR % 8 == 0, dR <= 64)
+#pragma unroll
+    for (int u = 0; u < 16; ++u)
+        x[u] = tok ? __ldg(reinterpret_cast<const float4*>(q_nope + flat * dn + 64 * half) + u)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+        r[u] = (tok && u < rq) ? __ldg(reinterpret_cast<const float4*>(q_rope + flat * dR + (dR / 2) * half) + u)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tmem_slot;
-    if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(a_full, 2u * dn * 128u);
-        tma_load_2d(a_u32, &tmap_w, a_full, m0, h * dn);
-        tma_load_2d(a_u32 + dn * 128, &tmap_w, a_full, m0 + 64, h * dn);
-    }
-    // B operand: q_nope of the block's tokens, fp32 -> hi and lo parts in T, K-major
-    // 128-byte-swizzled rows. Eight 32-byte items per thread are loaded before any is stored,
-    // so the loads overlap.
-    const int upr = dn / 8;  // 16-byte units (8 elements) per token row
-    const int items = ntp * upr;
-    const uint32_t lo_off = static_cast<uint32_t>(absorb_b_part_bytes(dn, ntp));
-    for (int i0 = threadIdx.x; i0 < items; i0 += 8 * 128) {
-        float4 x[8], y[8];
+    {
+        // hi = round(q), lo = round(q - hi): 16-byte units u of row t, swizzled by (t % 8)
+        const uint32_t row = a_u32 + half * chunk_bytes + t * 128;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int i = i0 + q * 128, t = i / upr, u = i % upr;
-            x[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-            y[q] = x[q];
-            if (i < items && t < ntok) {
-                const float4* src = reinterpret_cast<const float4*>(
-                    q_nope + (static_cast<long long>(b0 + t) * P.H + h) * dn + 8 * u);
-                x[q] = __ldg(src);
-                y[q] = __ldg(src + 1);
+        for (int u = 0; u < 8; ++u) {
+            const float v[8] = {x[2 * u].x, x[2 * u].y, x[2 * u].z, x[2 * u].w,
+                                x[2 * u + 1].x, x[2 * u + 1].y, x[2 * u + 1].z, x[2 * u + 1].w};
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                hi[e] = pack_pair<T>(v[2 * e], v[2 * e + 1]);
+                const float2 hv = ElemTraits<T>::to_f2(*reinterpret_cast<const typename ElemTraits<T>::T2*>(&hi[e]));
+                lo[e] = pack_pair<T>(v[2 * e] - hv.x, v[2 * e + 1] - hv.y);
             }
+            const uint32_t dst = row + ((u ^ (t & 7)) << 4);
+            st_shared_v4(dst, hi[0], hi[1], hi[2], hi[3]);
+            st_shared_v4(dst + part_bytes, lo[0], lo[1], lo[2], lo[3]);
         }
+        // rope columns: scaled and rounded once, written straight to qpack
+        if (tok) {
+            T* dst = qpack + qpack_row(P, b0 + t, h) * K + dc + (dR / 2) * half;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int i = i0 + q * 128, t = i / upr, u = i % upr;
-            if (i < items) {
-                const uint32_t dst = b_u32 + (u >> 3) * (ntp * 128) + t * 128 + (((u & 7) ^ (t & 7)) << 4);
-                const float v[8] = {x[q].x, x[q].y, x[q].z, x[q].w, y[q].x, y[q].y, y[q].z, y[q].w};
-                uint32_t hi[4], lo[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    hi[e] = pack_pair<T>(v[2 * e], v[2 * e + 1]);
-                    const float2 h = ElemTraits<T>::to_f2(*reinterpret_cast<const typename ElemTraits<T>::T2*>(&hi[e]));
-                    lo[e] = pack_pair<T>(v[2 * e] - h.x, v[2 * e + 1] - h.y);
+            for (int u = 0; u < 8; u += 2) {
+                if (u < rq) {
+                    const uint4 y = make_uint4(pack_pair<T>(r[u].x * q_scale, r[u].y * q_scale),
+                                               pack_pair<T>(r[u].z * q_scale, r[u].w * q_scale),
+                                               pack_pair<T>(r[u + 1].x * q_scale, r[u + 1].y * q_scale),
+                                               pack_pair<T>(r[u + 1].z * q_scale, r[u + 1].w * q_scale));
+                    *reinterpret_cast<uint4*>(dst + 4 * u) = y;
                 }
-                st_shared_v4(dst, hi[0], hi[1], hi[2], hi[3]);
-                st_shared_v4(dst + lo_off, lo[0], lo[1], lo[2], lo[3]);
             }
         }
     }
     fence_proxy_async_smem();
     __syncthreads();
-    bool issued = true;   // thread 0: the W boxes landed and the MMAs were issued
+    bool issued = true;   // thread 0: W_UK landed and the MMAs were issued
     if (threadIdx.x == 0) {
-        issued = mbar_wait(a_full, 0, err, gcode(kSiteAbsorbA));
+        // a wait that ends only on completion or its time limit: shared memory must not be released
+        // under a TMA write
+        issued = mbar_wait_impl<false, false>(w_full, 0, err, gcode(kSiteAbsorbA), kDefaultWaitNs);
         if (issued) {
             tc_fence_after();
-            const uint32_t idesc = idesc_f16(128, ntp, GemmFmt<T>::v, true, false);
-            for (int part = 0; part < 2; ++part)   // hi, then lo, into the same accumulator
-                for (int k = 0; k < dn / 16; ++k) {
-                    const uint64_t ad = smem_desc_sw128(a_u32 + k * 2048, dn * 128, 1024);
-                    const uint64_t bd = smem_desc_sw128(b_u32 + part * lo_off + (k >> 2) * (ntp * 128) + (k & 3) * 32,
-                                                        16, 1024);
-                    mma_ss(tbase, ad, bd, idesc, (part | k) > 0 ? 1u : 0u);
-                }
+            const uint32_t idesc = idesc_f16(128, 256, GemmFmt<T>::v, false, true);
+            for (int nh = 0; nh < dc / 256; ++nh)
+                for (int part = 0; part < 2; ++part)   // hi, then lo, into the same accumulator
+                    for (int k = 0; k < dn / 16; ++k) {
+                        const uint64_t ad = smem_desc_sw128(a_u32 + part * part_bytes + (k >> 2) * chunk_bytes +
+                                                                (k & 3) * 32, 16, 1024);
+                        const uint64_t bd = smem_desc_sw128(w_u32 + nh * 4 * box_bytes + k * 2048, box_bytes, 1024);
+                        mma_ss(tbase + nh * 256, ad, bd, idesc, (part | k) > 0 ? 1u : 0u);
+                    }
         }
         mma_commit(mma_done);  // also arrives when nothing was issued
     }
-    // epilogue: thread (warp w, lane) holds d_c index m0 + 32 w + lane for every token column.
-    // The values go through shared memory (the B operand's space, free once the MMAs are done)
-    // as [token][128] rows of T, which are then written to qpack with 16-byte stores.
-    // the block-wide AND carries thread 0's result to every thread (no global status read)
-    bool ok = mbar_wait(mma_done, 0, err, gcode(kSiteAbsorbMma)) && issued;
-    ok = __all_sync(0xffffffffu, ok);
-    const bool all_ok = __syncthreads_and(ok);
-    T* stage = reinterpret_cast<T*>(smem + 2 * dn * 128);   // ntp x 128 elements <= B operand bytes
-    if (all_ok) {
+    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (its tokens) and the d_c columns of half
+    // w / 4, scales and rounds them into token rows of T in shared memory (the W_UK space, free once
+    // the MMAs completed; 16-byte units swizzled by token % 8), and the block then writes the rows to
+    // qpack with coalesced 16-byte stores (a warp covers 512 contiguous bytes).
+    bool ok = mbar_wait(mma_done, 0, err, gcode(kSiteAbsorbMma));
+    ok = __syncthreads_and(ok && (threadIdx.x != 0 || issued));
+    if (ok) {
         tc_fence_after();
-        const uint32_t trow = tbase + (static_cast<uint32_t>(32 * warp) << 16);
-        for (int c0 = 0; c0 < ntok; c0 += 16) {
-            uint32_t r[16];
-            tmem_ld16_sync(trow + c0, r);
+        const int tt = 32 * (warp & 3) + lane, ch = warp >> 2;
+        const uint32_t trow = tbase + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
+        const uint32_t srow = w_u32 + tt * (dc * 2);
+        for (int c0 = ch * (dc / 2); c0 < (ch + 1) * (dc / 2); c0 += 32) {
+            uint32_t v[32];
+            tmem_ld32_sync(trow + c0, v);
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-                stage[(c0 + j) * 128 + 32 * warp + lane] = ElemTraits<T>::from_f(__uint_as_float(r[j]) * q_scale);
+            for (int q = 0; q < 4; ++q) {
+                const int j = c0 / 8 + q;   // 16-byte unit of the row
+                st_shared_v4(srow + (((j & ~7) | ((j & 7) ^ (tt & 7))) << 4),
+                             pack_pair<T>(__uint_as_float(v[8 * q + 0]) * q_scale, __uint_as_float(v[8 * q + 1]) * q_scale),
+                             pack_pair<T>(__uint_as_float(v[8 * q + 2]) * q_scale, __uint_as_float(v[8 * q + 3]) * q_scale),
+                             pack_pair<T>(__uint_as_float(v[8 * q + 4]) * q_scale, __uint_as_float(v[8 * q + 5]) * q_scale),
+                             pack_pair<T>(__uint_as_float(v[8 * q + 6]) * q_scale, __uint_as_float(v[8 * q + 7]) * q_scale));
+            }
         }
         __syncthreads();
-        for (int i = threadIdx.x; i < ntok * 16; i += blockDim.x) {
-            const int n = i >> 4, v = i & 15;
-            const uint4 x = *reinterpret_cast<const uint4*>(stage + n * 128 + 8 * v);
-            *reinterpret_cast<uint4*>(qpack + qpack_row(P, b0 + n, h) * K + m0 + 8 * v) = x;
-        }
-    }
-    if (blockIdx.x == 0) {
-        // rope columns, 4 at a time
-        const int q4 = P.dR / 4;
-        for (int i = threadIdx.x; i < ntok * q4; i += blockDim.x) {
-            const int t = i / q4, j = 4 * (i % q4);
-            const long long flat = static_cast<long long>(b0 + t) * P.H + h;
-            const float4 x = *reinterpret_cast<const float4*>(q_rope + flat * P.dR + j);
-            const uint2 y = make_uint2(pack_pair<T>(x.x * q_scale, x.y * q_scale), pack_pair<T>(x.z * q_scale, x.w * q_scale));
-            *reinterpret_cast<uint2*>(qpack + qpack_row(P, b0 + t, h) * K + dc + j) = y;
+        const int upr = dc / 8;   // 16-byte units per row
+        for (int i2 = threadIdx.x; i2 < ntok * upr; i2 += blockDim.x) {
+            const int tk = i2 / upr, j = i2 % upr;
+            const uint4 y = *reinterpret_cast<const uint4*>(smem + tk * (dc * 2) + ((((j & ~7) | ((j & 7) ^ (tk & 7)))) << 4));
+            *reinterpret_cast<uint4*>(qpack + qpack_row(P, b0 + tk, h) * K + 8 * j) = y;
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tbase, tmem_cols);
+        tmem_dealloc(tbase, 512);
     }
+    // a W_UK wait that gave up: wait (bounded) for the boxes before the shared memory is released
+    if (threadIdx.x == 0 && !issued) mbar_wait_impl<false, false>(w_full, 0, err, gcode(kSiteAbsorbA), 100000000ull);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -398,11 +412,12 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
         mbar_arrive_expect_tx(a_full, static_cast<uint32_t>(nk * dv * 128));
         for (int j = 0; j < nk; ++j) tma_load_2d(a_u32 + j * dv * 128, &tmap_w, a_full, 64 * j, h * dv);
     }
-    pdl_wait();  // records and status come from the decode kernel
-    // The status load is issued now (unconditionally, so nothing waits for it here) and consumed
-    // after the merge, so it overlaps the record loads; a failed decode leaves garbage in the
-    // records, which are merged but never multiplied.
-    const int status0 = *err;
+    // With uniform lengths (or partial sets) the record lists are arithmetic on the plan and are
+    // built before the wait on the decode kernel; with variable lengths they read the tile prefix,
+    // which is complete only when that wait returns.
+    const bool lists_early = parts > 0 || P.uniform_len > 0;
+    if (!lists_early) pdl_wait();
+    int status0 = kStatusOk;
     const int step = parts ? P.B * P.H : kGroupRows;          // rows between a token's consecutive records
     const float mscale = parts ? 1.4426950408889634f : 1.f;   // m in log2 units
     {
@@ -446,6 +461,10 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
             }
         }
         __syncthreads();
+        if (lists_early) pdl_wait();  // records and status come from the decode kernel
+        // The status load is issued now and consumed after the merge, so it overlaps the record
+        // loads; a failed decode leaves garbage in the records, which are merged but never multiplied.
+        status0 = *err;
         // ---- merge into the B operand (fp32 sums, rounded once to T).
         // Job p = (token p % ntok, record split p / ntok) takes the records s, s + S, ... of the token,
         // lane l holding float4 units l, l + 32, l + 64, l + 96 of the d_c row. A warp carries two jobs
@@ -743,20 +762,22 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
         mbar_arrive_expect_tx(w_full, static_cast<uint32_t>(nk * dv * 128));
         for (int j = 0; j < nk; ++j) tma_load_2d(smem_u32(wsm) + j * dv * 128, &tmap_w, w_full, 64 * j, h * dv);
     }
-    pdl_wait();  // records and status come from the decode kernel
-    const int status0 = *err;   // consumed after the merge
     const int step = parts ? B * P.H : kGroupRows;
     const float mscale = parts ? 1.4426950408889634f : 1.f;   // m in log2 units
     const int U = dc / 4;                                      // float4 units per row, <= 128
 
-    // ---- 1. merge: warp w takes token t = w / wpt and records k = s, s + wpt, ... (s = w % wpt)
+    // ---- 1. merge: warp w takes token t = w / wpt and records k = s, s + wpt, ... (s = w % wpt).
+    // With uniform lengths (or partial sets) the record list is arithmetic on the plan and is built
+    // before the wait on the decode kernel; with variable lengths it reads the tile prefix.
     const int wpt = kGemvWarps / B;
     const int t = warp / wpt, s = warp % wpt;
+    const bool lists_early = parts > 0 || P.uniform_len > 0;
+    if (!lists_early) pdl_wait();
+    int n = parts, w0 = 0, ntiles = 0;
+    long long base = static_cast<long long>(t) * P.H + h;
+    bool busy = true;
     if (t < B) {
         const int b = t;
-        int n = parts, w0 = 0, ntiles = 0;
-        long long base = static_cast<long long>(b) * P.H + h;
-        bool busy = true;
         if (!parts) {
             ntiles = total_tiles(P);
             busy = ntiles >= P.W;   // every worker owns a tile: every record in the range exists
@@ -777,6 +798,10 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
             }
             base = static_cast<long long>(g + w0) * kGroupRows + r;
         }
+    }
+    if (lists_early) pdl_wait();  // records and status come from the decode kernel
+    const int status0 = *err;     // consumed after the merge
+    if (t < B) {
         const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
         float mrun = -INFINITY, lrun = 0.f;
         float4 acc[4] = {zero4, zero4, zero4, zero4};
@@ -905,7 +930,7 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
 }
 
 bool absorb_sm100_supported(const DecodePlan& P) {
-    return P.dc % 128 == 0 && P.dn % 64 == 0 && P.dn <= 256 && P.dR % 8 == 0;
+    return P.dn == 128 && P.dc % 256 == 0 && P.dc <= 512 && P.dR % 16 == 0 && P.dR <= 64;
 }
 
 bool project_sm100_supported(const DecodePlan& P) {
@@ -928,7 +953,7 @@ template <typename T>
 cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const T* W_UK, const float* q_rope,
                                 float q_scale, T* qpack, int* tile_prefix_out, cudaStream_t s) {
     if (!absorb_sm100_supported(P)) return cudaErrorInvalidValue;
-    if (P.B <= gemv_max_tokens() && P.dn == 128 && P.dc % kAbsorbGemvCols == 0) {
+    if (P.B <= gemv_max_tokens()) {
         const cudaError_t e = launch_ex(absorb_gemv_kernel<T>, dim3(P.dc / kAbsorbGemvCols, P.H), dim3(256), 0, s, false,
                                         P, q_nope, W_UK, q_rope, q_scale, qpack, tile_prefix_out);
         count_launches(1);
@@ -938,13 +963,12 @@ cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const 
     if (!make_tmap_2d_16b(&tmap, W_UK, static_cast<uint64_t>(P.H) * P.dn, static_cast<uint64_t>(P.dc),
                           static_cast<uint64_t>(P.dc), static_cast<uint32_t>(P.dn), 64))
         return cudaErrorInvalidValue;
-    const int ntp = pad16(P.B < kAbsorbTok ? P.B : kAbsorbTok);
-    const size_t smem = 1024 + 2 * P.dn * 128 + absorb_b_bytes(P.dn, ntp) + 64;
+    const size_t smem = 1024 + absorb_smem_bytes(P.dn, P.dc);
     cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(absorb_sm100_kernel<T>), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    dim3 grid(P.dc / 128, P.H, ceil_div(P.B, kAbsorbTok));
-    e = launch_ex(absorb_sm100_kernel<T>, grid, dim3(128), smem, s, false, tmap, P, q_nope, q_rope, q_scale, qpack,
-                  tile_prefix_out, ntp, tmem_cols_for(ntp));
+    dim3 grid(ceil_div(P.B, kAbsorbTok), P.H);
+    e = launch_ex(absorb_sm100_kernel<T>, grid, dim3(kAbsorbThreads), smem, s, false, tmap, P, q_nope, q_rope, q_scale,
+                  qpack, tile_prefix_out);
     count_launches(1);
     return e != cudaSuccess ? e : cudaGetLastError();
 }

@@ -116,12 +116,16 @@ __device__ inline int tile_prefix(const DecodePlan& P, int g) {
 
 __device__ inline int total_tiles(const DecodePlan& P) { return tile_prefix(P, P.G); }
 
+// (32-bit division while the products stay below 2^31: T < 2^23 tiles and W <= 256 workers)
 __device__ inline int worker_begin(int T, int W, int w) {
+    if (T < (1 << 23) && W <= 256) return static_cast<int>(static_cast<unsigned>(T * w) / static_cast<unsigned>(W));
     return static_cast<int>((static_cast<long long>(T) * w) / W);
 }
 
 // Worker owning global tile t.
 __device__ inline int worker_of_tile(int T, int W, int t) {
+    if (T < (1 << 23) && W <= 256)
+        return static_cast<int>(static_cast<unsigned>((t + 1) * W - 1) / static_cast<unsigned>(T));
     return static_cast<int>(((static_cast<long long>(t) + 1) * W - 1) / T);
 }
 
