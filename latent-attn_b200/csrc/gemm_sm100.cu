@@ -365,11 +365,44 @@ struct alignas(16) ProjLists {   // size a multiple of 16: the float4 scratch an
     float split_w[kProjRedMax];     // per (split, token): weight of the split's sum in the token's row
 };
 
+// Records of (token b, head h): n rows starting at `base`, `step` rows apart (decode records: the
+// workers w0 .. w0 + n - 1 that own tiles of the token's group; partial sets: all `parts` of them).
+__device__ __forceinline__ void proj_record_list(const DecodePlan& P, int b, int h, int parts, int ntiles, int& n,
+                                                 int& w0, int& base) {
+    n = parts;
+    w0 = 0;
+    base = b * P.H + h;
+    if (parts) return;
+    int g, r;
+    if (P.shared) {
+        const int f = b * P.H + h;
+        g = f / kGroupRows;
+        r = f % kGroupRows;
+    } else {
+        g = b * P.head_blocks + h / kGroupRows;
+        r = h % kGroupRows;
+    }
+    const int gt0 = tile_prefix(P, g), gt1 = tile_prefix(P, g + 1);
+    n = 0;
+    if (gt1 > gt0 && ntiles > 0) {
+        w0 = worker_of_tile(ntiles, P.W, gt0);
+        n = worker_of_tile(ntiles, P.W, gt1 - 1) - w0 + 1;
+    }
+    base = (g + w0) * kGroupRows + r;
+}
+
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 template <typename T>
 __global__ void __launch_bounds__(32 * kProjWarps)
 project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
                      const float* __restrict__ rec_o, float* __restrict__ out, int ntp, uint32_t tmem_cols,
-                     int parts, int ml_stride, int o_stride) {
+                     int parts, int ml_stride, int o_stride, int prefetch_stride) {
     // parts == 0: the decode kernel's partial records (m in log2 units, record g + w of group g).
     // parts > 0: that many partial sets of [part][B][H] rows (m, l at rec_ml + row * ml_stride, o at
     // rec_o + row * o_stride: the separate arrays of mla_decode_partial or its packed rows), with
@@ -426,45 +459,50 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
         const int ntiles = parts ? 0 : total_tiles(P);
         // every worker owns at least one tile unless there are fewer tiles than workers
         const bool all_workers_busy = ntiles >= P.W;
-        for (int t = warp; t < ntok; t += kProjWarps) {
-            const int b = b0 + t;
-            int n = parts, w0 = 0, base = b * P.H + h;
-            if (!parts) {
-                int g, r;
-                if (P.shared) {
-                    const int f = b * P.H + h;
-                    g = f / kGroupRows;
-                    r = f % kGroupRows;
+        // thread t builds token t's list (the record count and first row are a few integer divisions;
+        // with every worker busy, or for partial sets, record k exists for every k < n)
+        for (int t = threadIdx.x; t < ntok; t += blockDim.x) {
+            int n, w0, base;
+            proj_record_list(P, b0 + t, h, parts, ntiles, n, w0, base);
+            for (int c = 0; c < 4; ++c) {  // bit k % 32 of word k / 32: record k exists (n <= 128)
+                uint32_t mask = 0u;
+                const int k0 = 32 * c;
+                if (parts || all_workers_busy) {
+                    const int m = n - k0;
+                    mask = m >= 32 ? 0xffffffffu : (m > 0 ? (1u << m) - 1u : 0u);
                 } else {
-                    g = b * P.head_blocks + h / kGroupRows;
-                    r = h % kGroupRows;
+                    for (int k = k0; k < n && k < k0 + 32; ++k)
+                        if (worker_begin(ntiles, P.W, w0 + k) != worker_begin(ntiles, P.W, w0 + k + 1))
+                            mask |= 1u << (k - k0);
                 }
-                const int gt0 = tile_prefix(P, g), gt1 = tile_prefix(P, g + 1);
-                n = 0;
-                if (gt1 > gt0 && ntiles > 0) {
-                    w0 = worker_of_tile(ntiles, P.W, gt0);
-                    n = worker_of_tile(ntiles, P.W, gt1 - 1) - w0 + 1;
-                }
-                base = (g + w0) * kGroupRows + r;
+                L->valid[t][c] = mask;
             }
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {  // lane handles records k = lane + 32 c (n <= 128)
-                const int k = lane + 32 * c, w = w0 + k;
-                const bool in = k < n && (parts || all_workers_busy ||
-                                          worker_begin(ntiles, P.W, w) != worker_begin(ntiles, P.W, w + 1));
-                const uint32_t mask = __ballot_sync(0xffffffffu, in);
-                if (lane == 0) L->valid[t][c] = mask;
-            }
-            if (lane == 0) {
-                L->cnt[t] = n;
-                L->base[t] = base;
-            }
+            L->cnt[t] = n;
+            L->base[t] = base;
         }
         __syncthreads();
         if (lists_early) pdl_wait();  // records and status come from the decode kernel
         // The status load is issued now and consumed after the merge, so it overlaps the record
         // loads; a failed decode leaves garbage in the records, which are merged but never multiplied.
         status0 = *err;
+        // With more CTAs than SMs, the CTA `prefetch_stride` positions later in launch order runs on an
+        // SM after one of this wave: its records are prefetched into L2 now, so its merge reads L2.
+        {
+            const int nxt = blockIdx.x + gridDim.x * blockIdx.y + prefetch_stride;
+            if (prefetch_stride > 0 && nxt < static_cast<int>(gridDim.x * gridDim.y)) {
+                const int xb = nxt % gridDim.x, hh = nxt / gridDim.x;
+                const int nt = min(kProjTok, P.B - xb * kProjTok);
+                for (int t = threadIdx.x; t < nt; t += blockDim.x) {
+                    int n, w0, base;
+                    proj_record_list(P, xb * kProjTok + t, hh, parts, ntiles, n, w0, base);
+                    for (int k = 0; k < n; ++k) {
+                        const long long row = static_cast<long long>(base) + static_cast<long long>(k) * step;
+                        prefetch_l2_bulk(rec_o + row * o_stride, static_cast<uint32_t>(dc * sizeof(float)));
+                        prefetch_l2(rec_ml + row * ml_stride);
+                    }
+                }
+            }
+        }
         // ---- merge into the B operand (fp32 sums, rounded once to T).
         // Job p = (token p % ntok, record split p / ntok) takes the records s, s + S, ... of the token,
         // lane l holding float4 units l, l + 32, l + 64, l + 96 of the d_c row. A warp carries two jobs
@@ -773,32 +811,10 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
     const int t = warp / wpt, s = warp % wpt;
     const bool lists_early = parts > 0 || P.uniform_len > 0;
     if (!lists_early) pdl_wait();
-    int n = parts, w0 = 0, ntiles = 0;
-    long long base = static_cast<long long>(t) * P.H + h;
-    bool busy = true;
-    if (t < B) {
-        const int b = t;
-        if (!parts) {
-            ntiles = total_tiles(P);
-            busy = ntiles >= P.W;   // every worker owns a tile: every record in the range exists
-            int g, r;
-            if (P.shared) {
-                const int f = b * P.H + h;
-                g = f / kGroupRows;
-                r = f % kGroupRows;
-            } else {
-                g = b * P.head_blocks + h / kGroupRows;
-                r = h % kGroupRows;
-            }
-            const int gt0 = tile_prefix(P, g), gt1 = tile_prefix(P, g + 1);
-            n = 0;
-            if (gt1 > gt0 && ntiles > 0) {
-                w0 = worker_of_tile(ntiles, P.W, gt0);
-                n = worker_of_tile(ntiles, P.W, gt1 - 1) - w0 + 1;
-            }
-            base = static_cast<long long>(g + w0) * kGroupRows + r;
-        }
-    }
+    const int ntiles = parts ? 0 : total_tiles(P);
+    const bool busy = parts || ntiles >= P.W;   // every worker owns a tile: every record in the range exists
+    int n = 0, w0 = 0, base = 0;
+    if (t < B) proj_record_list(P, t, h, parts, ntiles, n, w0, base);
     if (lists_early) pdl_wait();  // records and status come from the decode kernel
     const int status0 = *err;     // consumed after the merge
     if (t < B) {
@@ -812,9 +828,9 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
             for (int q = 0; q < kGemvRec; ++q) {
                 const int k = k0 + q * wpt;
                 // a worker that owns no tile of the group wrote no record: it is never read
-                const bool in = k < n && (parts || busy ||
+                const bool in = k < n && (busy ||
                                           worker_begin(ntiles, P.W, w0 + k) != worker_begin(ntiles, P.W, w0 + k + 1));
-                const long long row = base + static_cast<long long>(k) * step;
+                const long long row = static_cast<long long>(base) + static_cast<long long>(k) * step;
                 mlq[q] = in ? __ldg(reinterpret_cast<const float2*>(rec_ml + row * ml_stride))
                             : make_float2(-INFINITY, 0.f);
 #pragma unroll
@@ -949,6 +965,19 @@ int gemv_max_tokens() {
     return v;
 }
 
+// SM count of the current device (cached per device).
+int sm_count() {
+    static std::mutex mu;
+    static std::vector<int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    std::lock_guard<std::mutex> lk(mu);
+    if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1, 0);
+    if (cache[dev] == 0 && cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        cache[dev] = 0;
+    return cache[dev];
+}
+
 template <typename T>
 cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const T* W_UK, const float* q_rope,
                                 float q_scale, T* qpack, int* tile_prefix_out, cudaStream_t s) {
@@ -997,7 +1026,7 @@ cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const 
     if (e != cudaSuccess) return e;
     dim3 grid(ceil_div(P.B, kProjTok), P.H);
     e = launch_ex(project_sm100_kernel<T>, grid, dim3(32 * kProjWarps), smem, s, pdl, tmap, P, rec_ml, rec_o, out, ntp,
-                  tmem_cols_for(ntp), parts, ml_stride, o_stride);
+                  tmem_cols_for(ntp), parts, ml_stride, o_stride, sm_count());
     count_launches(1);
     return e != cudaSuccess ? e : cudaGetLastError();
 }
