@@ -1,7 +1,7 @@
 // Split-KV combine and output projection.
 //
 // For every (token b, head h) the partial records of its group row are merged with
-// the log-sum-exp identity (records hold m in log2 units):
+// the log-sum-exp identity (records hold m in log2 units, l, and o_k, or o_k / l_k in fp16):
 //     M = max_k m_k,  L = sum_k l_k 2^(m_k - M),  o_lat = sum_k 2^(m_k - M) o_k / L
 // and projected through W_UV: out[b, h, j] = sum_i o_lat[i] * W_UV[h*dv + j, i]
 // (the projection of src/fused_mla.cu:258-267 / src/fused_mla_batched.cu:97-105).
@@ -36,7 +36,7 @@ struct MergeList {
 
 // Record list and weights of (b, h) -> slot t (executed by one warp).
 __device__ void build_merge_list(const DecodePlan& P, int b, int h, const float* __restrict__ rec_ml,
-                                 MergeList& ml, int t, bool normalise) {
+                                 MergeList& ml, int t, bool normalise, bool rec_normalised) {
     const int lane = threadIdx.x & 31;
     int g, r;
     if (P.shared) {
@@ -73,8 +73,10 @@ __device__ void build_merge_list(const DecodePlan& P, int b, int h, const float*
         const int rec = ml.rec[t][k];
         float a = 0.f;
         if (rec >= 0) {
+            const float l = rec_ml[(static_cast<long long>(rec) * kGroupRows + r) * 2 + 1];
             a = exp2f(ml.wgt[t][k] - M);
-            L += a * rec_ml[(static_cast<long long>(rec) * kGroupRows + r) * 2 + 1];
+            L += a * l;
+            if (rec_normalised) a *= l;   // a record holding o / l: its weight carries its row sum
         }
         ml.wgt[t][k] = a;
     }
@@ -195,7 +197,7 @@ struct PartOut {
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
-combine_kernel(DecodePlan P, const float* __restrict__ rec_ml, const float* __restrict__ rec_o,
+combine_kernel(DecodePlan P, const float* __restrict__ rec_ml, const T* __restrict__ rec_o,
                const T* __restrict__ W_UV, float* __restrict__ out, PartOut part) {
     extern __shared__ float o_s[];  // kTok * dc
     __shared__ MergeList ml;
@@ -212,7 +214,7 @@ combine_kernel(DecodePlan P, const float* __restrict__ rec_ml, const float* __re
         return;
     }
     const bool partial = out == nullptr;
-    if (warp < ntok) build_merge_list(P, b0 + warp, h, rec_ml, ml, warp, !partial);
+    if (warp < ntok) build_merge_list(P, b0 + warp, h, rec_ml, ml, warp, !partial, RecNorm<T>::value);
     __syncthreads();
     // merge: thread -> (token, column)
     for (int i = threadIdx.x; i < ntok * P.dc; i += kThreads) {
@@ -221,7 +223,9 @@ combine_kernel(DecodePlan P, const float* __restrict__ rec_ml, const float* __re
         float a = 0.f;
         for (int k = 0; k < ml.count[t]; ++k) {
             const int rec = ml.rec[t][k];
-            if (rec >= 0) a = fmaf(ml.wgt[t][k], rec_o[(static_cast<long long>(rec) * kGroupRows + r) * P.dc + c], a);
+            if (rec >= 0)
+                a = fmaf(ml.wgt[t][k], ElemTraits<T>::to_f(rec_o[(static_cast<long long>(rec) * kGroupRows + r) * P.dc + c]),
+                         a);
         }
         if (partial) part.o_at(part.row(b0 + t, h, P.B, P.H), P.dc)[c] = a;
         else o_s[t * P.dc + c] = a;
@@ -286,7 +290,7 @@ combine_parts_kernel(int B, int H, int dc, int dv, int parts, const float* __res
 }
 
 template <typename T>
-cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
+cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const T* rec_o, const T* W_UV,
                            float* out, float* part_ml, float* part_o, int packed_slices, cudaStream_t s) {
     if (P.W > kMaxRec) return cudaErrorInvalidValue;
     const size_t smem = static_cast<size_t>(kTok) * P.dc * sizeof(float);
@@ -317,7 +321,7 @@ cudaError_t launch_combine_parts(int B, int H, int dc, int dv, int parts, const 
 }
 
 #define MLA_INST(T)                                                                                   \
-    template cudaError_t launch_combine<T>(const DecodePlan&, const float*, const float*, const T*,  \
+    template cudaError_t launch_combine<T>(const DecodePlan&, const float*, const T*, const T*,      \
                                            float*, float*, float*, int, cudaStream_t);               \
     template cudaError_t launch_combine_parts<T>(int, int, int, int, int, const float*, const float*, \
                                                  int, int, const T*, float*, cudaStream_t);

@@ -27,7 +27,7 @@ template <typename T>
 __global__ void __launch_bounds__(kWarps * 32)
 decode_simt_kernel(DecodePlan P, const T* __restrict__ kv, const T* __restrict__ qpack,
                    const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
-                   float* __restrict__ rec_ml, float* __restrict__ rec_o) {
+                   float* __restrict__ rec_ml, T* __restrict__ rec_o) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int dc = P.dc, dR = P.dR, K = dc + dR, half = dR / 2;
     const int ldt = K / 2 + 1;                   // tile row stride in 32-bit words (padded)
@@ -142,10 +142,12 @@ decode_simt_kernel(DecodePlan P, const T* __restrict__ kv, const T* __restrict__
         }
         if (active_block && row < group_rows(P, g)) {
             const int rec = g + w;
-            float* o = rec_o + (static_cast<long long>(rec) * kGroupRows + row) * dc;
+            // the record holds o (bf16) or o / l (fp16) in T (l >= 1: the row's largest score contributes 2^0)
+            T* o = rec_o + (static_cast<long long>(rec) * kGroupRows + row) * dc;
+            const float inv_l = RecNorm<T>::value ? (l > 0.f ? 1.f / l : 0.f) : 1.f;
 #pragma unroll
             for (int i = 0; i < kMaxDcPerLane; ++i)
-                if (i < nper) o[lane + 32 * i] = acc[i];
+                if (i < nper) o[lane + 32 * i] = ElemTraits<T>::from_f(acc[i] * inv_l);
             if (lane == 0) {
                 float* ml = rec_ml + (static_cast<long long>(rec) * kGroupRows + row) * 2;
                 ml[0] = m;
@@ -160,7 +162,7 @@ decode_simt_kernel(DecodePlan P, const T* __restrict__ kv, const T* __restrict__
 
 template <typename T>
 cudaError_t launch_decode_simt(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
-                               const float* sin, float* rec_ml, float* rec_o, cudaStream_t s) {
+                               const float* sin, float* rec_ml, T* rec_o, cudaStream_t s) {
     const int K = P.dc + P.dR;
     size_t smem = static_cast<size_t>(kTile) * (K / 2 + 1) * 4 + static_cast<size_t>(kTile) * (P.dR + 1) * 4 +
                   static_cast<size_t>(kWarps) * K * 4;
@@ -176,9 +178,9 @@ cudaError_t launch_decode_simt(const DecodePlan& P, const T* kv, const T* qpack,
 int simt_tile() { return kTile; }
 
 template cudaError_t launch_decode_simt<__half>(const DecodePlan&, const __half*, const __half*,
-                                                const float*, const float*, float*, float*, cudaStream_t);
+                                                const float*, const float*, float*, __half*, cudaStream_t);
 template cudaError_t launch_decode_simt<__nv_bfloat16>(const DecodePlan&, const __nv_bfloat16*,
                                                        const __nv_bfloat16*, const float*, const float*,
-                                                       float*, float*, cudaStream_t);
+                                                       float*, __nv_bfloat16*, cudaStream_t);
 
 }  // namespace mla

@@ -97,6 +97,7 @@ struct __align__(8) Barriers {
     // and the other set, idle by then, writes half of the record's O columns
     uint64_t epi_go;
     int epi_rec, epi_rows;            // that record's index and valid rows
+    float epi_l[128];                 // and its rows' sums (an fp16 record holds o / l)
     uint32_t tmem_base;
 };
 
@@ -192,16 +193,26 @@ __device__ __forceinline__ void st_row32(float* p, const uint32_t (&v)[32]) {
                      : "memory");
 }
 
-// Writes `ncols` (a multiple of 32) fp32 columns of this thread's TMEM row to `orow` (skipped when
-// !row_ok), 32 columns at a time; 32-byte stores halve the store instructions of this
-// row-per-thread layout. Warp-collective.
-__device__ __forceinline__ void write_o_cols(uint32_t tsrc, float* orow, bool row_ok, int ncols) {
+// Writes `ncols` (a multiple of 64) columns of this thread's TMEM row to `orow` (skipped when
+// !row_ok) rounded to T (o / l when RecNorm<T>, else o): 64 columns (128 bytes) at a time, as
+// four 32-byte stores of this row-per-thread layout. Warp-collective.
+template <typename T>
+__device__ __forceinline__ void write_o_cols(uint32_t tsrc, T* orow, float inv_l, bool row_ok, int ncols) {
     for (int c0 = 0; c0 < ncols; c0 += 64) {
         uint32_t o[64];
         tmem_ld64_sync(tsrc + c0, o);
         if (row_ok) {
-            st_row32(orow + c0, *reinterpret_cast<const uint32_t(*)[32]>(&o[0]));
-            st_row32(orow + c0 + 32, *reinterpret_cast<const uint32_t(*)[32]>(&o[32]));
+            uint32_t p[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                float a = __uint_as_float(o[2 * i]), b = __uint_as_float(o[2 * i + 1]);
+                if constexpr (RecNorm<T>::value) {
+                    a *= inv_l;
+                    b *= inv_l;
+                }
+                p[i] = pack2<T>(a, b);
+            }
+            st_row32(reinterpret_cast<float*>(orow + c0), p);
         }
     }
 }
@@ -238,7 +249,7 @@ template <typename T, bool kPaged, bool kOtf>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_rope,
                     const DecodePlan P, const T* __restrict__ qpack, const float* __restrict__ cos_tab,
-                    const float* __restrict__ sin_tab, float* __restrict__ rec_ml, float* __restrict__ rec_o) {
+                    const float* __restrict__ sin_tab, float* __restrict__ rec_ml, T* __restrict__ rec_o) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     unsigned char* stages = smem;
@@ -843,11 +854,12 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
                         bars->epi_rec = rec;
                         bars->epi_rows = rows;
                     }
+                    bars->epi_l[t] = l_tot;
                     tc_fence_before();
                     mbar_arrive(smem_u32(&bars->epi_go));
                 }
-                write_o_cols(trow + kColO, rec_o + (static_cast<long long>(rec) * kGroupRows + t) * 512 + 256 * rank,
-                             t < rows, shared_epi ? 128 : 256);
+                write_o_cols<T>(trow + kColO, rec_o + (static_cast<long long>(rec) * kGroupRows + t) * 512 + 256 * rank,
+                                l_tot > 0.f ? 1.f / l_tot : 0.f, t < rows, shared_epi ? 128 : 256);
                 if (rank == 0 && t < rows)
                     *reinterpret_cast<float2*>(rec_ml + (static_cast<long long>(rec) * kGroupRows + t) * 2) =
                         make_float2(m, l_tot);
@@ -863,8 +875,10 @@ decode_sm100_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_const
             if (warp_ok(got)) {
                 tc_fence_after();
                 const int rec = bars->epi_rec;
-                write_o_cols(trow + kColO + 128, rec_o + (static_cast<long long>(rec) * kGroupRows + t) * 512 + 256 * rank + 128,
-                             t < bars->epi_rows, 128);
+                const float le = bars->epi_l[t];
+                write_o_cols<T>(trow + kColO + 128,
+                                rec_o + (static_cast<long long>(rec) * kGroupRows + t) * 512 + 256 * rank + 128,
+                                le > 0.f ? 1.f / le : 0.f, t < bars->epi_rows, 128);
             } else if (!got) {
                 note_fail(err, kWaitEpilogue, n - 1);
             }
@@ -894,7 +908,7 @@ bool decode_sm100_available() { return true; }
 
 template <typename T>
 cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
-                                const float* sin, float* rec_ml, float* rec_o, bool pdl, cudaStream_t s) {
+                                const float* sin, float* rec_ml, T* rec_o, bool pdl, cudaStream_t s) {
     if (P.dc != 512 || P.dR != 64 || P.tile != kTileN) return cudaErrorInvalidValue;
     CUtensorMap tmap, tmap_rope;
     const uint64_t rows = static_cast<uint64_t>(P.kv_rows), stride = static_cast<uint64_t>(P.row_stride);
@@ -937,9 +951,9 @@ cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack
 }
 
 template cudaError_t launch_decode_sm100<__half>(const DecodePlan&, const __half*, const __half*, const float*,
-                                                 const float*, float*, float*, bool, cudaStream_t);
+                                                 const float*, float*, __half*, bool, cudaStream_t);
 template cudaError_t launch_decode_sm100<__nv_bfloat16>(const DecodePlan&, const __nv_bfloat16*,
                                                         const __nv_bfloat16*, const float*, const float*, float*,
-                                                        float*, bool, cudaStream_t);
+                                                        __nv_bfloat16*, bool, cudaStream_t);
 
 }  // namespace mla

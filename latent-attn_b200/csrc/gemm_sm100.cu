@@ -398,15 +398,52 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
-template <typename T>
+// A lane's 16 elements of a partial row, as four float4 groups at columns col(lane, g):
+//   fp32 rows (the caller's partial sets, unnormalised): float4 unit lane + 32 g, i.e. columns 4 (lane + 32 g) ..;
+//   16-bit rows (the decode kernel's records, o or o / l by RecNorm): 16-byte unit lane + 32 (g / 2), i.e. columns
+//   8 (lane + 32 (g / 2)) + 4 (g % 2) ...
+// Rows hold d_c <= 512 elements; groups past d_c read as zeros.
+template <typename R> struct RecRow {
+    static constexpr bool kNormalised = RecNorm<R>::value;   // o / l (fp16 records of the decode kernel)
+    __device__ static int col(int lane, int g) { return 8 * (lane + 32 * (g >> 1)) + 4 * (g & 1); }
+    __device__ static void load(const R* row, int lane, int dc, bool in, float4 (&v)[4]) {
+        using T2 = typename ElemTraits<R>::T2;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int c = 8 * (lane + 32 * hh);
+            uint4 x = make_uint4(0u, 0u, 0u, 0u);
+            if (in && c < dc) x = __ldg(reinterpret_cast<const uint4*>(row + c));
+            const float2 a = ElemTraits<R>::to_f2(*reinterpret_cast<const T2*>(&x.x));
+            const float2 b = ElemTraits<R>::to_f2(*reinterpret_cast<const T2*>(&x.y));
+            const float2 cc = ElemTraits<R>::to_f2(*reinterpret_cast<const T2*>(&x.z));
+            const float2 d = ElemTraits<R>::to_f2(*reinterpret_cast<const T2*>(&x.w));
+            v[2 * hh] = make_float4(a.x, a.y, b.x, b.y);
+            v[2 * hh + 1] = make_float4(cc.x, cc.y, d.x, d.y);
+        }
+    }
+};
+template <> struct RecRow<float> {
+    static constexpr bool kNormalised = false;  // unnormalised o (partial sets of mla_decode_partial)
+    __device__ static int col(int lane, int g) { return 4 * (lane + 32 * g); }
+    __device__ static void load(const float* row, int lane, int dc, bool in, float4 (&v)[4]) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const int c = 4 * (lane + 32 * g);
+            v[g] = (in && c < dc) ? __ldg(reinterpret_cast<const float4*>(row + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+};
+
+template <typename T, typename R>
 __global__ void __launch_bounds__(32 * kProjWarps)
 project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
-                     const float* __restrict__ rec_o, float* __restrict__ out, int ntp, uint32_t tmem_cols,
+                     const R* __restrict__ rec_o, float* __restrict__ out, int ntp, uint32_t tmem_cols,
                      int parts, int ml_stride, int o_stride, int prefetch_stride) {
-    // parts == 0: the decode kernel's partial records (m in log2 units, record g + w of group g).
-    // parts > 0: that many partial sets of [part][B][H] rows (m, l at rec_ml + row * ml_stride, o at
-    // rec_o + row * o_stride: the separate arrays of mla_decode_partial or its packed rows), with
-    // m in natural-log units and l = 0 for an empty part (the KV-range shards' merge).
+    // parts == 0 (R = T): the decode kernel's partial records (m in log2 units, o rounded to T, or
+    // o / l for fp16, record g + w of group g). parts > 0 (R = float): that many partial sets of [part][B][H] rows
+    // (m, l at rec_ml + row * ml_stride, unnormalised o at rec_o + row * o_stride: the separate arrays
+    // of mla_decode_partial or its packed rows), with m in natural-log units and l = 0 for an empty
+    // part (the KV-range shards' merge).
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int dc = P.dc, dv = P.dv;
@@ -497,7 +534,7 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                     proj_record_list(P, xb * kProjTok + t, hh, parts, ntiles, n, w0, base);
                     for (int k = 0; k < n; ++k) {
                         const long long row = static_cast<long long>(base) + static_cast<long long>(k) * step;
-                        prefetch_l2_bulk(rec_o + row * o_stride, static_cast<uint32_t>(dc * sizeof(float)));
+                        prefetch_l2_bulk(rec_o + row * o_stride, static_cast<uint32_t>(dc * sizeof(R)));
                         prefetch_l2(rec_ml + row * ml_stride);
                     }
                 }
@@ -505,7 +542,7 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
         }
         // ---- merge into the B operand (fp32 sums, rounded once to T).
         // Job p = (token p % ntok, record split p / ntok) takes the records s, s + S, ... of the token,
-        // lane l holding float4 units l, l + 32, l + 64, l + 96 of the d_c row. A warp carries two jobs
+        // lane l holding the four float4 groups RecRow<R>::col(l, 0..3) of the d_c row. A warp carries two jobs
         // at once and loads the (m, l) pair and the o row of two records of each in one round trip,
         // folding them into a running log-sum-exp (max, row sum, rescaled o sum). With few tokens the
         // records of a token are split over S jobs (32 jobs in all), whose partial sums are rescaled
@@ -513,8 +550,7 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
         const int U = dc / 4;                                  // float4 units per row, <= 128
         int S = proj_red_rows(ntp) / ntok;
         S = S < 1 ? 1 : S;
-        auto store_b = [&](int t, int u, float4 v) {
-            const int c = 4 * u;
+        auto store_b = [&](int t, int c, float4 v) {   // columns c .. c + 3 of token t
             const uint32_t dst = b_u32 + (c >> 6) * (ntp * 128) + t * 128 + ((((c & 63) >> 3) ^ (t & 7)) << 4) +
                                  ((c & 7) >> 2) * 8;
             st_shared_v2(dst, pack_pair<T>(v.x, v.y), pack_pair<T>(v.z, v.w));
@@ -563,13 +599,7 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                     for (int q = 0; q < 2; ++q) {
                         mlq[j][q] = vq[j][q] ? __ldg(reinterpret_cast<const float2*>(rec_ml + rq[j][q] * ml_stride))
                                              : make_float2(-INFINITY, 0.f);
-#pragma unroll
-                        for (int u4 = 0; u4 < 4; ++u4) {
-                            const int u = lane + 32 * u4;
-                            v[j][q][u4] = (vq[j][q] && u < U)
-                                              ? __ldg(reinterpret_cast<const float4*>(rec_o + rq[j][q] * o_stride) + u)
-                                              : zero4;
-                        }
+                        RecRow<R>::load(rec_o + rq[j][q] * o_stride, lane, dc, vq[j][q], v[j][q]);
                     }
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
@@ -580,9 +610,13 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                     const float mnew = fmaxf(mrun[j], fmaxf(mq[0], mq[1]));
                     if (mnew == -INFINITY) continue;   // nothing in this job yet
                     const float sc = exp2f(mrun[j] - mnew);
-                    const float w0 = exp2f(mq[0] - mnew), w1 = exp2f(mq[1] - mnew);
+                    float w0 = exp2f(mq[0] - mnew), w1 = exp2f(mq[1] - mnew);
                     mrun[j] = mnew;
                     lrun[j] = fmaf(lrun[j], sc, fmaf(w0, mlq[j][0].y, w1 * mlq[j][1].y));
+                    if (RecRow<R>::kNormalised) {   // an fp16 record holds o / l: weigh it by its row sum
+                        w0 *= mlq[j][0].y;
+                        w1 *= mlq[j][1].y;
+                    }
 #pragma unroll
                     for (int u4 = 0; u4 < 4; ++u4) {
                         acc[j][u4].x = fmaf(acc[j][u4].x, sc, fmaf(w0, v[j][0][u4].x, w1 * v[j][1][u4].x));
@@ -599,17 +633,17 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                     const float inv = lrun[j] > 0.f ? 1.f / lrun[j] : 0.f;
 #pragma unroll
                     for (int u4 = 0; u4 < 4; ++u4) {
-                        const int u = lane + 32 * u4;
-                        if (u < U)
-                            store_b(tj[j], u, make_float4(acc[j][u4].x * inv, acc[j][u4].y * inv,
+                        const int c = RecRow<R>::col(lane, u4);
+                        if (c < dc)
+                            store_b(tj[j], c, make_float4(acc[j][u4].x * inv, acc[j][u4].y * inv,
                                                           acc[j][u4].z * inv, acc[j][u4].w * inv));
                     }
                 } else {
                     const int row = sj[j] * ntok + tj[j];
 #pragma unroll
                     for (int u4 = 0; u4 < 4; ++u4) {
-                        const int u = lane + 32 * u4;
-                        if (u < U) reinterpret_cast<float4*>(red)[row * U + u] = acc[j][u4];
+                        const int c = RecRow<R>::col(lane, u4);
+                        if (c < dc) reinterpret_cast<float4*>(red)[row * U + c / 4] = acc[j][u4];
                     }
                     if (lane == 0) L->split_ml[row] = make_float2(mrun[j], lrun[j]);
                 }
@@ -648,12 +682,12 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
                     a.z += __shfl_xor_sync(0xffffffffu, a.z, o);
                     a.w += __shfl_xor_sync(0xffffffffu, a.w, o);
                 }
-                if (q == 0) store_b(t, u, a);
+                if (q == 0) store_b(t, 4 * u, a);
             }
         }
         // padding token rows are zero
         for (int i = threadIdx.x; i < (ntp - ntok) * U; i += blockDim.x)
-            store_b(ntok + i / U, i % U, make_float4(0.f, 0.f, 0.f, 0.f));
+            store_b(ntok + i / U, 4 * (i % U), make_float4(0.f, 0.f, 0.f, 0.f));
     }
     const bool failed = parts == 0 && status0 != kStatusOk;
     if (failed) {
@@ -773,10 +807,10 @@ __host__ __device__ inline size_t gemv_smem_bytes(int dc, int dv) {
            16;                                                    // mbarrier
 }
 
-template <typename T>
+template <typename T, typename R>
 __global__ void __launch_bounds__(32 * kGemvWarps, 1)
 project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
-                    const float* __restrict__ rec_o, float* __restrict__ out, int parts, int ml_stride, int o_stride) {
+                    const R* __restrict__ rec_o, float* __restrict__ out, int parts, int ml_stride, int o_stride) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int dc = P.dc, dv = P.dv, B = P.B;   // dv == 128, dc % 64 == 0, dc <= 512, B <= kGemvMaxTok
@@ -802,7 +836,6 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
     }
     const int step = parts ? B * P.H : kGroupRows;
     const float mscale = parts ? 1.4426950408889634f : 1.f;   // m in log2 units
-    const int U = dc / 4;                                      // float4 units per row, <= 128
 
     // ---- 1. merge: warp w takes token t = w / wpt and records k = s, s + wpt, ... (s = w % wpt).
     // With uniform lengths (or partial sets) the record list is arithmetic on the plan and is built
@@ -833,12 +866,7 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
                 const long long row = static_cast<long long>(base) + static_cast<long long>(k) * step;
                 mlq[q] = in ? __ldg(reinterpret_cast<const float2*>(rec_ml + row * ml_stride))
                             : make_float2(-INFINITY, 0.f);
-#pragma unroll
-                for (int u4 = 0; u4 < 4; ++u4) {
-                    const int u = lane + 32 * u4;
-                    v[q][u4] = (in && u < U) ? __ldg(reinterpret_cast<const float4*>(rec_o + row * o_stride) + u)
-                                             : zero4;
-                }
+                RecRow<R>::load(rec_o + row * o_stride, lane, dc, in, v[q]);
             }
             float mq[kGemvRec];
             float mnew = mrun;
@@ -856,8 +884,9 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
             }
 #pragma unroll
             for (int q = 0; q < kGemvRec; ++q) {
-                const float wq = exp2f(mq[q] - mnew);
+                float wq = exp2f(mq[q] - mnew);
                 lrun = fmaf(wq, mlq[q].y, lrun);
+                if (RecRow<R>::kNormalised) wq *= mlq[q].y;   // an fp16 record holds o / l: weigh it by its row sum
 #pragma unroll
                 for (int u4 = 0; u4 < 4; ++u4) {
                     acc[u4].x = fmaf(wq, v[q][u4].x, acc[u4].x);
@@ -871,8 +900,8 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
         if (lane == 0) wml[warp] = make_float2(mrun, lrun);
 #pragma unroll
         for (int u4 = 0; u4 < 4; ++u4) {
-            const int u = lane + 32 * u4;
-            if (u < U) reinterpret_cast<float4*>(red + warp * dc)[u] = acc[u4];
+            const int c = RecRow<R>::col(lane, u4);
+            if (c < dc) *reinterpret_cast<float4*>(red + warp * dc + c) = acc[u4];
         }
     }
     __syncthreads();
@@ -1002,8 +1031,8 @@ cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const 
     return e != cudaSuccess ? e : cudaGetLastError();
 }
 
-template <typename T>
-cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
+template <typename T, typename R>
+cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const R* rec_o, const T* W_UV,
                                 float* out, bool pdl, int parts, int ml_stride, int o_stride, cudaStream_t s) {
     CUtensorMap tmap;
     if (!make_tmap_2d_16b(&tmap, W_UV, static_cast<uint64_t>(P.H) * P.dv, static_cast<uint64_t>(P.dc),
@@ -1011,9 +1040,9 @@ cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const 
         return cudaErrorInvalidValue;
     if (P.B <= gemv_max_tokens()) {
         const size_t smem = 1024 + gemv_smem_bytes(P.dc, P.dv);
-        cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(project_gemv_kernel<T>), static_cast<int>(smem));
+        cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(project_gemv_kernel<T, R>), static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        e = launch_ex(project_gemv_kernel<T>, dim3(P.H), dim3(32 * kGemvWarps), smem, s, pdl, tmap, P, rec_ml, rec_o,
+        e = launch_ex(project_gemv_kernel<T, R>, dim3(P.H), dim3(32 * kGemvWarps), smem, s, pdl, tmap, P, rec_ml, rec_o,
                       out, parts, ml_stride, o_stride);
         count_launches(1);
         return e != cudaSuccess ? e : cudaGetLastError();
@@ -1022,20 +1051,20 @@ cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const 
     const int nk = P.dc / 64;
     const size_t smem = 1024 + static_cast<size_t>(nk) * P.dv * 128 + static_cast<size_t>(nk) * ntp * 128 +
                         sizeof(ProjLists) + static_cast<size_t>(proj_red_rows(ntp)) * P.dc * sizeof(float) + 64;
-    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(project_sm100_kernel<T>), static_cast<int>(smem));
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(project_sm100_kernel<T, R>), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     dim3 grid(ceil_div(P.B, kProjTok), P.H);
-    e = launch_ex(project_sm100_kernel<T>, grid, dim3(32 * kProjWarps), smem, s, pdl, tmap, P, rec_ml, rec_o, out, ntp,
+    e = launch_ex(project_sm100_kernel<T, R>, grid, dim3(32 * kProjWarps), smem, s, pdl, tmap, P, rec_ml, rec_o, out, ntp,
                   tmem_cols_for(ntp), parts, ml_stride, o_stride, sm_count());
     count_launches(1);
     return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <typename T>
-cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
+cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const T* rec_o, const T* W_UV,
                                  float* out, bool pdl, cudaStream_t s) {
     if (!project_sm100_supported(P)) return cudaErrorInvalidValue;
-    return launch_project_impl<T>(P, rec_ml, rec_o, W_UV, out, pdl, 0, 2, P.dc, s);
+    return launch_project_impl<T, T>(P, rec_ml, rec_o, W_UV, out, pdl, 0, 2, P.dc, s);
 }
 
 // Status word of the partial-set merge: that path has no decode status to check, but the
@@ -1075,13 +1104,13 @@ cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, 
     P.B = B;
     P.head_blocks = ceil_div(H, kGroupRows);
     P.status = status;
-    return launch_project_impl<T>(P, part_ml, part_o, W_UV, out, false, parts, ml_stride, o_stride, s);
+    return launch_project_impl<T, float>(P, part_ml, part_o, W_UV, out, false, parts, ml_stride, o_stride, s);
 }
 
 #define MLA_INST(T)                                                                                              \
     template cudaError_t launch_absorb_sm100<T>(const DecodePlan&, const float*, const T*, const float*, float, T*, \
                                                 int*, cudaStream_t);                                             \
-    template cudaError_t launch_project_sm100<T>(const DecodePlan&, const float*, const float*, const T*, float*,   \
+    template cudaError_t launch_project_sm100<T>(const DecodePlan&, const float*, const T*, const T*, float*,       \
                                                  bool, cudaStream_t);                                             \
     template cudaError_t launch_project_parts_sm100<T>(int, int, int, int, int, const float*, const float*, int, int, \
                                                        const T*, \

@@ -256,8 +256,8 @@ mla_status_t make_plan(const mla_config_t* cfg, const mla_decode_args_t* a, Plan
     off = align_up(off + static_cast<size_t>(d.G) * mla::kGroupRows * (dc + dR) * 2);
     p->off_rec_ml = off;
     off = align_up(off + static_cast<size_t>(p->nrec) * mla::kGroupRows * 2 * sizeof(float));
-    p->off_rec_o = off;
-    off = align_up(off + static_cast<size_t>(p->nrec) * mla::kGroupRows * dc * sizeof(float));
+    p->off_rec_o = off;   // o / l rows in the cache's 16-bit type
+    off = align_up(off + static_cast<size_t>(p->nrec) * mla::kGroupRows * dc * 2);
     p->total = off;
 
     // the tcgen05 GEMMs run on sm_100 whenever their shape constraints hold
@@ -291,7 +291,7 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
     d.status = reinterpret_cast<int*>(ws + pl.off_status);
     T* qpack = reinterpret_cast<T*>(ws + pl.off_qpack);
     float* rec_ml = reinterpret_cast<float*>(ws + pl.off_rec_ml);
-    float* rec_o = reinterpret_cast<float*>(ws + pl.off_rec_o);
+    T* rec_o = reinterpret_cast<T*>(ws + pl.off_rec_o);
     // the status words are cleared by the first kernel below (clear_status)
     cudaError_t e = cudaSuccess;
     int* prefix_out = d.uniform_len > 0 ? nullptr : prefix;
@@ -665,7 +665,8 @@ mla_status_t mla_launch_fused_noalloc(const mla_fused_params_t* p, mla_dtype_t d
     a.output = p->output;
     // Largest worker count whose workspace fits the static array (fewer workers, fewer
     // partial records). Each worker beyond the first adds one record of kGroupRows rows of
-    // (m, l, o[d_c]) fp32, a multiple of the 256-byte alignment, so the scratch grows by
+    // (m, l) fp32 and o[d_c] in the 16-bit cache type, each part a multiple of the 256-byte
+    // alignment, so the scratch grows by
     // exactly that much per worker and the cap follows from the one-worker size. A problem
     // that does not fit even with one worker is rejected before anything is launched.
     Plan pl;
@@ -675,7 +676,8 @@ mla_status_t mla_launch_fused_noalloc(const mla_fused_params_t* p, mla_dtype_t d
         return fail(MLA_ERR_UNSUPPORTED,
                     "problem needs %zu bytes of scratch; the static scratch of mla_launch_fused_noalloc holds %u",
                     pl.total, static_cast<unsigned>(MLA_NOALLOC_SCRATCH_BYTES));
-    const size_t per_worker = static_cast<size_t>(mla::kGroupRows) * (2 + p->cfg->kv_lora_rank) * sizeof(float);
+    const size_t per_worker =
+        static_cast<size_t>(mla::kGroupRows) * (2 * sizeof(float) + static_cast<size_t>(p->cfg->kv_lora_rank) * 2);
     const size_t extra = (MLA_NOALLOC_SCRATCH_BYTES - pl.total) / per_worker;
     const int workers = static_cast<int>(extra > 4096 ? 4097 : extra + 1);
     st = make_plan(p->cfg, &a, &pl, workers);

@@ -13,8 +13,10 @@
 //     rec(g, w) = g + w is unique because, walking tiles in order, every step to
 //     the next (group, worker) piece advances g or w. The combine kernel finds
 //     group g's records from the workers holding its first and last tile.
-//   * A record holds, per row: m (running max, log2 units), l (sum of 2^(s-m)),
-//     and o (unnormalised sum of 2^(s-m) * c_t, d_c floats).
+//   * A record holds, per row: m (running max, log2 units) and l (sum of 2^(s-m)) in
+//     fp32 (rec_ml), and the row's sum o of 2^(s-m) * c_t (d_c elements) rounded to the
+//     cache's 16-bit type (rec_o): o itself in bf16 (fp32's exponent range), o / l in fp16
+//     (a convex combination of fp16 cache rows stays inside fp16's range), see RecNorm.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -224,6 +226,12 @@ template <> struct ElemTraits<__nv_bfloat16> {
     using T2 = __nv_bfloat162;
 };
 
+// Partial-record o in the cache type T: the normalised o / l for fp16 (whose range an unnormalised
+// sum of up to 2^31 positions could leave), the plain sum o for bf16. The merge weighs a normalised
+// record by its row sum l.
+template <typename T> struct RecNorm { static constexpr bool value = false; };
+template <> struct RecNorm<__half> { static constexpr bool value = true; };
+
 // Device error codes written to DecodePlan::status.
 enum : int { kStatusOk = 0, kStatusTimeout = 1, kStatusBadPlan = 2, kStatusBadPage = 3 };
 
@@ -245,7 +253,7 @@ template <typename T>
 cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const T* W_UK, const float* q_rope,
                                 float q_scale, T* qpack, int* tile_prefix_out, cudaStream_t s);
 template <typename T>
-cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const float* rec_o, const T* W_UV,
+cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const T* rec_o, const T* W_UV,
                                  float* out, bool pdl, cudaStream_t s);
 // merge of gathered partial sets of [parts][B][H] rows -- (m natural-log max, l sum; l = 0 = empty)
 // at part_ml + row * ml_stride and o at part_o + row * o_stride -- followed by the W_UV projection
@@ -261,13 +269,13 @@ cudaError_t launch_linear_sm100(const T* X, const T* W, float* Y, int M, int N, 
 // decode_simt.cu
 template <typename T>
 cudaError_t launch_decode_simt(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
-                               const float* sin, float* rec_ml, float* rec_o, cudaStream_t s);
+                               const float* sin, float* rec_ml, T* rec_o, cudaStream_t s);
 // decode_sm100.cu
 // pdl: launch with a programmatic dependency on the previous kernel (its prologue and
 // cache loads overlap that kernel's tail)
 template <typename T>
 cudaError_t launch_decode_sm100(const DecodePlan& P, const T* kv, const T* qpack, const float* cos,
-                                const float* sin, float* rec_ml, float* rec_o, bool pdl, cudaStream_t s);
+                                const float* sin, float* rec_ml, T* rec_o, bool pdl, cudaStream_t s);
 bool decode_sm100_available();
 // cache.cu
 template <typename T>
@@ -278,7 +286,7 @@ cudaError_t launch_cache_append(T* kv, long long stride, long long kv_rows, int 
 // out == nullptr: export one partial per (b, h) instead, to part_ml (B, H, 2) / part_o (B, H, dc),
 // or with packed_slices > 0 to packed rows of dc + 4 floats at part_o (see mla_decode_partial_packed)
 template <typename T>
-cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const float* rec_o,
+cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const T* rec_o,
                            const T* W_UV, float* out, float* part_ml, float* part_o, int packed_slices,
                            cudaStream_t s);
 template <typename T>

@@ -88,11 +88,12 @@ def test_noalloc_matches_golden_directly():
 
 
 def test_noalloc_near_its_scratch_limit():
-    """2560 heads (20 query groups) fit the static array only with a single split-KV worker:
-    the call runs with the reduced worker count and matches the pool launcher, which splits
-    the same problem over many workers."""
+    """3840 heads (30 query groups) fit the static array only with a single split-KV worker
+    (query pack 4,423,680 bytes + 30 records of 132,096 bytes + status and prefix, 8,387,072 of
+    8,388,608 bytes): the call runs with the reduced worker count and matches the pool launcher,
+    which splits the same problem over many workers."""
     lib = _lib.load()
-    H, S = 2560, 300
+    H, S = 3840, 300
     dev = torch.device("cuda")
     g = torch.Generator().manual_seed(17)
     kv = torch.randn(S, 576, generator=g).to(torch.bfloat16).to(dev)
@@ -108,21 +109,28 @@ def test_noalloc_near_its_scratch_limit():
     st = _launch(lib.mla_launch_fused_noalloc, cfg, kv, S, qa, qr, wuv, cos, sin, got)
     assert st == _lib.MLA_OK, lib.mla_last_error()
     torch.cuda.synchronize()
-    _close(got.cpu().numpy(), want.cpu().numpy(), "noalloc vs pool launcher, H=2560")
+    _close(got.cpu().numpy(), want.cpu().numpy(), "noalloc vs pool launcher, H=3840")
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
-    """2816 heads need 22 query groups: more scratch than the static array holds.
-    The call is refused on the host before any launch, so the (tiny) buffers
-    passed here are never read."""
+    """8192 heads need 64 query groups: more scratch than the static array holds (the query pack
+    alone is 64 x 128 rows of 576 16-bit elements, 9.4 MB). The call is refused on the host before
+    any launch. Every buffer still has the size the problem needs, so that a launch, were the call
+    ever accepted, would stay inside them."""
     lib = _lib.load()
-    cfg = _lib.MlaConfig(0, 512, 128, 64, 2816, 128)
-    buf = torch.zeros(4096, dtype=torch.bfloat16, device="cuda")
-    f32 = torch.zeros(4096, dtype=torch.float32, device="cuda")
-    out = torch.zeros(16, dtype=torch.float32, device="cuda")
-    p = _lib.MlaFusedParams(buf.data_ptr(), 16, f32.data_ptr(), f32.data_ptr(), buf.data_ptr(), f32.data_ptr(),
-                            f32.data_ptr(), out.data_ptr(), C.pointer(cfg))
+    H, S = 8192, 16
+    dev = torch.device("cuda")
+    cfg = _lib.MlaConfig(0, 512, 128, 64, H, 128)
+    kv = torch.zeros(S, 576, dtype=torch.bfloat16, device=dev)
+    qa = torch.zeros(H, 512, dtype=torch.float32, device=dev)
+    qr = torch.zeros(H, 64, dtype=torch.float32, device=dev)
+    wuv = torch.zeros(H * 128, 512, dtype=torch.bfloat16, device=dev)
+    cos, sin = synthetic.build_rope_tables(S, 64, device=dev)
+    out = torch.zeros(H, 128, dtype=torch.float32, device=dev)
+    p = _lib.MlaFusedParams(kv.data_ptr(), S, qa.data_ptr(), qr.data_ptr(), wuv.data_ptr(), cos.data_ptr(),
+                            sin.data_ptr(), out.data_ptr(), C.pointer(cfg))
     st = lib.mla_launch_fused_noalloc(C.byref(p), _lib.DTYPE_BF16, C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
     assert st == _lib.MLA_ERR_UNSUPPORTED
     msg = lib.mla_last_error().decode()
     assert "scratch" in msg and str(_lib.NOALLOC_SCRATCH_BYTES) in msg, msg
