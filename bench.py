@@ -88,6 +88,17 @@ def measured_peaks():
     return HBM_FALLBACK_GBS, "fallback (6.65 TB/s, earlier pool measurement)"
 
 
+def measured_tensor_peak():
+    """Sustained dense bf16 TFLOP/s (MEASURED_PEAKS.json), the denominator for a kernel timed inside a long step."""
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        if "bf16_tflops_sustained" in d:
+            return float(d["bf16_tflops_sustained"]), "measured (MEASURED_PEAKS.json bf16_tflops_sustained)"
+    return 1400.0, "fallback (1.4 PFLOP/s sustained, earlier pool measurement)"
+
+
 def ncu_traffic(workload, share=1.0):
     """Per-launch DRAM bytes of the decode kernel from the committed ncu summary (a one-GPU launch
     over the whole workload), scaled by the share of the workload's cache rows this rank's launch
@@ -649,6 +660,14 @@ def main(argv=None):
                     "frac": round(achieved / peak, 4), "traffic": traffic,
                     "kernel": "mla::decode_sm100_kernel", "kernel_us": round(dmean * 1e3, 3),
                     "algorithmic_bytes": bytes_per_step, "peak_source": peak_src + " -- fraction is of measured"}
+            # the same kernel against the tensor pipe: per cache row 128 heads x 2 x (576 + 512) flop
+            # (score over [c_t | k_rope], then P . c_t), 242 flop per byte
+            tpeak, tsrc = measured_tensor_peak()
+            flops = bytes_per_step // CACHE_ROW_BYTES * 128 * 2 * (576 + 512)
+            tflops = flops / dmean / 1e9
+            roof["tensor"] = {"achieved": round(tflops, 1), "peak": tpeak, "unit": "TFLOP/s",
+                              "frac": round(tflops / tpeak, 4), "flops": flops,
+                              "peak_source": tsrc + " -- fraction is of measured"}
         cpu = cfg0 = None
         if world == 1 and not args.no_cpu_baseline:
             gbs, cores, sample = cpu_oracle_rate(lens_all, args.cpu_seconds)
