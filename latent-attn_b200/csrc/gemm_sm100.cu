@@ -37,6 +37,7 @@
 #include "mla_internal.cuh"
 #include "sm100_ptx.cuh"
 #include "tma_host.cuh"
+#include "proj_unit.cuh"
 
 namespace mla {
 using namespace sm100;
@@ -63,23 +64,6 @@ __device__ __forceinline__ uint32_t pack_pair<__nv_bfloat16>(float a, float b) {
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
-// AND of `pred` over the `nthreads` threads (whole warps) that reach named barrier `id`.
-__device__ __forceinline__ bool bar_red_and(int id, int nthreads, bool pred) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "barrier.red.and.pred q, %2, %3, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(nthreads)
-        : "memory");
-    return r != 0;
-}
-__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t a, uint32_t b) {
-    asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
-}
-
 // query-pack row of token n (single query per sequence: n = b; shared cache: flattened)
 __device__ __forceinline__ long long qpack_row(const DecodePlan& P, int b, int h) {
     return P.shared ? static_cast<long long>(b) * P.H + h
@@ -88,13 +72,8 @@ __device__ __forceinline__ long long qpack_row(const DecodePlan& P, int b, int h
 
 constexpr int kAbsorbTok = 128;    // tokens per absorption CTA (MMA M)
 constexpr int kAbsorbThreads = 256;
-constexpr int kProjTok = 64;       // tokens per projection CTA
+using proj::kProjTok;               // tokens per projection CTA
 constexpr int kProjWarps = 16;     // projection CTA: 16 warps merge, warp 0 issues the MMA, warps 4-7 store
-// rows of split partial sums of the merge (S * ntok <= rows): 32 when the token operand is at most
-// 16 rows (32 merge jobs for the 16 warps), else 8, which keeps the largest configuration inside the
-// shared-memory limit
-__host__ __device__ constexpr int proj_red_rows(int ntp) { return ntp <= 16 ? 32 : 8; }
-constexpr int kProjRedMax = 32;    // the largest proj_red_rows
 
 // absorption shared memory: W_UK_h (d_c / 64 boxes of dn rows x 128 B), the hi and lo A parts, barriers
 __host__ __device__ inline size_t absorb_smem_bytes(int dn, int dc) {
@@ -356,41 +335,6 @@ absorb_gemv_kernel(const DecodePlan P, const float* __restrict__ q_nope, const T
 // ------------------------------------------------------------------------------------------
 // merge + projection
 // ------------------------------------------------------------------------------------------
-// Per-token record lists (records are read straight from global memory / L2).
-struct alignas(16) ProjLists {   // size a multiple of 16: the float4 scratch and mbarriers follow it
-    int cnt[kProjTok];           // records of token t
-    int base[kProjTok];          // row of token t's first record; record k is at row base + k * step
-    uint32_t valid[kProjTok][4]; // bit k: record k exists (a worker that owns no tile of the group wrote none)
-    float2 split_ml[kProjRedMax];   // per (split, token) job: running max (log2 units) and row sum
-    float split_w[kProjRedMax];     // per (split, token): weight of the split's sum in the token's row
-};
-
-// Records of (token b, head h): n rows starting at `base`, `step` rows apart (decode records: the
-// workers w0 .. w0 + n - 1 that own tiles of the token's group; partial sets: all `parts` of them).
-__device__ __forceinline__ void proj_record_list(const DecodePlan& P, int b, int h, int parts, int ntiles, int& n,
-                                                 int& w0, int& base) {
-    n = parts;
-    w0 = 0;
-    base = b * P.H + h;
-    if (parts) return;
-    int g, r;
-    if (P.shared) {
-        const int f = b * P.H + h;
-        g = f / kGroupRows;
-        r = f % kGroupRows;
-    } else {
-        g = b * P.head_blocks + h / kGroupRows;
-        r = h % kGroupRows;
-    }
-    const int gt0 = tile_prefix(P, g), gt1 = tile_prefix(P, g + 1);
-    n = 0;
-    if (gt1 > gt0 && ntiles > 0) {
-        w0 = worker_of_tile(ntiles, P.W, gt0);
-        n = worker_of_tile(ntiles, P.W, gt1 - 1) - w0 + 1;
-    }
-    base = (g + w0) * kGroupRows + r;
-}
-
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
@@ -398,42 +342,7 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
-// A lane's 16 elements of a partial row, as four float4 groups at columns col(lane, g):
-//   fp32 rows (the caller's partial sets, unnormalised): float4 unit lane + 32 g, i.e. columns 4 (lane + 32 g) ..;
-//   16-bit rows (the decode kernel's records, o or o / l by RecNorm): 16-byte unit lane + 32 (g / 2), i.e. columns
-//   8 (lane + 32 (g / 2)) + 4 (g % 2) ...
-// Rows hold d_c <= 512 elements; groups past d_c read as zeros.
-template <typename R> struct RecRow {
-    static constexpr bool kNormalised = RecNorm<R>::value;   // o / l (fp16 records of the decode kernel)
-    __device__ static int col(int lane, int g) { return 8 * (lane + 32 * (g >> 1)) + 4 * (g & 1); }
-    __device__ static void load(const R* row, int lane, int dc, bool in, float4 (&v)[4]) {
-        using T2 = typename ElemTraits<R>::T2;
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-            const int c = 8 * (lane + 32 * hh);
-            uint4 x = make_uint4(0u, 0u, 0u, 0u);
-            if (in && c < dc) x = __ldg(reinterpret_cast<const uint4*>(row + c));
-            const float2 a = ElemTraits<R>::to_f2(*reinterpret_cast<const T2*>(&x.x));
-            const float2 b = ElemTraits<R>::to_f2(*reinterpret_cast<const T2*>(&x.y));
-            const float2 cc = ElemTraits<R>::to_f2(*reinterpret_cast<const T2*>(&x.z));
-            const float2 d = ElemTraits<R>::to_f2(*reinterpret_cast<const T2*>(&x.w));
-            v[2 * hh] = make_float4(a.x, a.y, b.x, b.y);
-            v[2 * hh + 1] = make_float4(cc.x, cc.y, d.x, d.y);
-        }
-    }
-};
-template <> struct RecRow<float> {
-    static constexpr bool kNormalised = false;  // unnormalised o (partial sets of mla_decode_partial)
-    __device__ static int col(int lane, int g) { return 4 * (lane + 32 * g); }
-    __device__ static void load(const float* row, int lane, int dc, bool in, float4 (&v)[4]) {
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-            const int c = 4 * (lane + 32 * g);
-            v[g] = (in && c < dc) ? __ldg(reinterpret_cast<const float4*>(row + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-    }
-};
-
+// One CTA per (block of up to 64 tokens, head); the unit's steps are in proj_unit.cuh.
 template <typename T, typename R>
 __global__ void __launch_bounds__(32 * kProjWarps)
 project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
@@ -451,14 +360,14 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
     const uint32_t a_u32 = smem_u32(smem);                    // nk x (dv rows x 128 B)
     const uint32_t b_u32 = a_u32 + nk * dv * 128;             // nk x (ntp rows x 128 B)
     unsigned char* tail = smem + nk * dv * 128 + nk * ntp * 128;
-    ProjLists* L = reinterpret_cast<ProjLists*>(tail);
-    float* red = reinterpret_cast<float*>(tail + sizeof(ProjLists));   // split partial sums: proj_red_rows(ntp) x d_c
-    uint64_t* bars = reinterpret_cast<uint64_t*>(tail + sizeof(ProjLists) +
-                                                 static_cast<size_t>(proj_red_rows(ntp)) * dc * sizeof(float));
+    proj::Lists* L = reinterpret_cast<proj::Lists*>(tail);
+    float* red = reinterpret_cast<float*>(tail + sizeof(proj::Lists));   // split partial sums: red_rows(ntp) x d_c
+    uint64_t* bars = reinterpret_cast<uint64_t*>(tail + sizeof(proj::Lists) +
+                                                 static_cast<size_t>(proj::red_rows(ntp)) * dc * sizeof(float));
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
     const uint32_t a_full = smem_u32(&bars[0]), mma_done = smem_u32(&bars[1]);
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
     const int b0 = blockIdx.x * kProjTok, h = blockIdx.y;
     const int ntok = min(kProjTok, P.B - b0);
     volatile int* err = P.status;
@@ -487,215 +396,34 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
     // which is complete only when that wait returns.
     const bool lists_early = parts > 0 || P.uniform_len > 0;
     if (!lists_early) pdl_wait();
-    int status0 = kStatusOk;
     const int step = parts ? P.B * P.H : kGroupRows;          // rows between a token's consecutive records
-    const float mscale = parts ? 1.4426950408889634f : 1.f;   // m in log2 units
+    const int ntiles = parts ? 0 : total_tiles(P);
+    proj::build_lists(P, L, b0, ntok, h, parts, ntiles);
+    __syncthreads();
+    if (lists_early) pdl_wait();  // records and status come from the decode kernel
+    // The status load is issued now and consumed after the merge, so it overlaps the record loads;
+    // a failed decode leaves garbage in the records, which are merged but never multiplied.
+    const int status0 = *err;
+    // With more CTAs than SMs, the CTA `prefetch_stride` positions later in launch order runs on an
+    // SM after one of this wave: its records are prefetched into L2 now, so its merge reads L2.
     {
-        // ---- record lists: token t's group row is merged from the workers w0 .. w0 + cnt - 1 of its
-        // tiles (decode records) or from all parts
-        const int ntiles = parts ? 0 : total_tiles(P);
-        // every worker owns at least one tile unless there are fewer tiles than workers
-        const bool all_workers_busy = ntiles >= P.W;
-        // thread t builds token t's list (the record count and first row are a few integer divisions;
-        // with every worker busy, or for partial sets, record k exists for every k < n)
-        for (int t = threadIdx.x; t < ntok; t += blockDim.x) {
-            int n, w0, base;
-            proj_record_list(P, b0 + t, h, parts, ntiles, n, w0, base);
-            for (int c = 0; c < 4; ++c) {  // bit k % 32 of word k / 32: record k exists (n <= 128)
-                uint32_t mask = 0u;
-                const int k0 = 32 * c;
-                if (parts || all_workers_busy) {
-                    const int m = n - k0;
-                    mask = m >= 32 ? 0xffffffffu : (m > 0 ? (1u << m) - 1u : 0u);
-                } else {
-                    for (int k = k0; k < n && k < k0 + 32; ++k)
-                        if (worker_begin(ntiles, P.W, w0 + k) != worker_begin(ntiles, P.W, w0 + k + 1))
-                            mask |= 1u << (k - k0);
-                }
-                L->valid[t][c] = mask;
-            }
-            L->cnt[t] = n;
-            L->base[t] = base;
-        }
-        __syncthreads();
-        if (lists_early) pdl_wait();  // records and status come from the decode kernel
-        // The status load is issued now and consumed after the merge, so it overlaps the record
-        // loads; a failed decode leaves garbage in the records, which are merged but never multiplied.
-        status0 = *err;
-        // With more CTAs than SMs, the CTA `prefetch_stride` positions later in launch order runs on an
-        // SM after one of this wave: its records are prefetched into L2 now, so its merge reads L2.
-        {
-            const int nxt = blockIdx.x + gridDim.x * blockIdx.y + prefetch_stride;
-            if (prefetch_stride > 0 && nxt < static_cast<int>(gridDim.x * gridDim.y)) {
-                const int xb = nxt % gridDim.x, hh = nxt / gridDim.x;
-                const int nt = min(kProjTok, P.B - xb * kProjTok);
-                for (int t = threadIdx.x; t < nt; t += blockDim.x) {
-                    int n, w0, base;
-                    proj_record_list(P, xb * kProjTok + t, hh, parts, ntiles, n, w0, base);
-                    for (int k = 0; k < n; ++k) {
-                        const long long row = static_cast<long long>(base) + static_cast<long long>(k) * step;
-                        prefetch_l2_bulk(rec_o + row * o_stride, static_cast<uint32_t>(dc * sizeof(R)));
-                        prefetch_l2(rec_ml + row * ml_stride);
-                    }
+        const int nxt = blockIdx.x + gridDim.x * blockIdx.y + prefetch_stride;
+        if (prefetch_stride > 0 && nxt < static_cast<int>(gridDim.x * gridDim.y)) {
+            const int xb = nxt % gridDim.x, hh = nxt / gridDim.x;
+            const int nt = min(kProjTok, P.B - xb * kProjTok);
+            for (int t = threadIdx.x; t < nt; t += blockDim.x) {
+                int n, w0, base;
+                proj::record_list(P, xb * kProjTok + t, hh, parts, ntiles, n, w0, base);
+                for (int k = 0; k < n; ++k) {
+                    const long long row = static_cast<long long>(base) + static_cast<long long>(k) * step;
+                    prefetch_l2_bulk(rec_o + row * o_stride, static_cast<uint32_t>(dc * sizeof(R)));
+                    prefetch_l2(rec_ml + row * ml_stride);
                 }
             }
         }
-        // ---- merge into the B operand (fp32 sums, rounded once to T).
-        // Job p = (token p % ntok, record split p / ntok) takes the records s, s + S, ... of the token,
-        // lane l holding the four float4 groups RecRow<R>::col(l, 0..3) of the d_c row. A warp carries two jobs
-        // at once and loads the (m, l) pair and the o row of two records of each in one round trip,
-        // folding them into a running log-sum-exp (max, row sum, rescaled o sum). With few tokens the
-        // records of a token are split over S jobs (32 jobs in all), whose partial sums are rescaled
-        // to the common max and added through shared memory.
-        const int U = dc / 4;                                  // float4 units per row, <= 128
-        int S = proj_red_rows(ntp) / ntok;
-        S = S < 1 ? 1 : S;
-        auto store_b = [&](int t, int c, float4 v) {   // columns c .. c + 3 of token t
-            const uint32_t dst = b_u32 + (c >> 6) * (ntp * 128) + t * 128 + ((((c & 63) >> 3) ^ (t & 7)) << 4) +
-                                 ((c & 7) >> 2) * 8;
-            st_shared_v2(dst, pack_pair<T>(v.x, v.y), pack_pair<T>(v.z, v.w));
-        };
-        const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        const int njobs = ntok * S;
-        for (int p0 = warp; p0 < njobs; p0 += 2 * kProjWarps) {
-            int tj[2], sj[2], nj[2], basej[2];
-            const uint32_t* vmask[2];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int p = p0 + j * kProjWarps;
-                const bool on = p < njobs;
-                tj[j] = on ? p % ntok : 0;
-                sj[j] = on ? p / ntok : 0;
-                nj[j] = on ? L->cnt[tj[j]] : 0;
-                basej[j] = L->base[tj[j]];
-                vmask[j] = L->valid[tj[j]];
-            }
-            float mrun[2] = {-INFINITY, -INFINITY}, lrun[2] = {0.f, 0.f};
-            float4 acc[2][4];
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-#pragma unroll
-                for (int u = 0; u < 4; ++u) acc[j][u] = zero4;
-            for (int i = 0;; i += 2) {
-                bool more = false;
-                long long rq[2][2];
-                bool vq[2][2];
-#pragma unroll
-                for (int j = 0; j < 2; ++j)
-#pragma unroll
-                    for (int q = 0; q < 2; ++q) {
-                        // record kk of the token: row base + kk * step; a missing record is never read
-                        const int kk = sj[j] + (i + q) * S;
-                        more |= kk < nj[j];
-                        rq[j][q] = static_cast<long long>(basej[j]) + static_cast<long long>(kk) * step;
-                        vq[j][q] = kk < nj[j] && ((vmask[j][kk >> 5] >> (kk & 31)) & 1u);
-                    }
-                if (!more) break;
-                float2 mlq[2][2];
-                float4 v[2][2][4];
-#pragma unroll
-                for (int j = 0; j < 2; ++j)
-#pragma unroll
-                    for (int q = 0; q < 2; ++q) {
-                        mlq[j][q] = vq[j][q] ? __ldg(reinterpret_cast<const float2*>(rec_ml + rq[j][q] * ml_stride))
-                                             : make_float2(-INFINITY, 0.f);
-                        RecRow<R>::load(rec_o + rq[j][q] * o_stride, lane, dc, vq[j][q], v[j][q]);
-                    }
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    float mq[2];
-#pragma unroll
-                    for (int q = 0; q < 2; ++q)   // an empty part (l = 0) contributes nothing
-                        mq[q] = mlq[j][q].y > 0.f ? mlq[j][q].x * mscale : -INFINITY;
-                    const float mnew = fmaxf(mrun[j], fmaxf(mq[0], mq[1]));
-                    if (mnew == -INFINITY) continue;   // nothing in this job yet
-                    const float sc = exp2f(mrun[j] - mnew);
-                    float w0 = exp2f(mq[0] - mnew), w1 = exp2f(mq[1] - mnew);
-                    mrun[j] = mnew;
-                    lrun[j] = fmaf(lrun[j], sc, fmaf(w0, mlq[j][0].y, w1 * mlq[j][1].y));
-                    if (RecRow<R>::kNormalised) {   // an fp16 record holds o / l: weigh it by its row sum
-                        w0 *= mlq[j][0].y;
-                        w1 *= mlq[j][1].y;
-                    }
-#pragma unroll
-                    for (int u4 = 0; u4 < 4; ++u4) {
-                        acc[j][u4].x = fmaf(acc[j][u4].x, sc, fmaf(w0, v[j][0][u4].x, w1 * v[j][1][u4].x));
-                        acc[j][u4].y = fmaf(acc[j][u4].y, sc, fmaf(w0, v[j][0][u4].y, w1 * v[j][1][u4].y));
-                        acc[j][u4].z = fmaf(acc[j][u4].z, sc, fmaf(w0, v[j][0][u4].z, w1 * v[j][1][u4].z));
-                        acc[j][u4].w = fmaf(acc[j][u4].w, sc, fmaf(w0, v[j][0][u4].w, w1 * v[j][1][u4].w));
-                    }
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                if (p0 + j * kProjWarps >= njobs) continue;
-                if (S == 1) {
-                    const float inv = lrun[j] > 0.f ? 1.f / lrun[j] : 0.f;
-#pragma unroll
-                    for (int u4 = 0; u4 < 4; ++u4) {
-                        const int c = RecRow<R>::col(lane, u4);
-                        if (c < dc)
-                            store_b(tj[j], c, make_float4(acc[j][u4].x * inv, acc[j][u4].y * inv,
-                                                          acc[j][u4].z * inv, acc[j][u4].w * inv));
-                    }
-                } else {
-                    const int row = sj[j] * ntok + tj[j];
-#pragma unroll
-                    for (int u4 = 0; u4 < 4; ++u4) {
-                        const int c = RecRow<R>::col(lane, u4);
-                        if (c < dc) reinterpret_cast<float4*>(red)[row * U + c / 4] = acc[j][u4];
-                    }
-                    if (lane == 0) L->split_ml[row] = make_float2(mrun[j], lrun[j]);
-                }
-            }
-        }
-        if (S > 1) {
-            __syncthreads();
-            // per token: the splits' common max and final weights 2^(m_s - M) / sum_s 2^(m_s - M) l_s
-            // (lane s of a warp takes split s; S <= 32)
-            for (int t = warp; t < ntok; t += kProjWarps) {
-                const float2 ml = lane < S ? L->split_ml[lane * ntok + t] : make_float2(-INFINITY, 0.f);
-                float M = ml.x;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-                const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);   // an empty split weighs 0
-                float l = w * ml.y;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-                if (lane < S) L->split_w[lane * ntok + t] = l > 0.f ? w / l : 0.f;
-            }
-            __syncthreads();
-            // weighted sum over the splits: four lanes per (token, unit), each taking every fourth
-            // split, then two shuffles (ntok * U * 4 is a multiple of 64: whole warps take part)
-            for (int i = threadIdx.x; i < ntok * U * 4; i += blockDim.x) {
-                const int q = i & 3, tu = i >> 2, u = tu % U, t = tu / U;
-                float4 a = zero4;
-                for (int sp = q; sp < S; sp += 4) {
-                    const float w = L->split_w[sp * ntok + t];
-                    const float4 v = reinterpret_cast<float4*>(red)[(sp * ntok + t) * U + u];
-                    a.x = fmaf(w, v.x, a.x); a.y = fmaf(w, v.y, a.y); a.z = fmaf(w, v.z, a.z); a.w = fmaf(w, v.w, a.w);
-                }
-#pragma unroll
-                for (int o = 1; o < 4; o <<= 1) {
-                    a.x += __shfl_xor_sync(0xffffffffu, a.x, o);
-                    a.y += __shfl_xor_sync(0xffffffffu, a.y, o);
-                    a.z += __shfl_xor_sync(0xffffffffu, a.z, o);
-                    a.w += __shfl_xor_sync(0xffffffffu, a.w, o);
-                }
-                if (q == 0) store_b(t, 4 * u, a);
-            }
-        }
-        // padding token rows are zero
-        for (int i = threadIdx.x; i < (ntp - ntok) * U; i += blockDim.x)
-            store_b(ntok + i / U, 4 * (i % U), make_float4(0.f, 0.f, 0.f, 0.f));
     }
+    proj::merge<T, R, kProjWarps>(P, L, red, b_u32, ntok, ntp, parts, ml_stride, o_stride, rec_ml, rec_o);
     const bool failed = parts == 0 && status0 != kStatusOk;
-    if (failed) {
-        // the decode kernel gave up on a wait: make the failure visible in the output
-        const float nan = __int_as_float(0x7fc00000);
-        for (int i = threadIdx.x; i < ntok * dv; i += blockDim.x)
-            out[(static_cast<long long>(b0 + i / dv) * P.H + h) * dv + i % dv] = nan;
-    }
     fence_proxy_async_smem();
     __syncthreads();
     bool issued = true;   // thread 0: the W_UV boxes landed (and, unless failed, the MMAs were issued)
@@ -704,49 +432,25 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
         issued = mbar_wait(a_full, 0, err, gcode(kSiteProjA));
         if (issued && !failed) {
             tc_fence_after();
-            const uint32_t idesc = idesc_f16(dv, ntp, GemmFmt<T>::v, false, false);
-            for (int k = 0; k < dc / 16; ++k) {
-                const uint64_t ad = smem_desc_sw128(a_u32 + (k >> 2) * (dv * 128) + (k & 3) * 32, 16, 1024);
-                const uint64_t bd = smem_desc_sw128(b_u32 + (k >> 2) * (ntp * 128) + (k & 3) * 32, 16, 1024);
-                mma_ss(tbase, ad, bd, idesc, k > 0 ? 1u : 0u);
-            }
+            proj::issue_mma<T>(tbase, a_u32, b_u32, dc, dv, ntp);
         }
         mma_commit(mma_done);
     }
     if (warp == 0 || (warp >= 4 && warp < 8)) {
         // thread 0's result reaches the epilogue warps through an AND over a named barrier of
         // warps 0 and 4-7 (no global status read)
-        issued = bar_red_and(1, 160, issued);
+        issued = proj::bar_and(1, 160, issued);
     }
-    if (warp >= 4 && warp < 8 && !failed) {
-        // warps 4-7: warp w reads TMEM lanes 32 (w - 4) .. + 31, i.e. output columns j < dv = 128
-        bool ok = mbar_wait(mma_done, 0, err, gcode(kSiteProjMma)) && issued;
+    if (warp >= 4 && warp < 8) {
+        bool ok = mbar_wait(mma_done, 0, err, gcode(kSiteProjMma)) && issued && !failed;
         ok = __all_sync(0xffffffffu, ok);
-        if (ok) {
-            tc_fence_after();
-            const int j = 32 * (warp - 4) + lane;
-            const uint32_t trow = tbase + (static_cast<uint32_t>(32 * (warp - 4)) << 16);
-            for (int c0 = 0; c0 < ntok; c0 += 16) {
-                uint32_t r[16];
-                tmem_ld16_sync(trow + c0, r);
-#pragma unroll
-                for (int q = 0; q < 16; ++q) {
-                    const int n = c0 + q;
-                    if (n < ntok) out[(static_cast<long long>(b0 + n) * P.H + h) * dv + j] = __uint_as_float(r[q]);
-                }
-            }
-        } else {
-            // a wait gave up (the status word holds where): the output shows it
-            const int j = 32 * (warp - 4) + lane;
-            for (int n = 0; n < ntok; ++n)
-                out[(static_cast<long long>(b0 + n) * P.H + h) * dv + j] = __int_as_float(0x7fc00000);
-        }
+        // a failed decode, or a wait that gave up (the status word holds where): the output shows it
+        proj::store_out(P, tbase, out, b0, ntok, h, ok);
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
-        // the MMAs (if any) completed: mma_done was waited on by warps 4-7, or nothing was issued
-        if (threadIdx.x == 0 && failed) mbar_wait(mma_done, 0, err, gcode(kSiteProjMma));
+        // the MMAs (if any) completed: mma_done was waited on by warps 4-7
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tbase, tmem_cols);
@@ -754,7 +458,7 @@ project_sm100_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePla
 }
 
 // ------------------------------------------------------------------------------------------
-// host side
+// launch helpers
 // ------------------------------------------------------------------------------------------
 namespace {
 uint32_t tmem_cols_for(int n) {
@@ -847,7 +551,7 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
     const int ntiles = parts ? 0 : total_tiles(P);
     const bool busy = parts || ntiles >= P.W;   // every worker owns a tile: every record in the range exists
     int n = 0, w0 = 0, base = 0;
-    if (t < B) proj_record_list(P, t, h, parts, ntiles, n, w0, base);
+    if (t < B) proj::record_list(P, t, h, parts, ntiles, n, w0, base);
     if (lists_early) pdl_wait();  // records and status come from the decode kernel
     const int status0 = *err;     // consumed after the merge
     if (t < B) {
@@ -866,7 +570,7 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
                 const long long row = static_cast<long long>(base) + static_cast<long long>(k) * step;
                 mlq[q] = in ? __ldg(reinterpret_cast<const float2*>(rec_ml + row * ml_stride))
                             : make_float2(-INFINITY, 0.f);
-                RecRow<R>::load(rec_o + row * o_stride, lane, dc, in, v[q]);
+                proj::RecRow<R>::load(rec_o + row * o_stride, lane, dc, in, v[q]);
             }
             float mq[kGemvRec];
             float mnew = mrun;
@@ -886,7 +590,7 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
             for (int q = 0; q < kGemvRec; ++q) {
                 float wq = exp2f(mq[q] - mnew);
                 lrun = fmaf(wq, mlq[q].y, lrun);
-                if (RecRow<R>::kNormalised) wq *= mlq[q].y;   // an fp16 record holds o / l: weigh it by its row sum
+                if (proj::RecRow<R>::kNormalised) wq *= mlq[q].y;   // an fp16 record holds o / l: weigh it by its row sum
 #pragma unroll
                 for (int u4 = 0; u4 < 4; ++u4) {
                     acc[u4].x = fmaf(wq, v[q][u4].x, acc[u4].x);
@@ -900,7 +604,7 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
         if (lane == 0) wml[warp] = make_float2(mrun, lrun);
 #pragma unroll
         for (int u4 = 0; u4 < 4; ++u4) {
-            const int c = RecRow<R>::col(lane, u4);
+            const int c = proj::RecRow<R>::col(lane, u4);
             if (c < dc) *reinterpret_cast<float4*>(red + warp * dc + c) = acc[u4];
         }
     }
@@ -1048,9 +752,7 @@ cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const 
         return e != cudaSuccess ? e : cudaGetLastError();
     }
     const int ntp = pad16(P.B < kProjTok ? P.B : kProjTok);
-    const int nk = P.dc / 64;
-    const size_t smem = 1024 + static_cast<size_t>(nk) * P.dv * 128 + static_cast<size_t>(nk) * ntp * 128 +
-                        sizeof(ProjLists) + static_cast<size_t>(proj_red_rows(ntp)) * P.dc * sizeof(float) + 64;
+    const size_t smem = 1024 + proj::unit_smem_bytes(P.dc, P.dv, ntp) + 64;
     cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(project_sm100_kernel<T, R>), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     dim3 grid(ceil_div(P.B, kProjTok), P.H);
