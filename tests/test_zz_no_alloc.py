@@ -113,12 +113,12 @@ def test_noalloc_near_its_scratch_limit():
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
-    """8192 heads need 64 query groups: more scratch than the static array holds (the query pack
-    alone is 64 x 128 rows of 576 16-bit elements, 9.4 MB). The call is refused on the host before
-    any launch. Every buffer still has the size the problem needs, so that a launch, were the call
-    ever accepted, would stay inside them."""
+    """3968 heads need 31 query groups, one more than the largest accepted problem (3840 heads,
+    test_noalloc_near_its_scratch_limit): with one split-KV worker the plan needs 8,666,624 bytes of the
+    8,388,608. The call is refused on the host before any launch. Every buffer still has the size the
+    problem needs, so that a launch, were the call ever accepted, would stay inside them."""
     lib = _lib.load()
-    H, S = 8192, 16
+    H, S = 3968, 16
     dev = torch.device("cuda")
     cfg = _lib.MlaConfig(0, 512, 128, 64, H, 128)
     kv = torch.zeros(S, 576, dtype=torch.bfloat16, device=dev)
