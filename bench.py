@@ -24,7 +24,7 @@ every timed step because the config-1 inputs fit in the 126 MB L2.
 
 Device-timed leg: each timed step is one replay of a CUDA graph captured from the
 public call (latent_attn.functional.mla_decode, or the KV-range decoder with its
-NCCL all-gather on several GPUs), so the events bracket the step's kernels rather
+NCCL exchange on several GPUs), so the events bracket the step's kernels rather
 than the host's time to enqueue them (--eager launches it directly). The roofline's
 decode-kernel time comes from a second loop of the same steps, each carrying the
 library's kernel timer. Graphs that hold NCCL calls are released before the process
@@ -38,7 +38,8 @@ reference's fp32 tables instead.
 Besides the headline workload, the same line carries the other BASELINE
 configurations measured in the same run ("workloads": step time, cache GB/s and
 the decode kernel's fraction of the HBM peak): on one GPU configs 2, 3 and 4; on
-several GPUs config 3 KV-range sharded with its NCCL all-gather and config 4
+several GPUs config 3 KV-range sharded with its NCCL exchange (an all-to-all of
+per-head partials, then an all-gather of the outputs) and config 4
 batch-sharded. Their inputs are drawn on the device with the same distributions.
 The CPU leg also times BASELINE config 0 (H=16, L=1024, fp32) on the host.
 """
@@ -124,7 +125,7 @@ def workload_spec(name):
                     desc="config 2: B=64 variable-length decode, L_b~U[1024,16384], H=128, bf16")
     if name == "cfg3":
         return dict(name=name, lens=[131072], sharding="kv-range",
-                    desc="config 3: B=1, L=131072, H=128, bf16, KV-range sharded + NCCL combine")
+                    desc="config 3: B=1, L=131072, H=128, bf16, KV-range sharded + NCCL exchange of partials")
     return dict(name=name, lens=[4096] * 256, sharding="batch",
                 desc="config 4: B=256, L=4096, H=128 (DeepSeek-V3 MLA dims), bf16")
 
@@ -290,7 +291,8 @@ def config_of(spec, world):
             "seq_len": max(spec["lens"]), "heads": 128, "kv_lora_rank": 512, "qk_rope_head_dim": 64,
             "parallelism": {"batch-replica": f"dp{world} (one sequence per GPU, no collective)",
                             "batch": f"batch-sharded over {world} GPU(s), LPT, no collective",
-                            "kv-range": f"KV-range over {world} GPU(s) + NCCL all-gather"}[spec["sharding"]],
+                            "kv-range": f"KV-range over {world} GPU(s) + NCCL all-to-all of head slices and "
+                                        "output all-gather"}[spec["sharding"]],
             "l2": "flushed before every timed step (256 MiB write outside the events)"}
 
 
