@@ -12,7 +12,9 @@ Workloads (seeded synthetic inputs with the BASELINE shapes; no dataset exists):
                   N GPUs run N independent sequences (batch-sharded, weak scaling).
   cfg2            B=64 sequences, L_b ~ U[1024, 16384], sharded by batch (LPT) over GPUs.
   cfg3            B=1, L=131072, KV-range sharded over GPUs; per-head partials
-                  (m, l, o_latent) are all-gathered with NCCL and merged.
+                  (m, l, o_latent) go to the rank owning the head (put kernels storing
+                  into the peers' memory over NVLink), which merges and projects them,
+                  and the outputs go back to every rank the same way.
   cfg4            B=256, L=4096 (DeepSeek-V3 shape), sharded by batch.
 
 A step = Q absorption (q_nope @ W_UK) + split-KV latent attention over the cache
@@ -24,11 +26,11 @@ every timed step because the config-1 inputs fit in the 126 MB L2.
 
 Device-timed leg: each timed step is one replay of a CUDA graph captured from the
 public call (latent_attn.functional.mla_decode, or the KV-range decoder with its
-NCCL exchange on several GPUs), so the events bracket the step's kernels rather
+peer-memory exchange on several GPUs), so the events bracket the step's kernels rather
 than the host's time to enqueue them (--eager launches it directly). The roofline's
 decode-kernel time comes from a second loop of the same steps, each carrying the
-library's kernel timer. Graphs that hold NCCL calls are released before the process
-group is destroyed.
+library's kernel timer. Graphs are released, and the exchange's peer buffers closed,
+before the process group is destroyed.
 The end-to-end leg calls the public API every step, with the host copies inside.
 
 RoPE: by default the step passes no cos/sin tables, so the kernels compute the
@@ -38,8 +40,9 @@ reference's fp32 tables instead.
 Besides the headline workload, the same line carries the other BASELINE
 configurations measured in the same run ("workloads": step time, cache GB/s and
 the decode kernel's fraction of the HBM peak): on one GPU configs 2, 3 and 4; on
-several GPUs config 3 KV-range sharded with its NCCL exchange (an all-to-all of
-per-head partials, then an all-gather of the outputs) and config 4
+several GPUs config 3 KV-range sharded with its exchange (an all-to-all of per-head
+partials, then an all-gather of the outputs, both as the library's own put / wait
+kernels storing into the peers' memory over NVLink) and config 4
 batch-sharded. Their inputs are drawn on the device with the same distributions.
 The CPU leg also times BASELINE config 0 (H=16, L=1024, fp32) on the host.
 """
@@ -125,7 +128,7 @@ def workload_spec(name):
                     desc="config 2: B=64 variable-length decode, L_b~U[1024,16384], H=128, bf16")
     if name == "cfg3":
         return dict(name=name, lens=[131072], sharding="kv-range",
-                    desc="config 3: B=1, L=131072, H=128, bf16, KV-range sharded + NCCL exchange of partials")
+                    desc="config 3: B=1, L=131072, H=128, bf16, KV-range sharded + exchange of per-head partials")
     return dict(name=name, lens=[4096] * 256, sharding="batch",
                 desc="config 4: B=256, L=4096, H=128 (DeepSeek-V3 MLA dims), bf16")
 
@@ -291,8 +294,8 @@ def config_of(spec, world):
             "seq_len": max(spec["lens"]), "heads": 128, "kv_lora_rank": 512, "qk_rope_head_dim": 64,
             "parallelism": {"batch-replica": f"dp{world} (one sequence per GPU, no collective)",
                             "batch": f"batch-sharded over {world} GPU(s), LPT, no collective",
-                            "kv-range": f"KV-range over {world} GPU(s) + NCCL all-to-all of head slices and "
-                                        "output all-gather"}[spec["sharding"]],
+                            "kv-range": f"KV-range over {world} GPU(s) + peer-memory (NVLink stores) all-to-all of "
+                                        "head slices and output all-gather"}[spec["sharding"]],
             "l2": "flushed before every timed step (256 MiB write outside the events)"}
 
 
@@ -394,7 +397,8 @@ def build_step(spec, world, rank, dev, cfg, rope, ws, host_inputs):
     if spec["sharding"] == "kv-range" and world > 1:
         sharded = KVRangeDecoder(cfg)
 
-        def step(q_n=q_nope, q_r=q_rope, o=out, t=None):
+        # the output lands in the exchange's own buffer (every rank's rows stored there by the peers)
+        def step(q_n=q_nope, q_r=q_rope, o=None, t=None):
             return sharded(kv, q_r, W_UV, cos, sin, pos_offset=lo, q_nope=q_n, W_UK=W_UK, out=o, workspace=ws,
                            timer=t)
     else:
@@ -402,7 +406,8 @@ def build_step(spec, world, rank, dev, cfg, rope, ws, host_inputs):
             return mla_decode(kv, q_r, W_UV, cos, sin, cfg, q_nope=q_n, W_UK=W_UK, seq_lens=seq, kv_offsets=offs,
                               max_seq_len=Lmax, seq_lens_host=my_lens if seq is not None else None, out=o,
                               workspace=ws, timer=t)
-    tensors = dict(kv=kv, q_nope=q_nope, q_rope=q_rope, W_UK=W_UK, W_UV=W_UV, out=out, inp=inp)
+    tensors = dict(kv=kv, q_nope=q_nope, q_rope=q_rope, W_UK=W_UK, W_UV=W_UV, out=out, inp=inp,
+                   close=sharded.close if spec["sharding"] == "kv-range" and world > 1 else None)
     return step, tensors, sum(my_lens) * CACHE_ROW_BYTES, B, my_lens
 
 
@@ -486,6 +491,8 @@ def run_leg(name, world, rank, dev, cfg, rope, ws, flush, barrier, steps, eager,
     barrier()
     dec = tm.decode_ms()
     tm.release()
+    if tensors["close"] is not None:
+        tensors["close"]()
     step_ms = sum(a.elapsed_time(b) for a, b in zip(ev0, ev1)) / steps
     dec_ms = statistics.mean(dec)
     frac_rank = nbytes / (dec_ms / 1e3) / 1e9 / peak
@@ -637,8 +644,10 @@ def main(argv=None):
     job_bytes = float(nbytes[0])
     value = job_bytes * args.steps / total_max / 1e6          # bytes / ms -> GB/s
     e2e_value = job_bytes * args.steps / e2e_max / 1e6
-    output_finite = bool(torch.isfinite(out).all())
-    del step, tens, inp, out
+    output_finite = bool(torch.isfinite(o).all())
+    if tens["close"] is not None:
+        tens["close"]()
+    del step, tens, inp, out, o
     torch.cuda.empty_cache()
 
     # ---- the other configurations, same run

@@ -241,6 +241,70 @@ MLA_API mla_status_t mla_combine_partials_packed(const mla_config_t* cfg, mla_dt
 MLA_API mla_status_t mla_linear(mla_dtype_t dtype, int M, int N, int K, const void* X, const void* W, float* Y,
                                 mla_stream_t stream);
 
+/* ---- Peer memory for the multi-GPU exchange (one process per GPU, GPUs of one node) ----
+ * The KV-range decode's two exchanges (per-head partials to the rank that merges those heads,
+ * then the merged outputs to every rank) can run as direct NVLink stores into the peers'
+ * buffers instead of NCCL collectives: no reference counterpart (the reference is single-GPU). */
+#define MLA_IPC_HANDLE_BYTES 64
+
+/* Allocates `bytes` of device memory on the current device that other processes can map:
+ * *ptr receives the local pointer and handle (MLA_IPC_HANDLE_BYTES bytes) the handle to pass
+ * to the peers (cudaIpcGetMemHandle). Free with mla_ipc_free. */
+MLA_API mla_status_t mla_ipc_alloc(size_t bytes, void** ptr, void* handle);
+MLA_API mla_status_t mla_ipc_free(void* ptr);
+/* Maps a peer's allocation from its handle (cudaIpcOpenMemHandle with lazy peer access);
+ * unmap with mla_ipc_close. */
+MLA_API mla_status_t mla_ipc_open(const void* handle, void** ptr);
+MLA_API mla_status_t mla_ipc_close(void* ptr);
+
+/* How a kernel that stores into other ranks' buffers tells them its data has landed. Receiver q
+ * has an int flag word per sender; this rank sets word `flag_index` of every receiver to
+ * *epoch + 1 once the kernel's stores bound for q are complete (system-scope release). The
+ * kernel's blocks count themselves per receiver in `counters` (world zeroed words of THIS rank's
+ * device memory, left zeroed); the block that completes a count releases the flag. flags and
+ * counters are DEVICE arrays (world pointers; world words); epoch is a device int of this rank. */
+typedef struct mla_peer_signal {
+    int* const* flags;
+    int flag_index;
+    const int* epoch;
+    unsigned int* counters;
+} mla_peer_signal_t;
+
+/* One kernel: for q < world, copies slice q of src to dst[q] and then signals receiver q. Slice
+ * q is `rows` rows of row_bytes; row i starts at src + q * src_stride + i * src_pitch and lands at
+ * dst[q] + dst_offset + i * dst_pitch (src_stride 0 sends the same slice to every rank: an
+ * all-gather; distinct slices make one rank's side of an all-to-all). Every size, pitch, stride,
+ * offset and pointer is a multiple of 16 bytes. `blocks` thread blocks share each slice. dst is
+ * a DEVICE array of `world` pointers (peer memory from mla_ipc_open, or local memory). */
+MLA_API mla_status_t mla_peer_put(const void* src, size_t rows, size_t row_bytes, size_t src_pitch, size_t src_stride,
+                                  void* const* dst, size_t dst_pitch, size_t dst_offset, int world, int blocks,
+                                  const mla_peer_signal_t* signal, mla_stream_t stream);
+/* mla_decode_partial_packed with its packed rows stored straight into the ranks that merge them:
+ * slice q (the B * H / world rows of heads [q H / world, (q + 1) H / world), ordered (token,
+ * head within the slice)) lands at dst[q] + dst_offset, and receiver q is signalled once it has
+ * (see mla_peer_signal_t). The export kernel itself does the stores (over NVLink for peers): one
+ * kernel replaces the export and the sender's half of an all-to-all. world divides num_heads;
+ * dst is a DEVICE array of world pointers; dst_offset a multiple of 16. */
+MLA_API mla_status_t mla_decode_partial_put(const mla_config_t* cfg, const mla_decode_args_t* args, int world,
+                                            void* const* dst, size_t dst_offset, const mla_peer_signal_t* signal,
+                                            void* workspace, size_t workspace_bytes, mla_stream_t stream);
+/* mla_combine_partials_packed with the (batch, heads, dv) fp32 output stored into every rank:
+ * token b's rows land at dst[q] + dst_offset + b * dst_pitch for every q < world, then every
+ * receiver is signalled. For batch <= 4 the merge kernel does the stores; larger batches are
+ * staged in scratch (batch * heads * dv floats of this rank) and sent by a put kernel. One call
+ * is this rank's half of the output all-gather. */
+MLA_API mla_status_t mla_combine_partials_put(const mla_config_t* cfg, mla_dtype_t dtype, int batch, int num_parts,
+                                              int heads, const float* packed, const void* W_UV_slice, int world,
+                                              void* const* dst, size_t dst_offset, size_t dst_pitch,
+                                              const mla_peer_signal_t* signal, float* scratch, mla_stream_t stream);
+/* Waits on the device (one small kernel, bounded: 2 s) until flags[i] >= *epoch + 1 for i < count,
+ * with system-scope acquire ordering, so the kernels after it on the stream see the data the
+ * peers stored before their flags; with advance != 0 it then increments *epoch (the last wait of
+ * an exchange step), so that a captured CUDA graph replays with a new value each time. A wait
+ * that gives up stores 1 to *status (a device int, or NULL) and leaves *epoch unchanged. */
+MLA_API mla_status_t mla_peer_wait(const int* flags, int count, int* epoch, int advance, int* status,
+                                   mla_stream_t stream);
+
 /* Device-side cache append, one new row per sequence: for each b, the row of position
  * p = seq_lens[b] receives [c_t[b] (d_c) | k_rope[b] (d_R)] (k_rope unrotated, as the cache
  * stores it) and seq_lens[b] advances by one. The row is (kv_offsets ? kv_offsets[b] :

@@ -15,6 +15,7 @@
 #include <cfloat>
 
 #include "mla_internal.cuh"
+#include "peer.cuh"
 
 namespace mla {
 
@@ -179,69 +180,58 @@ __device__ void project_rows(int h, int b0, int ntok, int H, int dc, int dv, con
     }
 }
 
-// Row of (b, h) in the partial-set export: (B, H, .) rows of part_ml (2 floats) and part_o (d_c
-// floats), or, with packed_slices > 0, one packed row of d_c + 4 floats [m, l, 0, 0, o] at
-// part_o, rows ordered (head slice q, b, head within the slice) for packed_slices equal slices.
-struct PartOut {
-    float* ml;
-    float* o;
-    int slices;  // 0: separate arrays
-    __device__ long long row(int b, int h, int B, int H) const {
-        if (!slices) return static_cast<long long>(b) * H + h;
-        const int hs = H / slices;
-        return (static_cast<long long>(h / hs) * B + b) * hs + h % hs;
-    }
-    __device__ float* ml_at(long long r, int dc) const { return slices ? o + r * (dc + 4) : ml + r * 2; }
-    __device__ float* o_at(long long r, int dc) const { return slices ? o + r * (dc + 4) + 4 : o + r * dc; }
-};
-
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
 combine_kernel(DecodePlan P, const float* __restrict__ rec_ml, const T* __restrict__ rec_o,
-               const T* __restrict__ W_UV, float* __restrict__ out, PartOut part) {
+               const T* __restrict__ W_UV, float* __restrict__ out, PartOut part, PeerSig sig) {
     extern __shared__ float o_s[];  // kTok * dc
     __shared__ MergeList ml;
     const int h = blockIdx.x, b0 = blockIdx.y * kTok;
     const int ntok = (P.B - b0) < kTok ? (P.B - b0) : kTok;
     const int warp = threadIdx.x >> 5;
+    const bool partial = out == nullptr;
     if (P.status && *reinterpret_cast<volatile int*>(P.status) != kStatusOk) {
         // the decode kernel gave up on a wait: make the failure visible in the output
         const float nan = __int_as_float(0x7fc00000);
         for (int i = threadIdx.x; i < ntok * P.dv; i += kThreads)
             if (out) out[(static_cast<long long>(b0 + i / P.dv) * P.H + h) * P.dv + i % P.dv] = nan;
-        if (!out && static_cast<int>(threadIdx.x) < ntok)
-            part.ml_at(part.row(b0 + threadIdx.x, h, P.B, P.H), P.dc)[1] = nan;
-        return;
-    }
-    const bool partial = out == nullptr;
-    if (warp < ntok) build_merge_list(P, b0 + warp, h, rec_ml, ml, warp, !partial, RecNorm<T>::value);
-    __syncthreads();
-    // merge: thread -> (token, column)
-    for (int i = threadIdx.x; i < ntok * P.dc; i += kThreads) {
-        const int t = i / P.dc, c = i % P.dc;
-        const int r = ml.row[t];
-        float a = 0.f;
-        for (int k = 0; k < ml.count[t]; ++k) {
-            const int rec = ml.rec[t][k];
-            if (rec >= 0)
-                a = fmaf(ml.wgt[t][k], ElemTraits<T>::to_f(rec_o[(static_cast<long long>(rec) * kGroupRows + r) * P.dc + c]),
-                         a);
+        if (partial && static_cast<int>(threadIdx.x) < ntok)
+            part.ml_at(b0 + threadIdx.x, h, P.B, P.H, P.dc)[1] = nan;
+    } else {
+        if (warp < ntok) build_merge_list(P, b0 + warp, h, rec_ml, ml, warp, !partial, RecNorm<T>::value);
+        __syncthreads();
+        // merge: thread -> (token, column)
+        for (int i = threadIdx.x; i < ntok * P.dc; i += kThreads) {
+            const int t = i / P.dc, c = i % P.dc;
+            const int r = ml.row[t];
+            float a = 0.f;
+            for (int k = 0; k < ml.count[t]; ++k) {
+                const int rec = ml.rec[t][k];
+                if (rec >= 0)
+                    a = fmaf(ml.wgt[t][k],
+                             ElemTraits<T>::to_f(rec_o[(static_cast<long long>(rec) * kGroupRows + r) * P.dc + c]), a);
+            }
+            if (partial) part.o_at(b0 + t, h, P.B, P.H, P.dc)[c] = a;
+            else o_s[t * P.dc + c] = a;
         }
-        if (partial) part.o_at(part.row(b0 + t, h, P.B, P.H), P.dc)[c] = a;
-        else o_s[t * P.dc + c] = a;
-    }
-    if (partial) {
-        if (static_cast<int>(threadIdx.x) < ntok) {
-            const int t = threadIdx.x;
-            float* pm = part.ml_at(part.row(b0 + t, h, P.B, P.H), P.dc);
-            pm[0] = ml.l[t] > 0.f ? ml.m[t] * kLn2 : -INFINITY;  // natural-log units for the caller
-            pm[1] = ml.l[t];
-            if (part.slices) pm[2] = pm[3] = 0.f;
+        if (partial) {
+            if (static_cast<int>(threadIdx.x) < ntok) {
+                const int t = threadIdx.x;
+                float* pm = part.ml_at(b0 + t, h, P.B, P.H, P.dc);
+                pm[0] = ml.l[t] > 0.f ? ml.m[t] * kLn2 : -INFINITY;  // natural-log units for the caller
+                pm[1] = ml.l[t];
+                if (part.slices) pm[2] = pm[3] = 0.f;
+            }
+        } else {
+            __syncthreads();
+            project_rows<T>(h, b0, ntok, P.H, P.dc, P.dv, o_s, W_UV, out);
         }
-        return;
     }
-    __syncthreads();
-    project_rows<T>(h, b0, ntok, P.H, P.dc, P.dv, o_s, W_UV, out);
+    // every block of head slice q (hs heads x gridDim.y token blocks) stores into q's receiver
+    if (part.to_peers()) {
+        const int hs = P.H / part.slices;
+        peer_block_done(sig, h / hs, static_cast<unsigned int>(hs) * gridDim.y);
+    }
 }
 
 template <typename T>
@@ -291,15 +281,14 @@ combine_parts_kernel(int B, int H, int dc, int dv, int parts, const float* __res
 
 template <typename T>
 cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const T* rec_o, const T* W_UV,
-                           float* out, float* part_ml, float* part_o, int packed_slices, cudaStream_t s) {
+                           float* out, const PartOut& part, const PeerSig& sig, cudaStream_t s) {
     if (P.W > kMaxRec) return cudaErrorInvalidValue;
     const size_t smem = static_cast<size_t>(kTok) * P.dc * sizeof(float);
     cudaError_t e =
         ensure_dynamic_smem(reinterpret_cast<const void*>(combine_kernel<T>), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     dim3 grid(P.H, ceil_div(P.B, kTok));
-    PartOut part{part_ml, part_o, packed_slices};
-    combine_kernel<T><<<grid, kThreads, smem, s>>>(P, rec_ml, rec_o, W_UV, out, part);
+    combine_kernel<T><<<grid, kThreads, smem, s>>>(P, rec_ml, rec_o, W_UV, out, part, sig);
     count_launches(1);
     return cudaGetLastError();
 }
@@ -322,7 +311,7 @@ cudaError_t launch_combine_parts(int B, int H, int dc, int dv, int parts, const 
 
 #define MLA_INST(T)                                                                                   \
     template cudaError_t launch_combine<T>(const DecodePlan&, const float*, const T*, const T*,      \
-                                           float*, float*, float*, int, cudaStream_t);               \
+                                           float*, const PartOut&, const PeerSig&, cudaStream_t);    \
     template cudaError_t launch_combine_parts<T>(int, int, int, int, int, const float*, const float*, \
                                                  int, int, const T*, float*, cudaStream_t);
 MLA_INST(__half)

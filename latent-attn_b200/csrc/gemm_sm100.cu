@@ -31,6 +31,7 @@
 // The projection kernels launch their W loads by TMA before waiting on the previous kernel
 // (programmatic dependent launch), so weight streaming overlaps its tail.
 // Every wait is bounded; on timeout the status word records it.
+#include <algorithm>
 #include <cfloat>
 #include <cstdlib>
 
@@ -38,6 +39,7 @@
 #include "sm100_ptx.cuh"
 #include "tma_host.cuh"
 #include "proj_unit.cuh"
+#include "peer.cuh"
 
 namespace mla {
 using namespace sm100;
@@ -79,6 +81,8 @@ constexpr int kProjWarps = 16;     // projection CTA: 16 warps merge, warp 0 iss
 __host__ __device__ inline size_t absorb_smem_bytes(int dn, int dc) {
     return static_cast<size_t>(dc / 64) * dn * 128 + 2 * static_cast<size_t>(dn / 64) * kAbsorbTok * 128 + 32;
 }
+
+constexpr float kLn2 = 0.6931471805599453f;
 
 enum : int { kSiteAbsorbA = 12, kSiteAbsorbMma = 13, kSiteProjA = 14, kSiteProjMma = 15 };
 __device__ __forceinline__ int gcode(int site) { return kStatusTimeout | (site << 8); }
@@ -511,39 +515,22 @@ __host__ __device__ inline size_t gemv_smem_bytes(int dc, int dv) {
            16;                                                    // mbarrier
 }
 
-template <typename T, typename R>
-__global__ void __launch_bounds__(32 * kGemvWarps, 1)
-project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
-                    const R* __restrict__ rec_o, float* __restrict__ out, int parts, int ml_stride, int o_stride) {
-    extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    const int dc = P.dc, dv = P.dv, B = P.B;   // dv == 128, dc % 64 == 0, dc <= 512, B <= kGemvMaxTok
-    const int nk = dc / 64;
-    unsigned char* wsm = smem;                                                    // nk x (dv rows x 128 B)
-    float* red = reinterpret_cast<float*>(smem + nk * dv * 128);                  // [warp][dc]
-    float2* wml = reinterpret_cast<float2*>(red + kGemvWarps * dc);               // [warp]
-    float* olat = reinterpret_cast<float*>(wml + kGemvWarps);                     // [token][dc]
-    float* qsum = olat + kGemvMaxTok * dc;                                        // [quarter][token][dv]
-    uint64_t* bar = reinterpret_cast<uint64_t*>(qsum + 4 * kGemvMaxTok * dv);
-    const uint32_t w_full = smem_u32(bar);
-
+// Step 1 of the GEMV merge, shared by the projection and the partial export: warp w takes token
+// t = w / wpt and records k = s, s + wpt, ... (s = w % wpt) of head h, and leaves its running
+// (max in log2 units, row sum) in wml[w] and its unnormalised latent sum at that max in red[w].
+// With uniform lengths (or partial sets) the record list is arithmetic on the plan and is built
+// before the wait on the previous kernel; with variable lengths it reads the tile prefix.
+// Returns the decode status word as read after that wait.
+template <typename R>
+__device__ __forceinline__ int gemv_merge(const DecodePlan& P, const float* __restrict__ rec_ml,
+                                          const R* __restrict__ rec_o, int parts, int ml_stride, int o_stride, int h,
+                                          float* red, float2* wml) {
+    const int dc = P.dc, B = P.B;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.x;
     volatile int* err = P.status;
-
-    if (threadIdx.x == 0) {
-        mbar_init(w_full, 1);
-        fence_mbar_init();
-        tma_prefetch_desc(&tmap_w);
-        mbar_arrive_expect_tx(w_full, static_cast<uint32_t>(nk * dv * 128));
-        for (int j = 0; j < nk; ++j) tma_load_2d(smem_u32(wsm) + j * dv * 128, &tmap_w, w_full, 64 * j, h * dv);
-    }
     const int step = parts ? B * P.H : kGroupRows;
     const float mscale = parts ? 1.4426950408889634f : 1.f;   // m in log2 units
 
-    // ---- 1. merge: warp w takes token t = w / wpt and records k = s, s + wpt, ... (s = w % wpt).
-    // With uniform lengths (or partial sets) the record list is arithmetic on the plan and is built
-    // before the wait on the decode kernel; with variable lengths it reads the tile prefix.
     const int wpt = kGemvWarps / B;
     const int t = warp / wpt, s = warp % wpt;
     const bool lists_early = parts > 0 || P.uniform_len > 0;
@@ -608,6 +595,39 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
             if (c < dc) *reinterpret_cast<float4*>(red + warp * dc + c) = acc[u4];
         }
     }
+    return status0;
+}
+
+template <typename T, typename R>
+__global__ void __launch_bounds__(32 * kGemvWarps, 1)
+project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
+                    const R* __restrict__ rec_o, float* __restrict__ out, int parts, int ml_stride, int o_stride,
+                    const PeerRows rows) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int dc = P.dc, dv = P.dv, B = P.B;   // dv == 128, dc % 64 == 0, dc <= 512, B <= kGemvMaxTok
+    const int nk = dc / 64;
+    unsigned char* wsm = smem;                                                    // nk x (dv rows x 128 B)
+    float* red = reinterpret_cast<float*>(smem + nk * dv * 128);                  // [warp][dc]
+    float2* wml = reinterpret_cast<float2*>(red + kGemvWarps * dc);               // [warp]
+    float* olat = reinterpret_cast<float*>(wml + kGemvWarps);                     // [token][dc]
+    float* qsum = olat + kGemvMaxTok * dc;                                        // [quarter][token][dv]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(qsum + 4 * kGemvMaxTok * dv);
+    const uint32_t w_full = smem_u32(bar);
+
+    const int h = blockIdx.x;
+    const int wpt = kGemvWarps / B;
+    volatile int* err = P.status;
+
+    if (threadIdx.x == 0) {
+        mbar_init(w_full, 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tmap_w);
+        mbar_arrive_expect_tx(w_full, static_cast<uint32_t>(nk * dv * 128));
+        for (int j = 0; j < nk; ++j) tma_load_2d(smem_u32(wsm) + j * dv * 128, &tmap_w, w_full, 64 * j, h * dv);
+    }
+    // ---- 1. merge
+    const int status0 = gemv_merge<R>(P, rec_ml, rec_o, parts, ml_stride, o_stride, h, red, wml);
     __syncthreads();
     // ---- 2. per token: the warps' partials at the common max, summed in warp order
     for (int i = threadIdx.x; i < B * dc; i += blockDim.x) {
@@ -672,10 +692,64 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
         if (!failed)
             y = ((qsum[(0 * kGemvMaxTok + tt) * dv + j] + qsum[(1 * kGemvMaxTok + tt) * dv + j]) +
                  qsum[(2 * kGemvMaxTok + tt) * dv + j]) + qsum[(3 * kGemvMaxTok + tt) * dv + j];
-        out[(static_cast<long long>(tt) * P.H + h) * dv + j] = y;
+        if (rows.world == 0) {
+            out[(static_cast<long long>(tt) * P.H + h) * dv + j] = y;
+        } else {
+            // every rank's copy of the row (over NVLink for the peers)
+            for (int q = 0; q < rows.world; ++q)
+                reinterpret_cast<float*>(static_cast<unsigned char*>(rows.dst[q]) + rows.offset + tt * rows.pitch)
+                    [h * dv + j] = y;
+        }
     }
+    if (rows.world > 0) peer_block_done_all(rows.sig, rows.world, gridDim.x);
     // shared memory is not released under a TMA write: if the wait gave up, wait (bounded) again
     if (threadIdx.x == 0 && !ok) mbar_wait_impl<false, false>(w_full, 0, err, gcode(kSiteProjA), 100000000ull);
+}
+
+// Partial export by the GEMV merge (B <= kGemvMaxTok): block h merges the decode's records of
+// head h for every token and writes [m (natural log), l, 0, 0, o] with o the latent sum at the
+// merged max, unnormalised (PartOut gives the place); a failed decode writes NaN into m and l.
+// With part.peer the rows go to their slice's receiver, which is signalled by the last of the
+// slice's H / slices blocks.
+template <typename T>
+__global__ void __launch_bounds__(32 * kGemvWarps, 1)
+export_gemv_kernel(const DecodePlan P, const float* __restrict__ rec_ml, const T* __restrict__ rec_o,
+                   const PartOut part, const PeerSig sig) {
+    extern __shared__ __align__(16) unsigned char smem_e[];
+    const int dc = P.dc, B = P.B;
+    float* red = reinterpret_cast<float*>(smem_e);                      // [warp][dc]
+    float2* wml = reinterpret_cast<float2*>(red + kGemvWarps * dc);     // [warp]
+    const int h = blockIdx.x;
+    const int wpt = kGemvWarps / B;
+    const int status0 = gemv_merge<T>(P, rec_ml, rec_o, 0, 2, dc, h, red, wml);
+    __syncthreads();
+    const bool failed = status0 != kStatusOk;
+    for (int i = threadIdx.x; i < B * (dc + 4); i += blockDim.x) {
+        const int tt = i / (dc + 4), c = i % (dc + 4) - 4;
+        float M = -INFINITY;
+        for (int w = tt * wpt; w < (tt + 1) * wpt; ++w) M = fmaxf(M, wml[w].x);
+        float L = 0.f, o = 0.f;
+        if (M != -INFINITY) {
+            for (int w = tt * wpt; w < (tt + 1) * wpt; ++w) {
+                const float a = wml[w].x == -INFINITY ? 0.f : exp2f(wml[w].x - M);
+                L = fmaf(a, wml[w].y, L);
+                if (c >= 0) o = fmaf(a, red[w * dc + c], o);
+            }
+        }
+        if (c >= 0) {
+            part.o_at(tt, h, B, P.H, dc)[c] = o;
+        } else if (c == -4 || c == -3) {
+            const float nan = __int_as_float(0x7fc00000);
+            const float v = c == -4 ? (L > 0.f ? M * kLn2 : -INFINITY) : L;
+            part.ml_at(tt, h, B, P.H, dc)[c + 4] = failed ? nan : v;
+        } else if (part.slices) {
+            part.ml_at(tt, h, B, P.H, dc)[c + 4] = 0.f;
+        }
+    }
+    if (part.to_peers()) {
+        const int hs = P.H / part.slices;
+        peer_block_done(sig, h / hs, static_cast<unsigned int>(hs));
+    }
 }
 
 bool absorb_sm100_supported(const DecodePlan& P) {
@@ -737,7 +811,8 @@ cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const 
 
 template <typename T, typename R>
 cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const R* rec_o, const T* W_UV,
-                                float* out, bool pdl, int parts, int ml_stride, int o_stride, cudaStream_t s) {
+                                float* out, bool pdl, int parts, int ml_stride, int o_stride, const PeerRows& rows,
+                                cudaStream_t s) {
     CUtensorMap tmap;
     if (!make_tmap_2d_16b(&tmap, W_UV, static_cast<uint64_t>(P.H) * P.dv, static_cast<uint64_t>(P.dc),
                           static_cast<uint64_t>(P.dc), static_cast<uint32_t>(P.dv), 64))
@@ -747,7 +822,7 @@ cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const 
         cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(project_gemv_kernel<T, R>), static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         e = launch_ex(project_gemv_kernel<T, R>, dim3(P.H), dim3(32 * kGemvWarps), smem, s, pdl, tmap, P, rec_ml, rec_o,
-                      out, parts, ml_stride, o_stride);
+                      out, parts, ml_stride, o_stride, rows);
         count_launches(1);
         return e != cudaSuccess ? e : cudaGetLastError();
     }
@@ -759,14 +834,20 @@ cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const 
     e = launch_ex(project_sm100_kernel<T, R>, grid, dim3(32 * kProjWarps), smem, s, pdl, tmap, P, rec_ml, rec_o, out, ntp,
                   tmem_cols_for(ntp), parts, ml_stride, o_stride, sm_count());
     count_launches(1);
-    return e != cudaSuccess ? e : cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess || rows.world == 0) return e;
+    // the tensor-core kernel stages the rows in `out`; a put kernel sends them to every rank
+    const size_t row_bytes = static_cast<size_t>(P.H) * P.dv * sizeof(float);
+    const int blocks = static_cast<int>(std::min<size_t>(32, (static_cast<size_t>(P.B) * row_bytes + 16383) / 16384));
+    return launch_peer_put(out, P.B, row_bytes, row_bytes, 0, rows.dst, rows.pitch, rows.offset, rows.world, blocks,
+                           rows.sig, s);
 }
 
 template <typename T>
 cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const T* rec_o, const T* W_UV,
                                  float* out, bool pdl, cudaStream_t s) {
     if (!project_sm100_supported(P)) return cudaErrorInvalidValue;
-    return launch_project_impl<T, T>(P, rec_ml, rec_o, W_UV, out, pdl, 0, 2, P.dc, s);
+    return launch_project_impl<T, T>(P, rec_ml, rec_o, W_UV, out, pdl, 0, 2, P.dc, PeerRows{}, s);
 }
 
 // Status word of the partial-set merge: that path has no decode status to check, but the
@@ -780,7 +861,7 @@ bool project_parts_sm100_supported(int H, int dc, int dv, int parts) {
 template <typename T>
 cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, const float* part_ml,
                                        const float* part_o, int ml_stride, int o_stride, const T* W_UV, float* out,
-                                       cudaStream_t s) {
+                                       const PeerRows& rows, cudaStream_t s) {
     if (!project_parts_sm100_supported(H, dc, dv, parts)) return cudaErrorInvalidValue;
     static std::mutex mu;
     static std::vector<int*> status_addr;  // per device
@@ -806,7 +887,23 @@ cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, 
     P.B = B;
     P.head_blocks = ceil_div(H, kGroupRows);
     P.status = status;
-    return launch_project_impl<T, float>(P, part_ml, part_o, W_UV, out, false, parts, ml_stride, o_stride, s);
+    return launch_project_impl<T, float>(P, part_ml, part_o, W_UV, out, false, parts, ml_stride, o_stride, rows, s);
+}
+
+bool export_gemv_supported(const DecodePlan& P) {
+    return P.B >= 1 && P.B <= gemv_max_tokens() && P.dc % 64 == 0 && P.dc <= 512;
+}
+
+template <typename T>
+cudaError_t launch_export_gemv(const DecodePlan& P, const float* rec_ml, const T* rec_o, const PartOut& part,
+                               const PeerSig& sig, bool pdl, cudaStream_t s) {
+    if (!export_gemv_supported(P)) return cudaErrorInvalidValue;
+    const size_t smem = static_cast<size_t>(kGemvWarps) * P.dc * sizeof(float) + kGemvWarps * sizeof(float2);
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(export_gemv_kernel<T>), static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    e = launch_ex(export_gemv_kernel<T>, dim3(P.H), dim3(32 * kGemvWarps), smem, s, pdl, P, rec_ml, rec_o, part, sig);
+    count_launches(1);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 #define MLA_INST(T)                                                                                              \
@@ -815,8 +912,9 @@ cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, 
     template cudaError_t launch_project_sm100<T>(const DecodePlan&, const float*, const T*, const T*, float*,       \
                                                  bool, cudaStream_t);                                             \
     template cudaError_t launch_project_parts_sm100<T>(int, int, int, int, int, const float*, const float*, int, int, \
-                                                       const T*, \
-                                                       float*, cudaStream_t);
+                                                       const T*, float*, const PeerRows&, cudaStream_t);           \
+    template cudaError_t launch_export_gemv<T>(const DecodePlan&, const float*, const T*, const PartOut&,         \
+                                               const PeerSig&, bool, cudaStream_t);
 MLA_INST(__half)
 MLA_INST(__nv_bfloat16)
 #undef MLA_INST

@@ -6,6 +6,7 @@
 // errors those the torch binding rejects (csrc/bindings.cpp:28-40, 146-152,
 // 208-221); here they become status codes with a thread-local message instead of
 // exceptions, and nothing ever exits, aborts or synchronises the host.
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -18,6 +19,7 @@
 
 #include "latent_attn_b200/mla.h"
 #include "mla_internal.cuh"
+#include "peer.cuh"
 
 struct mla_timer_st {
     cudaEvent_t begin = nullptr, end = nullptr;
@@ -284,7 +286,7 @@ cudaError_t timer_record(cudaEvent_t ev, cudaStream_t s) {
 
 template <typename T>
 mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned char* ws, float* out,
-                        float* part_ml, float* part_o, int packed_slices, cudaStream_t s) {
+                        const mla::PartOut& part, const mla::PeerSig& sig, cudaStream_t s) {
     mla::DecodePlan d = pl.dp;
     int* prefix = reinterpret_cast<int*>(ws + pl.off_prefix);
     d.tile_prefix = d.uniform_len > 0 ? nullptr : prefix;
@@ -327,16 +329,17 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
     }
     if (out && pl.use_gemm_project)
         e = mla::launch_project_sm100<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, true, s);
+    else if (!out && pl.use_gemm_project && mla::export_gemv_supported(d))
+        e = mla::launch_export_gemv<T>(d, rec_ml, rec_o, part, sig, true, s);
     else
-        e = mla::launch_combine<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, part_ml, part_o,
-                                   packed_slices, s);
+        e = mla::launch_combine<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, part, sig, s);
     if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
     return MLA_OK;
 }
 
 mla_status_t decode_impl(const mla_config_t* cfg, const mla_decode_args_t* a, void* workspace,
-                         size_t ws_bytes, float* out, float* part_ml, float* part_o, cudaStream_t s,
-                         int max_workers = 0, int packed_slices = 0) {
+                         size_t ws_bytes, float* out, const mla::PartOut& part, cudaStream_t s,
+                         int max_workers = 0, const mla::PeerSig& sig = mla::PeerSig{}) {
     Plan pl;
     mla_status_t st = make_plan(cfg, a, &pl, max_workers);
     if (st != MLA_OK) return st;
@@ -346,9 +349,8 @@ mla_status_t decode_impl(const mla_config_t* cfg, const mla_decode_args_t* a, vo
     if (ws_bytes < pl.total)
         return fail(MLA_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", ws_bytes, pl.total);
     unsigned char* ws = static_cast<unsigned char*>(workspace);
-    if (a->dtype == MLA_DTYPE_BF16)
-        return run_decode<__nv_bfloat16>(pl, a, ws, out, part_ml, part_o, packed_slices, s);
-    return run_decode<__half>(pl, a, ws, out, part_ml, part_o, packed_slices, s);
+    if (a->dtype == MLA_DTYPE_BF16) return run_decode<__nv_bfloat16>(pl, a, ws, out, part, sig, s);
+    return run_decode<__half>(pl, a, ws, out, part, sig, s);
 }
 
 // Scratch for the reference-shaped launchers, whose signatures carry no workspace.
@@ -359,7 +361,7 @@ mla_status_t decode_with_pool(const mla_config_t* cfg, const mla_decode_args_t* 
     void* ws = nullptr;
     cudaError_t e = cudaMallocAsync(&ws, pl.total, s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(workspace)");
-    st = decode_impl(cfg, a, ws, pl.total, a->output, nullptr, nullptr, s);
+    st = decode_impl(cfg, a, ws, pl.total, a->output, mla::PartOut{}, s);
     e = cudaFreeAsync(ws, s);
     if (st == MLA_OK && e != cudaSuccess) return cuda_fail(e, "cudaFreeAsync(workspace)");
     return st;
@@ -396,10 +398,12 @@ mla_status_t noalloc_scratch(void** out) {
 }
 
 // Merge `num_parts` partial sets of (B, heads) rows and project with W_UV (heads * dv, d_c):
-// m, l at part_ml + row * ml_stride, o at part_o + row * o_stride.
+// m, l at part_ml + row * ml_stride, o at part_o + row * o_stride. With rows.world > 0 the
+// output also goes to every rank (the GEMV kernel stores it itself; otherwise `output` stages it
+// for a put kernel).
 mla_status_t combine_impl(const mla_config_t* cfg, mla_dtype_t dtype, int batch, int num_parts, int heads,
                           const float* part_ml, const float* part_o, int ml_stride, int o_stride,
-                          const void* W_UV, float* output, cudaStream_t s) {
+                          const void* W_UV, float* output, cudaStream_t s, const mla::PeerRows& rows = mla::PeerRows{}) {
     mla_status_t st = validate_cfg(cfg);
     if (st != MLA_OK) return st;
     if (batch <= 0 || num_parts <= 0 || heads <= 0)
@@ -416,20 +420,40 @@ mla_status_t combine_impl(const mla_config_t* cfg, mla_dtype_t dtype, int batch,
     cudaError_t e;
     if (gemm && dtype == MLA_DTYPE_BF16)
         e = mla::launch_project_parts_sm100<__nv_bfloat16>(batch, heads, dc, dv, num_parts, part_ml, part_o, ml_stride,
-                                                          o_stride, static_cast<const __nv_bfloat16*>(W_UV), output, s);
+                                                          o_stride, static_cast<const __nv_bfloat16*>(W_UV), output,
+                                                          rows, s);
     else if (gemm)
         e = mla::launch_project_parts_sm100<__half>(batch, heads, dc, dv, num_parts, part_ml, part_o, ml_stride, o_stride,
-                                                   static_cast<const __half*>(W_UV), output, s);
-    else if (dtype == MLA_DTYPE_BF16)
-        e = mla::launch_combine_parts<__nv_bfloat16>(batch, heads, dc, dv, num_parts, part_ml, part_o, ml_stride,
-                                                     o_stride, static_cast<const __nv_bfloat16*>(W_UV), output, s);
-    else
-        e = mla::launch_combine_parts<__half>(batch, heads, dc, dv, num_parts, part_ml, part_o, ml_stride, o_stride,
-                                              static_cast<const __half*>(W_UV), output, s);
+                                                   static_cast<const __half*>(W_UV), output, rows, s);
+    else {
+        if (dtype == MLA_DTYPE_BF16)
+            e = mla::launch_combine_parts<__nv_bfloat16>(batch, heads, dc, dv, num_parts, part_ml, part_o, ml_stride,
+                                                         o_stride, static_cast<const __nv_bfloat16*>(W_UV), output, s);
+        else
+            e = mla::launch_combine_parts<__half>(batch, heads, dc, dv, num_parts, part_ml, part_o, ml_stride, o_stride,
+                                                  static_cast<const __half*>(W_UV), output, s);
+        if (e == cudaSuccess && rows.world > 0) {
+            const size_t row_bytes = static_cast<size_t>(heads) * dv * sizeof(float);
+            const int blocks = static_cast<int>(std::min<size_t>(32, (batch * row_bytes + 16383) / 16384));
+            e = mla::launch_peer_put(output, batch, row_bytes, row_bytes, 0, rows.dst, rows.pitch, rows.offset,
+                                     rows.world, blocks, rows.sig, s);
+        }
+    }
     if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
     return MLA_OK;
 }
 
+}  // namespace
+
+namespace {
+// The signal description of a kernel that stores into other ranks' buffers.
+mla_status_t peer_sig(const mla_peer_signal_t* in, mla::PeerSig* out) {
+    if (!in || !in->flags || !in->epoch || !in->counters)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "peer signal: flags, epoch and counters must be non-null");
+    if (in->flag_index < 0) return fail(MLA_ERR_INVALID_ARGUMENT, "peer signal: flag_index must be >= 0");
+    *out = mla::PeerSig{in->flags, in->flag_index, in->epoch, in->counters};
+    return MLA_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -449,7 +473,7 @@ mla_status_t mla_decode(const mla_config_t* cfg, const mla_decode_args_t* a, voi
                         size_t workspace_bytes, mla_stream_t stream) {
     if (!a) return fail(MLA_ERR_INVALID_ARGUMENT, "args is null");
     if (!a->output) return fail(MLA_ERR_INVALID_ARGUMENT, "output is null");
-    return decode_impl(cfg, a, workspace, workspace_bytes, a->output, nullptr, nullptr,
+    return decode_impl(cfg, a, workspace, workspace_bytes, a->output, mla::PartOut{},
                        reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -457,7 +481,7 @@ mla_status_t mla_decode_partial(const mla_config_t* cfg, const mla_decode_args_t
                                 float* partial_o, void* workspace, size_t workspace_bytes,
                                 mla_stream_t stream) {
     if (!partial_ml || !partial_o) return fail(MLA_ERR_INVALID_ARGUMENT, "partial outputs are null");
-    return decode_impl(cfg, a, workspace, workspace_bytes, nullptr, partial_ml, partial_o,
+    return decode_impl(cfg, a, workspace, workspace_bytes, nullptr, mla::PartOut{partial_ml, partial_o, 0, nullptr, 0},
                        reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -503,8 +527,8 @@ mla_status_t mla_decode_partial_packed(const mla_config_t* cfg, const mla_decode
     if (num_slices <= 0 || cfg->num_heads % num_slices != 0)
         return fail(MLA_ERR_INVALID_ARGUMENT, "num_slices (%d) must divide num_heads (%d)", num_slices, cfg->num_heads);
     if (reinterpret_cast<uintptr_t>(packed) % 16 != 0) return fail(MLA_ERR_INVALID_ARGUMENT, "packed must be 16-byte aligned");
-    return decode_impl(cfg, a, workspace, workspace_bytes, nullptr, nullptr, packed,
-                       reinterpret_cast<cudaStream_t>(stream), 0, num_slices);
+    return decode_impl(cfg, a, workspace, workspace_bytes, nullptr, mla::PartOut{nullptr, packed, num_slices, nullptr, 0},
+                       reinterpret_cast<cudaStream_t>(stream));
 }
 
 mla_status_t mla_combine_partials_packed(const mla_config_t* cfg, mla_dtype_t dtype, int batch, int num_parts,
@@ -687,8 +711,106 @@ mla_status_t mla_launch_fused_noalloc(const mla_fused_params_t* p, mla_dtype_t d
     void* scratch = nullptr;
     st = noalloc_scratch(&scratch);
     if (st != MLA_OK) return st;
-    return decode_impl(p->cfg, &a, scratch, MLA_NOALLOC_SCRATCH_BYTES, a.output, nullptr, nullptr,
+    return decode_impl(p->cfg, &a, scratch, MLA_NOALLOC_SCRATCH_BYTES, a.output, mla::PartOut{},
                        reinterpret_cast<cudaStream_t>(stream), workers);
+}
+
+mla_status_t mla_decode_partial_put(const mla_config_t* cfg, const mla_decode_args_t* a, int world, void* const* dst,
+                                    size_t dst_offset, const mla_peer_signal_t* signal, void* workspace,
+                                    size_t workspace_bytes, mla_stream_t stream) {
+    mla_status_t st = validate_cfg(cfg);
+    if (st != MLA_OK) return st;
+    mla::PeerSig sig;
+    st = peer_sig(signal, &sig);
+    if (st != MLA_OK) return st;
+    if (!dst) return fail(MLA_ERR_INVALID_ARGUMENT, "dst is null");
+    if (world <= 0 || cfg->num_heads % world != 0)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "world (%d) must divide num_heads (%d)", world, cfg->num_heads);
+    if (dst_offset % 16 != 0) return fail(MLA_ERR_INVALID_ARGUMENT, "dst_offset must be a multiple of 16 bytes");
+    return decode_impl(cfg, a, workspace, workspace_bytes, nullptr, mla::PartOut{nullptr, nullptr, world, dst, dst_offset},
+                       reinterpret_cast<cudaStream_t>(stream), 0, sig);
+}
+
+mla_status_t mla_combine_partials_put(const mla_config_t* cfg, mla_dtype_t dtype, int batch, int num_parts, int heads,
+                                      const float* packed, const void* W_UV, int world, void* const* dst,
+                                      size_t dst_offset, size_t dst_pitch, const mla_peer_signal_t* signal,
+                                      float* scratch, mla_stream_t stream) {
+    mla_status_t st = validate_cfg(cfg);
+    if (st != MLA_OK) return st;
+    mla::PeerSig sig;
+    st = peer_sig(signal, &sig);
+    if (st != MLA_OK) return st;
+    if (!packed || !dst || !scratch) return fail(MLA_ERR_INVALID_ARGUMENT, "null pointer");
+    if (world <= 0 || world > 512) return fail(MLA_ERR_INVALID_ARGUMENT, "world must be in [1, 512]");
+    if (reinterpret_cast<uintptr_t>(packed) % 16 != 0 || reinterpret_cast<uintptr_t>(scratch) % 16 != 0)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "packed and scratch must be 16-byte aligned");
+    if (dst_offset % 16 != 0 || dst_pitch % 16 != 0)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "dst_offset and dst_pitch must be multiples of 16 bytes");
+    if (heads > 0 && dst_pitch < static_cast<size_t>(heads) * cfg->v_head_dim * sizeof(float))
+        return fail(MLA_ERR_INVALID_ARGUMENT, "dst_pitch is shorter than a token's rows");
+    const int row = cfg->kv_lora_rank + 4;
+    const mla::PeerRows rows{dst, dst_offset, dst_pitch, world, sig};
+    return combine_impl(cfg, dtype, batch, num_parts, heads, packed, packed + 4, row, row, W_UV, scratch,
+                        reinterpret_cast<cudaStream_t>(stream), rows);
+}
+
+mla_status_t mla_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+    if (!ptr || !handle) return fail(MLA_ERR_INVALID_ARGUMENT, "null pointer");
+    if (bytes == 0) return fail(MLA_ERR_INVALID_ARGUMENT, "bytes must be positive");
+    *ptr = nullptr;
+    const cudaError_t e = mla::ipc_alloc(bytes, ptr, handle);
+    if (e != cudaSuccess) {
+        if (*ptr) cudaFree(*ptr);
+        *ptr = nullptr;
+        return cuda_fail(e, "IPC allocation");
+    }
+    return MLA_OK;
+}
+
+mla_status_t mla_ipc_free(void* ptr) {
+    if (!ptr) return MLA_OK;
+    const cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? MLA_OK : cuda_fail(e, "cudaFree");
+}
+
+mla_status_t mla_ipc_open(const void* handle, void** ptr) {
+    if (!ptr || !handle) return fail(MLA_ERR_INVALID_ARGUMENT, "null pointer");
+    const cudaError_t e = mla::ipc_open(handle, ptr);
+    return e == cudaSuccess ? MLA_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+mla_status_t mla_ipc_close(void* ptr) {
+    if (!ptr) return MLA_OK;
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? MLA_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+mla_status_t mla_peer_put(const void* src, size_t rows, size_t row_bytes, size_t src_pitch, size_t src_stride,
+                          void* const* dst, size_t dst_pitch, size_t dst_offset, int world, int blocks,
+                          const mla_peer_signal_t* signal, mla_stream_t stream) {
+    mla::PeerSig sig;
+    mla_status_t st = peer_sig(signal, &sig);
+    if (st != MLA_OK) return st;
+    if (!src || !dst) return fail(MLA_ERR_INVALID_ARGUMENT, "null pointer");
+    if (world <= 0 || world > 65535 || blocks <= 0 || blocks > 1024)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "world in [1, 65535], blocks in [1, 1024]");
+    if (row_bytes % 16 || src_pitch % 16 || src_stride % 16 || dst_pitch % 16 || dst_offset % 16 ||
+        reinterpret_cast<uintptr_t>(src) % 16)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "sizes, pitches, strides, offsets and src must be multiples of 16 bytes");
+    if (rows == 0 || row_bytes == 0 || rows * (row_bytes / 16) >= (size_t{1} << 31) ||
+        rows * src_pitch >= (size_t{1} << 32) || rows * dst_pitch >= (size_t{1} << 32))
+        return fail(MLA_ERR_INVALID_ARGUMENT, "slice must be non-empty and span less than 4 GiB");
+    const cudaError_t e = mla::launch_peer_put(src, rows, row_bytes, src_pitch, src_stride, dst, dst_pitch, dst_offset,
+                                               world, blocks, sig, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MLA_OK : cuda_fail(e, "peer put kernel launch");
+}
+
+mla_status_t mla_peer_wait(const int* flags, int count, int* epoch, int advance, int* status, mla_stream_t stream) {
+    if (!flags || !epoch || count <= 0)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "flags and epoch must be non-null, count positive");
+    const cudaError_t e =
+        mla::launch_peer_wait(flags, count, epoch, advance, status, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MLA_OK : cuda_fail(e, "peer wait kernel launch");
 }
 
 const char* mla_last_error(void) { return g_last_error.c_str(); }

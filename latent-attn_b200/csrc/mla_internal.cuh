@@ -238,6 +238,52 @@ enum : int { kStatusOk = 0, kStatusTimeout = 1, kStatusBadPlan = 2, kStatusBadPa
 // Process-wide count of kernels launched by this library (mla_kernel_launch_count).
 void count_launches(int n);
 
+// How a kernel that stores into other ranks' buffers signals them (the protocol is in peer.cuh).
+struct PeerSig {
+    int* const* flags;       // world pointers: receiver q's flag words
+    int flag_index;          // the word this sender sets in every receiver
+    const int* epoch;        // this rank's step counter
+    unsigned int* counters;  // world words of this GPU: blocks of the kernel done per receiver
+};
+
+// Where the partial export writes the merged partial of (token b, head h):
+// - slices == 0: ml + (b H + h) * 2 holds (m, l) and o + (b H + h) * dc the latent sum;
+// - slices > 0: one packed row [m, l, 0, 0, o] of dc + 4 floats, rows grouped by head slice
+//   (H / slices heads a slice): at o + ((q B + b) hs + h % hs) (dc + 4) for q = h / hs, or, with
+//   peer != nullptr, in slice q's receiver: peer[q] + peer_offset bytes + (b hs + h % hs) rows.
+// m is in natural-log units (-inf with l = 0 for an empty partial).
+struct PartOut {
+    float* ml;
+    float* o;
+    int slices;
+    void* const* peer;
+    size_t peer_offset;
+    __host__ __device__ bool to_peers() const { return peer != nullptr; }
+    __device__ float* row(int b, int h, int B, int H, int dc) const {
+        if (!slices) return nullptr;
+        const int hs = H / slices, q = h / hs;
+        const long long r = static_cast<long long>(b) * hs + h % hs;
+        if (peer) return reinterpret_cast<float*>(static_cast<unsigned char*>(peer[q]) + peer_offset) + r * (dc + 4);
+        return o + (static_cast<long long>(q) * B * hs + r) * (dc + 4);
+    }
+    __device__ float* ml_at(int b, int h, int B, int H, int dc) const {
+        return slices ? row(b, h, B, H, dc) : ml + (static_cast<long long>(b) * H + h) * 2;
+    }
+    __device__ float* o_at(int b, int h, int B, int H, int dc) const {
+        return slices ? row(b, h, B, H, dc) + 4 : o + (static_cast<long long>(b) * H + h) * dc;
+    }
+};
+
+// The projection's output stored into every rank's buffer as well (world == 0: `out` only):
+// token b's (H, dv) rows at dst[q] + offset + b * pitch bytes for every q < world.
+struct PeerRows {
+    void* const* dst;
+    size_t offset;
+    size_t pitch;
+    int world;
+    PeerSig sig;
+};
+
 // ---- kernel launchers (defined in the .cu files; return cudaGetLastError()) ----
 // pack.cu
 template <typename T>
@@ -258,10 +304,20 @@ cudaError_t launch_project_sm100(const DecodePlan& P, const float* rec_ml, const
 // merge of gathered partial sets of [parts][B][H] rows -- (m natural-log max, l sum; l = 0 = empty)
 // at part_ml + row * ml_stride and o at part_o + row * o_stride -- followed by the W_UV projection
 bool project_parts_sm100_supported(int H, int dc, int dv, int parts);
+// With rows.world > 0 the merged, projected rows also go to every rank (PeerRows); with
+// B <= gemv_max_tokens() the GEMV kernel stores them itself, otherwise `out` is staged and a put
+// kernel follows.
 template <typename T>
 cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, const float* part_ml,
                                        const float* part_o, int ml_stride, int o_stride, const T* W_UV, float* out,
-                                       cudaStream_t s);
+                                       const PeerRows& rows, cudaStream_t s);
+// Partial export of a decode's records (one merged partial per (b, h), see PartOut) by the
+// GEMV merge, for B <= gemv_max_tokens(); with part.peer, slice q's receiver is signalled.
+bool export_gemv_supported(const DecodePlan& P);
+template <typename T>
+cudaError_t launch_export_gemv(const DecodePlan& P, const float* rec_ml, const T* rec_o, const PartOut& part,
+                               const PeerSig& sig, bool pdl, cudaStream_t s);
+int gemv_max_tokens();
 // linear_sm100.cu: Y[M x N] fp32 = X[M x K] . W[N x K]^T (the layer's projections)
 bool linear_sm100_supported(int M, int N, int K);
 template <typename T>
@@ -283,16 +339,24 @@ cudaError_t launch_cache_append(T* kv, long long stride, long long kv_rows, int 
                                 const T* k_rope, const int64_t* offs, const int* pages, int page_rows, int max_pages,
                                 int* seq_lens, int max_len, int* status, cudaStream_t s);
 // combine.cu
-// out == nullptr: export one partial per (b, h) instead, to part_ml (B, H, 2) / part_o (B, H, dc),
-// or with packed_slices > 0 to packed rows of dc + 4 floats at part_o (see mla_decode_partial_packed)
+// out == nullptr: export one partial per (b, h) instead (PartOut); with part.peer, slice q's
+// receiver is signalled once its rows have landed
 template <typename T>
 cudaError_t launch_combine(const DecodePlan& P, const float* rec_ml, const T* rec_o,
-                           const T* W_UV, float* out, float* part_ml, float* part_o, int packed_slices,
+                           const T* W_UV, float* out, const PartOut& part, const PeerSig& sig,
                            cudaStream_t s);
 template <typename T>
 cudaError_t launch_combine_parts(int B, int H, int dc, int dv, int parts, const float* part_ml,
                                  const float* part_o, int ml_stride, int o_stride, const T* W_UV, float* out,
                                  cudaStream_t s);
+
+// peer.cu: IPC allocations and the put / wait kernels of the multi-GPU exchange
+cudaError_t ipc_alloc(size_t bytes, void** ptr, void* handle);
+cudaError_t ipc_open(const void* handle, void** ptr);
+cudaError_t launch_peer_put(const void* src, size_t rows, size_t row_bytes, size_t src_pitch, size_t src_stride,
+                            void* const* dst, size_t dst_pitch, size_t dst_offset, int world, int blocks,
+                            const PeerSig& sig, cudaStream_t s);
+cudaError_t launch_peer_wait(const int* flags, int count, int* epoch, int advance, int* status, cudaStream_t s);
 
 // Raises a kernel's dynamic shared-memory limit once per device: the attribute persists,
 // and setting it on every launch would cost host time in every decode call.

@@ -442,6 +442,64 @@ def mla_combine_partials_packed(packed: torch.Tensor, W_UV_slice: torch.Tensor, 
     return out
 
 
+def mla_decode_partial_put(kv_cache, q_rope, W_UV, rope_cos, rope_sin, d_model, kv_lora_rank, qk_nope_head_dim,
+                           qk_rope_head_dim, num_heads, v_head_dim, *, dst_ptrs: torch.Tensor, dst_offset: int,
+                           signal: "PeerSignal", q_absorbed=None, q_nope=None, W_UK=None, kv_pos_offset: int = 0,
+                           softmax_scale: float = 0.0, workspace=None, kernel: int = 0, timer=None,
+                           rope_theta: float = 0.0) -> None:
+    """``mla_decode_partial_packed`` whose slice q lands in rank q's buffer
+    (``dst_ptrs[q] + dst_offset``), written by the export kernel itself, and rank q is signalled
+    (``signal``). world = ``dst_ptrs.numel()`` divides the heads."""
+    _check_half(kv_cache, "kv_cache")
+    _check_tables(rope_cos, rope_sin)
+    if dst_ptrs.dtype != torch.int64 or not dst_ptrs.is_cuda or dst_ptrs.dim() != 1:
+        raise RuntimeError("dst_ptrs must be a CUDA int64 vector of pointers")
+    world = int(dst_ptrs.numel())
+    if world != signal.world:
+        raise RuntimeError("dst_ptrs and the signal's flag pointers must have one entry per rank")
+    cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    B = q_rope.size(0)
+    L = kv_cache.size(0) // B
+    args = _decode_args(kv_cache.dtype, B, False, kv_cache, L, q_rope, W_UV, rope_cos, rope_sin, None,
+                        q_absorbed=q_absorbed, q_nope=None if q_absorbed is not None else q_nope,
+                        W_UK=None if q_absorbed is not None else W_UK, kv_pos_offset=kv_pos_offset,
+                        softmax_scale=softmax_scale, kernel=kernel, timer=timer, rope_theta=rope_theta)
+    ws = _workspace(cfg, args, kv_cache.device, workspace)
+    _lib.check(_lib.load().mla_decode_partial_put(C.byref(cfg), C.byref(args), world, C.c_void_p(dst_ptrs.data_ptr()),
+                                                  C.c_size_t(dst_offset), C.byref(signal.struct),
+                                                  C.c_void_p(ws.data_ptr()), C.c_size_t(ws.numel()),
+                                                  C.c_void_p(_stream(kv_cache.device))))
+
+
+def mla_combine_partials_put(packed: torch.Tensor, W_UV_slice: torch.Tensor, d_model, kv_lora_rank,
+                             qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim, *, dst_ptrs: torch.Tensor,
+                             dst_offset: int, dst_pitch: int, signal: "PeerSignal", scratch: torch.Tensor) -> None:
+    """``mla_combine_partials_packed`` whose (B, heads, dv) output lands in every rank's buffer:
+    token b's rows at ``dst_ptrs[q] + dst_offset + b * dst_pitch``; every rank is signalled.
+    ``scratch``: (B, heads, dv) fp32 of this rank (staging for batches the GEMV kernel does not
+    take)."""
+    _check_f32(packed, "packed")
+    _check_half(W_UV_slice, "W_UV_slice")
+    _check_f32(scratch, "scratch")
+    cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    if packed.dim() != 4 or packed.size(3) != kv_lora_rank + 4:
+        raise RuntimeError("packed must be (parts, batch, heads, kv_lora_rank + 4)")
+    P, B, heads = packed.size(0), packed.size(1), packed.size(2)
+    if W_UV_slice.dim() != 2 or W_UV_slice.size(0) != heads * v_head_dim or W_UV_slice.size(1) != kv_lora_rank:
+        raise RuntimeError("W_UV_slice must be (heads * v_head_dim, kv_lora_rank)")
+    if scratch.numel() < B * heads * v_head_dim:
+        raise RuntimeError("scratch must hold batch * heads * v_head_dim floats")
+    if dst_ptrs.dtype != torch.int64 or not dst_ptrs.is_cuda or dst_ptrs.dim() != 1:
+        raise RuntimeError("dst_ptrs must be a CUDA int64 vector of pointers")
+    if dst_ptrs.numel() != signal.world:
+        raise RuntimeError("dst_ptrs and the signal's flag pointers must have one entry per rank")
+    _lib.check(_lib.load().mla_combine_partials_put(
+        C.byref(cfg), _DT[W_UV_slice.dtype], B, P, heads, C.c_void_p(packed.data_ptr()),
+        C.c_void_p(W_UV_slice.data_ptr()), int(dst_ptrs.numel()), C.c_void_p(dst_ptrs.data_ptr()),
+        C.c_size_t(dst_offset), C.c_size_t(dst_pitch), C.byref(signal.struct), C.c_void_p(scratch.data_ptr()),
+        C.c_void_p(_stream(packed.device))))
+
+
 def mla_combine_partials(part_ml: torch.Tensor, part_o: torch.Tensor, W_UV: torch.Tensor, d_model,
                          kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim,
                          out: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -521,3 +579,107 @@ def mla_cache_append(kv_cache: torch.Tensor, c_t: torch.Tensor, k_rope: torch.Te
                                     C.c_void_p(_ptr(page_table)), int(page_rows), max_pages,
                                     C.c_void_p(seq_lens.data_ptr()), int(max_seq_len),
                                     C.c_void_p(_ptr(status)), C.c_void_p(_stream(kv_cache.device))))
+
+
+# ---- peer memory for the multi-GPU exchange (mla_ipc_* / mla_peer_*)
+
+class IpcBuffer:
+    """A device allocation other processes of the node can map (``mla_ipc_alloc``), zero-filled.
+
+    ``handle`` (bytes) goes to the peers, which map it with ``ipc_open``; ``view(dtype, count,
+    offset)`` is a tensor over part of it. The tensors do not own the memory: keep this object
+    alive while they are used, and ``free()`` it only after every peer has closed its mapping."""
+
+    def __init__(self, nbytes: int, device: torch.device):
+        self.nbytes, self.device = int(nbytes), device
+        p = C.c_void_p()
+        h = (C.c_char * _lib.IPC_HANDLE_BYTES)()
+        with torch.cuda.device(device):
+            _lib.check(_lib.load().mla_ipc_alloc(C.c_size_t(self.nbytes), C.byref(p), h))
+        self.ptr, self.handle = int(p.value), bytes(h)
+
+    def view(self, dtype: torch.dtype, count: int, offset: int = 0) -> torch.Tensor:
+        item = torch.empty((), dtype=dtype).element_size()
+        if offset % item or offset < 0 or offset + count * item > self.nbytes:
+            raise ValueError("view outside the allocation")
+        return _device_view(self.ptr + offset, dtype, count, self.device)
+
+    def free(self) -> None:
+        if self.ptr:
+            with torch.cuda.device(self.device):
+                _lib.check(_lib.load().mla_ipc_free(C.c_void_p(self.ptr)))
+            self.ptr = 0
+
+
+_TYPESTR = {torch.float32: "<f4", torch.int32: "<i4", torch.int64: "<i8", torch.uint8: "|u1"}
+
+
+def _device_view(ptr: int, dtype: torch.dtype, count: int, device: torch.device) -> torch.Tensor:
+    class _Iface:   # __cuda_array_interface__ v2 over a raw device pointer
+        __cuda_array_interface__ = {"shape": (int(count),), "typestr": _TYPESTR[dtype], "data": (int(ptr), False),
+                                    "version": 2, "strides": None}
+    return torch.as_tensor(_Iface(), device=device)
+
+
+def ipc_open(handle: bytes, device: torch.device) -> int:
+    """Maps a peer's ``IpcBuffer`` (by its handle) into this process; returns the device pointer."""
+    if len(handle) != _lib.IPC_HANDLE_BYTES:
+        raise ValueError("bad IPC handle length")
+    p = C.c_void_p()
+    with torch.cuda.device(device):
+        _lib.check(_lib.load().mla_ipc_open(C.c_char_p(handle), C.byref(p)))
+    return int(p.value)
+
+
+def ipc_close(ptr: int, device: torch.device) -> None:
+    with torch.cuda.device(device):
+        _lib.check(_lib.load().mla_ipc_close(C.c_void_p(ptr)))
+
+
+class PeerSignal:
+    """``mla_peer_signal_t``: how a kernel storing into other ranks' buffers flags them. Receiver
+    q's word ``flag_index`` (of the int32 words ``flag_ptrs[q]`` points to) is set to ``epoch + 1``
+    once the kernel's stores bound for q are done; ``counters`` are this rank's ``world`` zeroed
+    int32 words the kernel's blocks count themselves in. All tensors on this rank's GPU."""
+
+    def __init__(self, flag_ptrs: torch.Tensor, flag_index: int, epoch: torch.Tensor, counters: torch.Tensor):
+        if flag_ptrs.dtype != torch.int64 or not flag_ptrs.is_cuda or flag_ptrs.dim() != 1:
+            raise RuntimeError("flag_ptrs must be a CUDA int64 vector of pointers")
+        if epoch.dtype != torch.int32 or not epoch.is_cuda:
+            raise RuntimeError("epoch must be a CUDA int32 tensor")
+        if counters.dtype != torch.int32 or not counters.is_cuda or counters.numel() < flag_ptrs.numel():
+            raise RuntimeError("counters must be a CUDA int32 tensor with one word per rank")
+        self.world = int(flag_ptrs.numel())
+        self._keep = (flag_ptrs, epoch, counters)
+        self.struct = _lib.MlaPeerSignal(flag_ptrs.data_ptr(), int(flag_index), epoch.data_ptr(), counters.data_ptr())
+
+
+def peer_put(src: torch.Tensor, rows: int, row_bytes: int, src_pitch: int, src_stride: int, dst_ptrs: torch.Tensor,
+             dst_pitch: int, dst_offset: int, blocks: int, signal: PeerSignal) -> None:
+    """``mla_peer_put`` on the current stream: slice q of ``src`` (rows x row_bytes, rows
+    ``src_pitch`` apart, slices ``src_stride`` apart) to ``dst_ptrs[q] + dst_offset`` (rows
+    ``dst_pitch`` apart), ``blocks`` blocks a slice, then receiver q is signalled.
+    ``dst_ptrs``: CUDA int64 tensor of world pointers."""
+    if not src.is_cuda or not src.is_contiguous():
+        raise RuntimeError("src must be a contiguous CUDA tensor")
+    if dst_ptrs.dtype != torch.int64 or not dst_ptrs.is_cuda or dst_ptrs.dim() != 1:
+        raise RuntimeError("dst_ptrs must be a CUDA int64 vector of pointers")
+    if dst_ptrs.numel() != signal.world:
+        raise RuntimeError("dst_ptrs and the signal's flag pointers must have one entry per rank")
+    _lib.check(_lib.load().mla_peer_put(
+        C.c_void_p(src.data_ptr()), C.c_size_t(rows), C.c_size_t(row_bytes), C.c_size_t(src_pitch),
+        C.c_size_t(src_stride), C.c_void_p(dst_ptrs.data_ptr()), C.c_size_t(dst_pitch), C.c_size_t(dst_offset),
+        int(dst_ptrs.numel()), int(blocks), C.byref(signal.struct), C.c_void_p(_stream(src.device))))
+
+
+def peer_wait(flags: torch.Tensor, epoch: torch.Tensor, advance: bool, status: Optional[torch.Tensor]) -> None:
+    """``mla_peer_wait`` on the current stream: waits (bounded, 2 s) until every word of the int32
+    vector ``flags`` reaches ``epoch + 1``; ``advance`` then increments ``epoch``. A wait that
+    gives up stores 1 to ``status``."""
+    if flags.dtype != torch.int32 or not flags.is_cuda or not flags.is_contiguous():
+        raise RuntimeError("flags must be a contiguous CUDA int32 tensor")
+    if epoch.dtype != torch.int32 or not epoch.is_cuda:
+        raise RuntimeError("epoch must be a CUDA int32 tensor")
+    _lib.check(_lib.load().mla_peer_wait(C.c_void_p(flags.data_ptr()), int(flags.numel()),
+                                         C.c_void_p(epoch.data_ptr()), 1 if advance else 0,
+                                         C.c_void_p(_ptr(status)), C.c_void_p(_stream(flags.device))))

@@ -63,12 +63,18 @@ class MlaDecodeArgs(C.Structure):
                 ("page_table", C.c_void_p), ("page_rows", C.c_int), ("max_pages", C.c_int),
                 ("rope_theta", C.c_float)]
 
+class MlaPeerSignal(C.Structure):
+    _fields_ = [("flags", C.c_void_p), ("flag_index", C.c_int), ("epoch", C.c_void_p), ("counters", C.c_void_p)]
+
+
 KERNEL_AUTO = 0
 KERNEL_TENSOR_CORE = 1
 KERNEL_CUDA_CORE = 2
 
 
 # Every symbol the header declares, with (restype, argtypes).
+IPC_HANDLE_BYTES = 64   # MLA_IPC_HANDLE_BYTES
+
 SIGNATURES = {
     "mla_config_validate": (C.c_int, [C.POINTER(MlaConfig)]),
     "mla_launch_fused": (C.c_int, [C.POINTER(MlaFusedParams), C.c_int, C.c_void_p]),
@@ -90,6 +96,18 @@ SIGNATURES = {
                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                    C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "mla_linear": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "mla_ipc_alloc": (C.c_int, [C.c_size_t, C.POINTER(C.c_void_p), C.c_void_p]),
+    "mla_ipc_free": (C.c_int, [C.c_void_p]),
+    "mla_ipc_open": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "mla_ipc_close": (C.c_int, [C.c_void_p]),
+    "mla_peer_put": (C.c_int, [C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
+                               C.c_size_t, C.c_int, C.c_int, C.POINTER(MlaPeerSignal), C.c_void_p]),
+    "mla_decode_partial_put": (C.c_int, [C.POINTER(MlaConfig), C.POINTER(MlaDecodeArgs), C.c_int, C.c_void_p,
+                                         C.c_size_t, C.POINTER(MlaPeerSignal), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "mla_combine_partials_put": (C.c_int, [C.POINTER(MlaConfig), C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                           C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_size_t,
+                                           C.POINTER(MlaPeerSignal), C.c_void_p, C.c_void_p]),
+    "mla_peer_wait": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "mla_timer_create": (C.c_int, [C.POINTER(C.c_void_p)]),
     "mla_timer_destroy": (C.c_int, [C.c_void_p]),
     "mla_timer_decode_ms": (C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),

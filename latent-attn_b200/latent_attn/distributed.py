@@ -24,6 +24,16 @@ rank (about 0.25 MiB for one DeepSeek-V2 token), the output all-gather
 ``B * H * dv * 4`` bytes, and each rank merges and projects only its slice of
 the heads. With a head count the ranks do not divide, the partials are
 all-gathered instead and every rank merges all of them (``gather_partials``).
+
+The two exchanges run either through NCCL (``exchange="nccl"``) or inside the
+library's own kernels (``exchange="p2p"``, the default): every rank maps the
+others' buffers (CUDA IPC, ``PeerExchange``); the kernel that exports the
+partials stores each head slice straight into its owner's receive area over
+NVLink (``mla_decode_partial_put``) and flags it, a bounded wait kernel on the
+receiver orders the merge after the flags, and the merge kernel stores its
+128-wide outputs into every rank's output area the same way
+(``mla_combine_partials_put``). Flags carry a device-resident step counter, so
+the exchange can be captured in a CUDA graph and replayed.
 """
 
 from __future__ import annotations
@@ -128,6 +138,111 @@ def gather_head_slices(o_slice: torch.Tensor, group=None, out: Optional[torch.Te
     return out
 
 
+def _blocks_for(nbytes: int) -> int:
+    """Thread blocks a put kernel gives one destination: one per 16 KiB, 1 to 32."""
+    return max(1, min(32, -(-nbytes // 16384)))
+
+
+class PeerExchange:
+    """Peer-memory buffers of a head-sliced exchange on the ranks of one node.
+
+    Every rank allocates one IPC buffer holding the flag words of the two exchanges (one word per
+    sender for each), the receive area of the partials (world blocks of ``slice_bytes``) and the
+    output area (``out_bytes``); the handles are all-gathered once and every rank maps every
+    peer's buffer. ``sig_partials`` / ``sig_outputs`` describe how this rank's kernels signal
+    the receivers of each exchange (flag word ``rank`` or ``world + rank``); the matching waits
+    are ``wait_partials`` and ``wait_outputs`` (the latter ends the step). ``close()`` is a
+    collective (unmap everywhere, barrier, free)."""
+
+    def __init__(self, slice_bytes: int, out_bytes: int, device: torch.device, group=None):
+        from latent_attn import _C
+        self.group, self.device = group, device
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.slice_bytes, self.out_bytes = slice_bytes, out_bytes
+        self.flag_bytes = -(-2 * self.world * 4 // 256) * 256
+        self.recv_off = self.flag_bytes
+        self.out_off = self.recv_off + -(-self.world * slice_bytes // 256) * 256
+        total = self.out_off + -(-out_bytes // 256) * 256
+        self.buf = _C.IpcBuffer(total, device)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.buf.handle, group=group)
+        self.mapped = []
+        ptrs = []
+        try:
+            for q in range(self.world):
+                if q == self.rank:
+                    ptrs.append(self.buf.ptr)
+                else:
+                    ptrs.append(_C.ipc_open(handles[q], device))
+                    self.mapped.append(ptrs[-1])
+        except Exception:
+            for p in self.mapped:
+                _C.ipc_close(p, device)
+            self.buf.free()
+            raise
+        base = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self.flag_ptrs = base
+        self.recv_ptrs = base + self.recv_off
+        self.out_ptrs = base + self.out_off
+        self.flags = self.buf.view(torch.int32, 2 * self.world)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.counters = torch.zeros(2 * self.world, dtype=torch.int32, device=device)
+        self.sig_partials = _C.PeerSignal(self.flag_ptrs, self.rank, self.epoch, self.counters[:self.world])
+        self.sig_outputs = _C.PeerSignal(self.flag_ptrs, self.world + self.rank, self.epoch,
+                                         self.counters[self.world:])
+
+    def recv(self, dtype=torch.float32) -> torch.Tensor:
+        return self.buf.view(dtype, self.world * self.slice_bytes // 4, self.recv_off)
+
+    def out(self, dtype=torch.float32) -> torch.Tensor:
+        return self.buf.view(dtype, self.out_bytes // 4, self.out_off)
+
+    def wait_partials(self) -> None:
+        """Orders the stream after every rank's partials for this rank have landed."""
+        from latent_attn import _C
+        _C.peer_wait(self.flags[:self.world], self.epoch, False, self.status)
+
+    def wait_outputs(self) -> None:
+        """Orders the stream after every rank's outputs have landed; ends the exchange step."""
+        from latent_attn import _C
+        _C.peer_wait(self.flags[self.world:], self.epoch, True, self.status)
+
+    def all_to_all(self, send: torch.Tensor) -> None:
+        """Put kernel: slice q of ``send`` (world slices of ``slice_bytes``) to rank q's receive
+        block ``rank``; then ``wait_partials``."""
+        from latent_attn import _C
+        sb = self.slice_bytes
+        _C.peer_put(send, 1, sb, 0, sb, self.recv_ptrs, 0, self.rank * sb, _blocks_for(sb), self.sig_partials)
+        self.wait_partials()
+
+    def all_gather_rows(self, src: torch.Tensor, rows: int, row_bytes: int, dst_pitch: int) -> None:
+        """Put kernel: ``src`` (rows x row_bytes) to every rank's output area at column offset
+        ``rank * row_bytes`` (rows ``dst_pitch`` apart); then ``wait_outputs``."""
+        from latent_attn import _C
+        _C.peer_put(src, rows, row_bytes, row_bytes, 0, self.out_ptrs, dst_pitch, self.rank * row_bytes,
+                    _blocks_for(rows * row_bytes), self.sig_outputs)
+        self.wait_outputs()
+
+    def check(self) -> None:
+        """Raises if a wait of this rank gave up (a peer did not deliver within 2 s)."""
+        if int(self.status.item()):
+            raise RuntimeError("peer exchange: a wait for a peer's data timed out")
+
+    def close(self) -> None:
+        from latent_attn import _C
+        if self.buf is None:
+            return
+        torch.cuda.synchronize(self.device)
+        for p in self.mapped:
+            _C.ipc_close(p, self.device)
+        self.mapped = []
+        dist.barrier(group=self.group)
+        self.buf.free()
+        self.buf = None
+
+
 class KVRangeDecoder:
     """Decode one token per sequence over a cache whose rows are split across ranks.
 
@@ -136,14 +251,25 @@ class KVRangeDecoder:
     are the full tables (they are indexed by absolute position), or both None for
     on-the-fly RoPE. Exchange buffers are allocated on the first call and reused.
     When the ranks divide the heads, each rank merges and projects its slice of the
-    heads (one all-to-all, one output all-gather); otherwise every rank merges all
-    partials after an all-gather.
+    heads (one all-to-all, one output all-gather): through peer memory with
+    ``exchange="p2p"`` (the default; ranks of one node) or NCCL with
+    ``exchange="nccl"``. Otherwise every rank merges all partials after an NCCL
+    all-gather.
+
+    With the peer-memory exchange and no ``out``, the returned tensor is the
+    exchange's output area: it is overwritten by the next call. ``close()``
+    releases the peer buffers (a collective).
     """
 
-    def __init__(self, cfg, group=None):
+    def __init__(self, cfg, group=None, exchange: str = "p2p"):
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError("exchange must be 'p2p' or 'nccl'")
         self.cfg = cfg
         self.group = group
+        self.exchange = exchange
         self._buf = {}
+        self._peer = None
+        self._peer_key = None
 
     def _get(self, name, shape, like):
         t = self._buf.get(name)
@@ -151,6 +277,26 @@ class KVRangeDecoder:
             t = torch.empty(shape, dtype=torch.float32, device=like.device)
             self._buf[name] = t
         return t
+
+    def _peers(self, B, hs, world, device) -> PeerExchange:
+        c = self.cfg
+        key = (B, hs, world, device)
+        if self._peer_key != key:
+            if self._peer is not None:
+                self._peer.close()
+            R = c.kv_lora_rank + 4
+            self._peer = PeerExchange(B * hs * R * 4, B * world * hs * c.v_head_dim * 4, device, self.group)
+            self._peer_key = key
+        return self._peer
+
+    def check(self) -> None:
+        if self._peer is not None:
+            self._peer.check()
+
+    def close(self) -> None:
+        if self._peer is not None:
+            self._peer.close()
+            self._peer, self._peer_key = None, None
 
     def __call__(self, kv_local: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
                  rope_cos: Optional[torch.Tensor], rope_sin: Optional[torch.Tensor], *, pos_offset: int,
@@ -165,13 +311,31 @@ class KVRangeDecoder:
         B, H, dc, dv = q_rope.size(0), c.num_heads, c.kv_lora_rank, c.v_head_dim
         if H % world == 0:
             hs = H // world
+            W_slice = W_UV[rank * hs * dv:(rank + 1) * hs * dv]
+            if self.exchange == "p2p":
+                # the export kernel stores each head slice into its owner's receive area, the merge
+                # kernel stores the merged rows into every rank's output area (NVLink stores)
+                px = self._peers(B, hs, world, q_rope.device)
+                _C.mla_decode_partial_put(kv_local, q_rope, W_UV, rope_cos, rope_sin, *dims, dst_ptrs=px.recv_ptrs,
+                                          dst_offset=rank * px.slice_bytes, signal=px.sig_partials,
+                                          q_absorbed=q_absorbed, q_nope=q_nope, W_UK=W_UK, kv_pos_offset=pos_offset,
+                                          workspace=workspace, timer=timer)
+                px.wait_partials()
+                recv = px.recv().view(world, B, hs, dc + 4)
+                _C.mla_combine_partials_put(recv, W_slice, *dims, dst_ptrs=px.out_ptrs, dst_offset=rank * hs * dv * 4,
+                                            dst_pitch=H * dv * 4, signal=px.sig_outputs,
+                                            scratch=self._get("slice", (B, hs, dv), q_rope))
+                px.wait_outputs()
+                full = px.out().view(B, H, dv)
+                if out is None:
+                    return full
+                return out.copy_(full)
             send = self._get("send", (world, B, hs, dc + 4), q_rope)
             _C.mla_decode_partial_packed(kv_local, q_rope, W_UV, rope_cos, rope_sin, *dims, num_slices=world,
                                          q_absorbed=q_absorbed, q_nope=q_nope, W_UK=W_UK,
                                          kv_pos_offset=pos_offset, workspace=workspace, timer=timer, out=send)
             recv = exchange_head_slices(send, self.group, out=self._get("recv", send.shape, q_rope))
-            o_slice = _C.mla_combine_partials_packed(recv, W_UV[rank * hs * dv:(rank + 1) * hs * dv], *dims,
-                                                     out=self._get("slice", (B, hs, dv), q_rope))
+            o_slice = _C.mla_combine_partials_packed(recv, W_slice, *dims, out=self._get("slice", (B, hs, dv), q_rope))
             staging = self._get("stage", (world, B, hs, dv), q_rope) if B > 1 else None
             return gather_head_slices(o_slice, self.group, out=out, staging=staging)
         ml, o = _C.mla_decode_partial(kv_local, q_rope, W_UV, rope_cos, rope_sin, *dims,
@@ -183,4 +347,4 @@ class KVRangeDecoder:
 
 
 __all__ = ["lpt_shard", "kv_range", "gather_partials", "packed_row", "exchange_head_slices", "gather_head_slices",
-           "KVRangeDecoder"]
+           "PeerExchange", "KVRangeDecoder"]

@@ -48,6 +48,8 @@ int main(void) {
   P(mla_decode_args_t, kv_total_rows) P(mla_decode_args_t, seq_lens_host) P(mla_decode_args_t, softmax_scale)
   P(mla_decode_args_t, output) P(mla_decode_args_t, kernel) P(mla_fused_params_t, cfg)
   P(mla_batched_fused_params_t, output) P(mla_decode_args_t, page_table) P(mla_decode_args_t, max_pages)
+  printf("mla_peer_signal_t %zu\n", sizeof(mla_peer_signal_t));
+  P(mla_peer_signal_t, flag_index) P(mla_peer_signal_t, epoch) P(mla_peer_signal_t, counters)
   return 0;
 }
 '''
@@ -72,6 +74,10 @@ int main(void) {
         "mla_batched_fused_params_t.output": _lib.MlaBatchedFusedParams.output.offset,
         "mla_decode_args_t.page_table": _lib.MlaDecodeArgs.page_table.offset,
         "mla_decode_args_t.max_pages": _lib.MlaDecodeArgs.max_pages.offset,
+        "mla_peer_signal_t": C.sizeof(_lib.MlaPeerSignal),
+        "mla_peer_signal_t.flag_index": _lib.MlaPeerSignal.flag_index.offset,
+        "mla_peer_signal_t.epoch": _lib.MlaPeerSignal.epoch.offset,
+        "mla_peer_signal_t.counters": _lib.MlaPeerSignal.counters.offset,
     }
     for k, v in want.items():
         assert int(got[k]) == v, (k, got[k], v)

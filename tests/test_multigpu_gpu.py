@@ -1,8 +1,12 @@
-"""KV-range decode through latent_attn.distributed on CUDA with NCCL.
+"""KV-range decode through latent_attn.distributed on CUDA: the NCCL exchange and the library's
+peer-memory exchange (put / wait kernels over CUDA IPC mappings).
 
-A one-rank process group checks the glue (partial -> all-gather -> merge) on any
-GPU box; the two-rank case runs when the box has two GPUs, one process per GPU,
-and compares every rank's output with the fp64 oracle of the whole sequence.
+The put / wait kernels are checked on one GPU (every "rank" a local buffer, the puts stream-
+ordered before the waits, so nothing waits on a kernel that runs beside it), including a wait that
+runs out because nothing sets its flag. A one-rank process group checks the decode glue on any GPU
+box; the two-rank cases run when the box has two GPUs, one process per GPU, and compare every
+rank's output with the fp64 oracle of the whole sequence and the two exchanges with each other
+(bit-identical: same kernels, same merge order), eagerly and replayed from a CUDA graph.
 """
 
 import os
@@ -35,56 +39,240 @@ def _oracle(inp, L):
                              inp.W_UV.float().numpy(), cos, sin, 128, 512, 128, 64, 128)
 
 
-def _decode_rank(rank, world, L, seed):
+def _oracle_batch(inp, L, B):
+    cos, sin = O.rope_tables(L, 64)
+    outs = []
+    for b in range(B):
+        q_abs = O.absorb_query(inp.q_nope[b].float().numpy(), inp.W_UK.float().numpy(), 128, 512)
+        kv = inp.kv_cache[b * L:(b + 1) * L].float().numpy()
+        outs.append(O.absorbed_decode(kv, q_abs, inp.q_rope[b].float().numpy(), inp.W_UV.float().numpy(), cos, sin,
+                                      128, 512, 128, 64, 128))
+    return np.stack(outs)
+
+
+def _decode_rank(rank, world, L, seed, exchange="nccl", B=1, graph=False):
+    """Two eager calls (the second reuses the exchange buffers) and, with ``graph``, two replays
+    of a captured call; returns the inputs and every call's (B, H, dv) output."""
     dev = torch.device("cuda", rank)
-    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[L], seed=seed)
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[L] * B, seed=seed)
     lo, hi = kv_range(L, world, rank)
     cos, sin = synthetic.build_rope_tables(L, 64, device=dev)
-    dec = KVRangeDecoder(MLAConfig.deepseek_v2())
+    dec = KVRangeDecoder(MLAConfig.deepseek_v2(), exchange=exchange)
+    kv = torch.cat([inp.kv_cache[b * L + lo:b * L + hi] for b in range(B)]).contiguous().to(dev)
+    args = (kv, inp.q_rope.float().to(dev), inp.W_UV.to(dev), cos, sin)
+    kw = dict(pos_offset=lo, q_nope=inp.q_nope.float().to(dev), W_UK=inp.W_UK.to(dev))
     outs = []
-    for _ in range(2):                        # the second call reuses the gather buffers
-        out = dec(inp.kv_cache[lo:hi].contiguous().to(dev), inp.q_rope.float().to(dev), inp.W_UV.to(dev), cos,
-                  sin, pos_offset=lo, q_nope=inp.q_nope.float().to(dev), W_UK=inp.W_UK.to(dev))
-        outs.append(out.cpu().numpy()[0])
+    for _ in range(2):
+        outs.append(dec(*args, **kw).cpu().numpy())
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        with torch.cuda.graph(g, stream=side):
+            o = dec(*args, **kw)
+        for _ in range(2):
+            g.replay()
+            torch.cuda.synchronize(dev)
+            outs.append(o.cpu().numpy())
+        g.reset()
+        del g
+    dec.check()
+    dec.close()
     return inp, outs
 
 
-def test_kv_range_decoder_single_rank():
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+def test_kv_range_decoder_single_rank(exchange):
     L = 5000
     dist.init_process_group("nccl", rank=0, world_size=1, store=dist.HashStore(),
                             device_id=torch.device("cuda", 0))
     try:
-        inp, outs = _decode_rank(0, 1, L, 3)
+        inp, outs = _decode_rank(0, 1, L, 3, exchange, graph=exchange == "p2p")
     finally:
         dist.destroy_process_group()
     ref = _oracle(inp, L)
     for o in outs:
-        _close(o, ref, "one rank")
-    np.testing.assert_array_equal(outs[0], outs[1])
+        _close(o[0], ref, "one rank")
+        np.testing.assert_array_equal(outs[0], o)
 
 
-def _two_rank_worker(rank, world, port, L, seed, q):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+def _ptrs(values):
+    return torch.tensor(values, dtype=torch.int64, device="cuda")
+
+
+def _signals(flag_ptrs, world, r, epoch, counters):
+    from latent_attn import _C
+    return (_C.PeerSignal(flag_ptrs, r, epoch, counters[:world]),
+            _C.PeerSignal(flag_ptrs, world + r, epoch, counters[world:]))
+
+
+def test_peer_put_all_to_all_and_row_gather_on_one_gpu():
+    """Two emulated ranks on one GPU: an all-to-all of 4144-byte slices (rows = 1, three blocks
+    each) and a row-wise all-gather (rows = 5, destination pitch of the full row); every byte
+    checked, the flags at the step count, the block counters back at zero, and the step counter
+    advanced once per step by the ending wait."""
+    from latent_attn import _C
+    world, nblk = 2, 3
+    slice_bytes, rows, row_bytes = 4096 + 48, 5, 192
+    full_pitch = world * row_bytes
+    bufs = [_C.IpcBuffer(1 << 16, torch.device("cuda", 0)) for _ in range(world)]
+    try:
+        flags = [b.view(torch.int32, 2 * world) for b in bufs]
+        recv_off, out_off = 1024, 1024 + world * slice_bytes
+        flag_ptrs = _ptrs([b.ptr for b in bufs])
+        recv_ptrs, out_ptrs = flag_ptrs + recv_off, flag_ptrs + out_off
+        epochs = [torch.zeros(1, dtype=torch.int32, device="cuda") for _ in range(world)]
+        counters = [torch.zeros(2 * world, dtype=torch.int32, device="cuda") for _ in range(world)]
+        sigs = [_signals(flag_ptrs, world, r, epochs[r], counters[r]) for r in range(world)]
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        g = torch.Generator().manual_seed(9)
+        send = [torch.randint(0, 256, (world * slice_bytes,), generator=g, dtype=torch.uint8).cuda()
+                for _ in range(world)]
+        rowsrc = [torch.randint(0, 256, (rows * row_bytes,), generator=g, dtype=torch.uint8).cuda()
+                  for _ in range(world)]
+        for step in range(2):
+            for r in range(world):
+                _C.peer_put(send[r], 1, slice_bytes, 0, slice_bytes, recv_ptrs, 0, r * slice_bytes, nblk, sigs[r][0])
+            for r in range(world):
+                _C.peer_wait(flags[r][:world], epochs[r], False, status)
+            for r in range(world):
+                _C.peer_put(rowsrc[r], rows, row_bytes, row_bytes, 0, out_ptrs, full_pitch, r * row_bytes, nblk,
+                            sigs[r][1])
+            for r in range(world):
+                _C.peer_wait(flags[r][world:], epochs[r], True, status)
+            torch.cuda.synchronize()
+            assert int(status.item()) == 0
+            for r in range(world):
+                assert int(epochs[r].item()) == step + 1
+                assert torch.all(flags[r] == step + 1)
+                assert torch.all(counters[r] == 0)
+                recv = bufs[r].view(torch.uint8, world * slice_bytes, recv_off).view(world, slice_bytes)
+                for p in range(world):   # block p of rank r's receive area = rank p's slice r
+                    assert torch.equal(recv[p], send[p].view(world, slice_bytes)[r])
+                out = bufs[r].view(torch.uint8, rows * full_pitch, out_off).view(rows, world, row_bytes)
+                for p in range(world):
+                    assert torch.equal(out[:, p], rowsrc[p].view(rows, row_bytes))
+            send = [s.roll(1) for s in send]
+    finally:
+        for b in bufs:
+            b.free()
+
+
+@pytest.mark.parametrize("B", [1, 5])
+def test_fused_exchange_kernels_two_emulated_ranks_on_one_gpu(B):
+    """The kernels that store into other ranks' memory, with two emulated ranks on one GPU (every
+    call stream-ordered): the partial export (mla_decode_partial_put; B = 1 the GEMV merge, B = 5
+    the CUDA-core combine) must fill receiver q's block p with exactly what
+    mla_decode_partial_packed gives rank p for slice q, and the merge + projection
+    (mla_combine_partials_put; B = 1 stored by the GEMV kernel, B = 5 staged and put) must give
+    every receiver the same full output, bit-identical to mla_combine_partials_packed and within
+    the decode tolerance of the oracle."""
+    from latent_attn import _C
+    world, L, H, dc, dv = 2, 3001, 128, 512, 128
+    hs = H // world
+    cfg = MLAConfig.deepseek_v2()
+    dims = (cfg.d_model, 512, 128, 64, 128, 128)
+    dev = torch.device("cuda", 0)
+    inp = synthetic.baseline_inputs(num_heads=H, seq_lens=[L] * B, seed=11)
+    cos, sin = synthetic.build_rope_tables(L, 64, device=dev)
+    W_UV = inp.W_UV.to(dev)
+    qn, qr, WK = inp.q_nope.float().to(dev), inp.q_rope.float().to(dev), inp.W_UK.to(dev)
+    shards = []
+    for r in range(world):
+        lo, hi = kv_range(L, world, r)
+        shards.append((lo, torch.cat([inp.kv_cache[b * L + lo:b * L + hi] for b in range(B)]).contiguous().to(dev)))
+    sends = [_C.mla_decode_partial_packed(kv, qr, W_UV, cos, sin, *dims, num_slices=world, q_nope=qn, W_UK=WK,
+                                          kv_pos_offset=lo) for lo, kv in shards]
+    slice_bytes = B * hs * (dc + 4) * 4
+    out_bytes = B * H * dv * 4
+    recv_off = 256
+    out_off = recv_off + world * slice_bytes
+    bufs = [_C.IpcBuffer(out_off + out_bytes, dev) for _ in range(world)]
+    try:
+        flag_ptrs = _ptrs([b.ptr for b in bufs])
+        epochs = [torch.zeros(1, dtype=torch.int32, device=dev) for _ in range(world)]
+        counters = [torch.zeros(2 * world, dtype=torch.int32, device=dev) for _ in range(world)]
+        sigs = [_signals(flag_ptrs, world, r, epochs[r], counters[r]) for r in range(world)]
+        flags = [b.view(torch.int32, 2 * world) for b in bufs]
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        for r, (lo, kv) in enumerate(shards):
+            _C.mla_decode_partial_put(kv, qr, W_UV, cos, sin, *dims, dst_ptrs=flag_ptrs + recv_off,
+                                      dst_offset=r * slice_bytes, signal=sigs[r][0], q_nope=qn, W_UK=WK,
+                                      kv_pos_offset=lo)
+        for q in range(world):
+            _C.peer_wait(flags[q][:world], epochs[q], False, status)
+        recvs = [bufs[q].view(torch.float32, world * slice_bytes // 4, recv_off).view(world, B, hs, dc + 4)
+                 for q in range(world)]
+        for q in range(world):
+            for p in range(world):
+                assert torch.equal(recvs[q][p], sends[p][q]), (q, p)
+        scratch = torch.empty(B, hs, dv, device=dev)
+        want = []
+        for r in range(world):
+            W_slice = W_UV[r * hs * dv:(r + 1) * hs * dv]
+            want.append(_C.mla_combine_partials_packed(recvs[r].clone(), W_slice, *dims))
+            _C.mla_combine_partials_put(recvs[r], W_slice, *dims, dst_ptrs=flag_ptrs + out_off,
+                                        dst_offset=r * hs * dv * 4, dst_pitch=H * dv * 4, signal=sigs[r][1],
+                                        scratch=scratch)
+        for q in range(world):
+            _C.peer_wait(flags[q][world:], epochs[q], True, status)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        full = torch.cat(want, dim=1)
+        for q in range(world):
+            assert int(epochs[q].item()) == 1 and torch.all(flags[q] == 1) and torch.all(counters[q] == 0)
+            got = bufs[q].view(torch.float32, out_bytes // 4, out_off).view(B, H, dv)
+            assert torch.equal(got, full), q
+        ref = _oracle_batch(inp, L, B)
+        _close(full.cpu().numpy(), ref, f"fused exchange B={B}")
+    finally:
+        for b in bufs:
+            b.free()
+
+
+def test_peer_wait_gives_up_and_reports():
+    """A flag that nothing sets: the wait ends after its bound (2 s), stores 1 to the status word,
+    does not advance the counter, and the context stays usable."""
+    from latent_attn import _C
+    buf = _C.IpcBuffer(4096, torch.device("cuda", 0))
+    try:
+        flags = buf.view(torch.int32, 4)
+        epoch = torch.zeros(1, dtype=torch.int32, device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        _C.peer_wait(flags, epoch, False, status)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 1 and int(epoch.item()) == 0
+        x = torch.arange(10, device="cuda")
+        assert int(x.sum().item()) == 45
+    finally:
+        buf.free()
+
+
+def _two_rank_worker(rank, world, port, L, seed, B, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     from datetime import timedelta
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
-        _, outs = _decode_rank(rank, world, L, seed)
+        _, ref = _decode_rank(rank, world, L, seed, "nccl", B)
+        _, outs = _decode_rank(rank, world, L, seed, "p2p", B, graph=True)
+        for o in outs:              # same kernels and merge order: the exchanges agree bit for bit
+            np.testing.assert_array_equal(o, ref[-1])
         q.put((rank, outs[-1]))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_kv_range_decoder_two_ranks():
-    L, seed = 20011, 4                          # odd length: ranks hold 10005 and 10006 rows
+@pytest.mark.parametrize("L,B", [(20011, 1), (3001, 3)])
+def test_kv_range_decoder_two_ranks(L, B):
+    seed = 4                                    # odd lengths: the ranks' row counts differ by one
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = mp.start_processes(_two_rank_worker, args=(2, port, L, seed, q), nprocs=2, join=False,
+    procs = mp.start_processes(_two_rank_worker, args=(2, port, L, seed, B, q), nprocs=2, join=False,
                                start_method="spawn")
     got = {}
     try:
@@ -99,8 +287,8 @@ def test_kv_range_decoder_two_ranks():
                 for p in procs.processes:
                     p.kill()
                 pytest.fail("ranks did not finish")
-    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[L], seed=seed)
-    ref = _oracle(inp, L)
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[L] * B, seed=seed)
+    ref = _oracle_batch(inp, L, B)
     for r in range(2):
         _close(got[r], ref, f"rank {r}")
     np.testing.assert_array_equal(got[0], got[1])
