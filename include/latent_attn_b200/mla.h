@@ -297,6 +297,24 @@ MLA_API mla_status_t mla_combine_partials_put(const mla_config_t* cfg, mla_dtype
                                               int heads, const float* packed, const void* W_UV_slice, int world,
                                               void* const* dst, size_t dst_offset, size_t dst_pitch,
                                               const mla_peer_signal_t* signal, float* scratch, mla_stream_t stream);
+/* The gathered exchange for small batches (batch 1 .. 4, the long-sequence case): every rank
+ * receives every rank's partials of all heads and merges them itself, so one exchange replaces the
+ * all-to-all and the output all-gather. mla_decode_partial_gather stores this rank's (batch, H)
+ * packed rows [m, l, 0, 0, o] (rows ordered (token, head), kv_lora_rank + 4 floats each) at
+ * dst[q] + dst_offset + ((*epoch + 1) & 1) * parity_bytes for every q < world, then signals every
+ * receiver: the receive area is double-buffered by the step's flag value, so a rank may run one
+ * step ahead of a slower peer without overwriting what that peer is still merging.
+ * mla_combine_partials_gathered merges num_parts sets (num_parts, batch, H, kv_lora_rank + 4) at
+ * packed + (*epoch & 1) * parity_bytes (after mla_peer_wait with advance has moved *epoch to the
+ * step's flag value) and projects with W_UV into output (batch, H, v_head_dim) fp32. */
+MLA_API mla_status_t mla_decode_partial_gather(const mla_config_t* cfg, const mla_decode_args_t* args, int world,
+                                               void* const* dst, size_t dst_offset, size_t parity_bytes,
+                                               const mla_peer_signal_t* signal, void* workspace,
+                                               size_t workspace_bytes, mla_stream_t stream);
+MLA_API mla_status_t mla_combine_partials_gathered(const mla_config_t* cfg, mla_dtype_t dtype, int batch,
+                                                   int num_parts, const float* packed, size_t parity_bytes,
+                                                   const int* epoch, const void* W_UV, float* output,
+                                                   mla_stream_t stream);
 /* Waits on the device (one small kernel, bounded: 2 s) until flags[i] >= *epoch + 1 for i < count,
  * with system-scope acquire ordering, so the kernels after it on the stream see the data the
  * peers stored before their flags; with advance != 0 it then increments *epoch (the last wait of

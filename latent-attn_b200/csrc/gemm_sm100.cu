@@ -602,7 +602,7 @@ template <typename T, typename R>
 __global__ void __launch_bounds__(32 * kGemvWarps, 1)
 project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
                     const R* __restrict__ rec_o, float* __restrict__ out, int parts, int ml_stride, int o_stride,
-                    const PeerRows rows) {
+                    const PeerRows rows, const int* parity_epoch, size_t parity_elems) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int dc = P.dc, dv = P.dv, B = P.B;   // dv == 128, dc % 64 == 0, dc <= 512, B <= kGemvMaxTok
@@ -625,6 +625,11 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
         tma_prefetch_desc(&tmap_w);
         mbar_arrive_expect_tx(w_full, static_cast<uint32_t>(nk * dv * 128));
         for (int j = 0; j < nk; ++j) tma_load_2d(smem_u32(wsm) + j * dv * 128, &tmap_w, w_full, 64 * j, h * dv);
+    }
+    if (parity_epoch) {   // gathered partial sets: the half of the receive area the last step filled
+        const size_t off = static_cast<size_t>(*parity_epoch & 1) * parity_elems;
+        rec_ml += off;
+        rec_o += off;
     }
     // ---- 1. merge
     const int status0 = gemv_merge<R>(P, rec_ml, rec_o, parts, ml_stride, o_stride, h, red, wml);
@@ -710,7 +715,8 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
 // head h for every token and writes [m (natural log), l, 0, 0, o] with o the latent sum at the
 // merged max, unnormalised (PartOut gives the place); a failed decode writes NaN into m and l.
 // With part.peer the rows go to their slice's receiver, which is signalled by the last of the
-// slice's H / slices blocks.
+// slice's H / slices blocks; with part.gather every rank receives every row, in the half of its
+// receive area that the step's flag value selects, and is signalled by the last block.
 template <typename T>
 __global__ void __launch_bounds__(32 * kGemvWarps, 1)
 export_gemv_kernel(const DecodePlan P, const float* __restrict__ rec_ml, const T* __restrict__ rec_o,
@@ -724,6 +730,7 @@ export_gemv_kernel(const DecodePlan P, const float* __restrict__ rec_ml, const T
     const int status0 = gemv_merge<T>(P, rec_ml, rec_o, 0, 2, dc, h, red, wml);
     __syncthreads();
     const bool failed = status0 != kStatusOk;
+    const size_t half = part.gather ? static_cast<size_t>((*sig.epoch + 1) & 1) * part.parity_bytes : 0;
     for (int i = threadIdx.x; i < B * (dc + 4); i += blockDim.x) {
         const int tt = i / (dc + 4), c = i % (dc + 4) - 4;
         float M = -INFINITY;
@@ -736,17 +743,23 @@ export_gemv_kernel(const DecodePlan P, const float* __restrict__ rec_ml, const T
                 if (c >= 0) o = fmaf(a, red[w * dc + c], o);
             }
         }
-        if (c >= 0) {
-            part.o_at(tt, h, B, P.H, dc)[c] = o;
-        } else if (c == -4 || c == -3) {
-            const float nan = __int_as_float(0x7fc00000);
-            const float v = c == -4 ? (L > 0.f ? M * kLn2 : -INFINITY) : L;
-            part.ml_at(tt, h, B, P.H, dc)[c + 4] = failed ? nan : v;
-        } else if (part.slices) {
-            part.ml_at(tt, h, B, P.H, dc)[c + 4] = 0.f;
+        float v = 0.f;   // the value of column c + 4 of the packed row ([m, l, 0, 0, o])
+        if (c >= 0) v = o;
+        else if (c == -4) v = failed ? __int_as_float(0x7fc00000) : (L > 0.f ? M * kLn2 : -INFINITY);
+        else if (c == -3) v = failed ? __int_as_float(0x7fc00000) : L;
+        if (part.gather) {
+            const long long r = (static_cast<long long>(tt) * P.H + h) * (dc + 4) + (c + 4);
+            for (int q = 0; q < part.gather; ++q)
+                reinterpret_cast<float*>(static_cast<unsigned char*>(part.peer[q]) + part.peer_offset + half)[r] = v;
+        } else if (c >= 0) {
+            part.o_at(tt, h, B, P.H, dc)[c] = v;
+        } else if (c <= -3 || part.slices) {   // m, l, and the packed row's padding
+            part.ml_at(tt, h, B, P.H, dc)[c + 4] = v;
         }
     }
-    if (part.to_peers()) {
+    if (part.gather) {
+        peer_block_done_all(sig, part.gather, gridDim.x);
+    } else if (part.to_peers()) {
         const int hs = P.H / part.slices;
         peer_block_done(sig, h / hs, static_cast<unsigned int>(hs));
     }
@@ -812,20 +825,21 @@ cudaError_t launch_absorb_sm100(const DecodePlan& P, const float* q_nope, const 
 template <typename T, typename R>
 cudaError_t launch_project_impl(const DecodePlan& P, const float* rec_ml, const R* rec_o, const T* W_UV,
                                 float* out, bool pdl, int parts, int ml_stride, int o_stride, const PeerRows& rows,
-                                cudaStream_t s) {
+                                cudaStream_t s, const int* parity_epoch = nullptr, size_t parity_elems = 0) {
     CUtensorMap tmap;
     if (!make_tmap_2d_16b(&tmap, W_UV, static_cast<uint64_t>(P.H) * P.dv, static_cast<uint64_t>(P.dc),
                           static_cast<uint64_t>(P.dc), static_cast<uint32_t>(P.dv), 64))
         return cudaErrorInvalidValue;
-    if (P.B <= gemv_max_tokens()) {
+    if (P.B <= gemv_max_tokens() || (parity_epoch && P.B <= kGemvMaxTok)) {
         const size_t smem = 1024 + gemv_smem_bytes(P.dc, P.dv);
         cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(project_gemv_kernel<T, R>), static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         e = launch_ex(project_gemv_kernel<T, R>, dim3(P.H), dim3(32 * kGemvWarps), smem, s, pdl, tmap, P, rec_ml, rec_o,
-                      out, parts, ml_stride, o_stride, rows);
+                      out, parts, ml_stride, o_stride, rows, parity_epoch, parity_elems);
         count_launches(1);
         return e != cudaSuccess ? e : cudaGetLastError();
     }
+    if (parity_epoch) return cudaErrorInvalidValue;   // gathered sets: B <= kGemvMaxTok only
     const int ntp = pad16(P.B < kProjTok ? P.B : kProjTok);
     const size_t smem = 1024 + proj::unit_smem_bytes(P.dc, P.dv, ntp) + 64;
     cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(project_sm100_kernel<T, R>), static_cast<int>(smem));
@@ -861,7 +875,8 @@ bool project_parts_sm100_supported(int H, int dc, int dv, int parts) {
 template <typename T>
 cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, const float* part_ml,
                                        const float* part_o, int ml_stride, int o_stride, const T* W_UV, float* out,
-                                       const PeerRows& rows, cudaStream_t s) {
+                                       const PeerRows& rows, cudaStream_t s, const int* parity_epoch,
+                                       size_t parity_elems) {
     if (!project_parts_sm100_supported(H, dc, dv, parts)) return cudaErrorInvalidValue;
     static std::mutex mu;
     static std::vector<int*> status_addr;  // per device
@@ -887,17 +902,18 @@ cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, 
     P.B = B;
     P.head_blocks = ceil_div(H, kGroupRows);
     P.status = status;
-    return launch_project_impl<T, float>(P, part_ml, part_o, W_UV, out, false, parts, ml_stride, o_stride, rows, s);
+    return launch_project_impl<T, float>(P, part_ml, part_o, W_UV, out, false, parts, ml_stride, o_stride, rows, s,
+                                         parity_epoch, parity_elems);
 }
 
-bool export_gemv_supported(const DecodePlan& P) {
-    return P.B >= 1 && P.B <= gemv_max_tokens() && P.dc % 64 == 0 && P.dc <= 512;
+bool export_gemv_supported(const DecodePlan& P, bool gather) {
+    return P.B >= 1 && P.B <= (gather ? kGemvMaxTok : gemv_max_tokens()) && P.dc % 64 == 0 && P.dc <= 512;
 }
 
 template <typename T>
 cudaError_t launch_export_gemv(const DecodePlan& P, const float* rec_ml, const T* rec_o, const PartOut& part,
                                const PeerSig& sig, bool pdl, cudaStream_t s) {
-    if (!export_gemv_supported(P)) return cudaErrorInvalidValue;
+    if (!export_gemv_supported(P, part.gather > 0)) return cudaErrorInvalidValue;
     const size_t smem = static_cast<size_t>(kGemvWarps) * P.dc * sizeof(float) + kGemvWarps * sizeof(float2);
     cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(export_gemv_kernel<T>), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
@@ -912,7 +928,8 @@ cudaError_t launch_export_gemv(const DecodePlan& P, const float* rec_ml, const T
     template cudaError_t launch_project_sm100<T>(const DecodePlan&, const float*, const T*, const T*, float*,       \
                                                  bool, cudaStream_t);                                             \
     template cudaError_t launch_project_parts_sm100<T>(int, int, int, int, int, const float*, const float*, int, int, \
-                                                       const T*, float*, const PeerRows&, cudaStream_t);           \
+                                                       const T*, float*, const PeerRows&, cudaStream_t,           \
+                                                       const int*, size_t);                                         \
     template cudaError_t launch_export_gemv<T>(const DecodePlan&, const float*, const T*, const PartOut&,         \
                                                const PeerSig&, bool, cudaStream_t);
 MLA_INST(__half)

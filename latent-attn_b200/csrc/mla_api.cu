@@ -329,8 +329,10 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
     }
     if (out && pl.use_gemm_project)
         e = mla::launch_project_sm100<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, true, s);
-    else if (!out && pl.use_gemm_project && mla::export_gemv_supported(d))
+    else if (!out && pl.use_gemm_project && mla::export_gemv_supported(d, part.gather > 0))
         e = mla::launch_export_gemv<T>(d, rec_ml, rec_o, part, sig, true, s);
+    else if (part.gather > 0)
+        return fail(MLA_ERR_UNSUPPORTED, "the gathered export needs the tensor-core path and batch <= 4");
     else
         e = mla::launch_combine<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, part, sig, s);
     if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
@@ -403,7 +405,8 @@ mla_status_t noalloc_scratch(void** out) {
 // for a put kernel).
 mla_status_t combine_impl(const mla_config_t* cfg, mla_dtype_t dtype, int batch, int num_parts, int heads,
                           const float* part_ml, const float* part_o, int ml_stride, int o_stride,
-                          const void* W_UV, float* output, cudaStream_t s, const mla::PeerRows& rows = mla::PeerRows{}) {
+                          const void* W_UV, float* output, cudaStream_t s, const mla::PeerRows& rows = mla::PeerRows{},
+                          const int* parity_epoch = nullptr, size_t parity_elems = 0) {
     mla_status_t st = validate_cfg(cfg);
     if (st != MLA_OK) return st;
     if (batch <= 0 || num_parts <= 0 || heads <= 0)
@@ -416,15 +419,20 @@ mla_status_t combine_impl(const mla_config_t* cfg, mla_dtype_t dtype, int batch,
     if (!device_info(&di)) return fail(MLA_ERR_CUDA, "no CUDA device");
     const int dc = cfg->kv_lora_rank, dv = cfg->v_head_dim;
     // tcgen05 merge + W_UV GEMM when the shape fits, else the CUDA-core combine
-    const bool gemm = di.major == 10 && env_gemm_enabled() && mla::project_parts_sm100_supported(heads, dc, dv, num_parts);
+    const bool gemm = di.major == 10 && (env_gemm_enabled() || parity_epoch) &&
+                      mla::project_parts_sm100_supported(heads, dc, dv, num_parts);
+    if (parity_epoch && (!gemm || batch > 4))
+        return fail(MLA_ERR_UNSUPPORTED, "gathered partial sets need an sm_100 GPU, batch <= 4, v_head_dim 128, "
+                                         "kv_lora_rank a multiple of 64 up to 512 and at most 128 parts");
     cudaError_t e;
     if (gemm && dtype == MLA_DTYPE_BF16)
         e = mla::launch_project_parts_sm100<__nv_bfloat16>(batch, heads, dc, dv, num_parts, part_ml, part_o, ml_stride,
                                                           o_stride, static_cast<const __nv_bfloat16*>(W_UV), output,
-                                                          rows, s);
+                                                          rows, s, parity_epoch, parity_elems);
     else if (gemm)
         e = mla::launch_project_parts_sm100<__half>(batch, heads, dc, dv, num_parts, part_ml, part_o, ml_stride, o_stride,
-                                                   static_cast<const __half*>(W_UV), output, rows, s);
+                                                   static_cast<const __half*>(W_UV), output, rows, s, parity_epoch,
+                                                   parity_elems);
     else {
         if (dtype == MLA_DTYPE_BF16)
             e = mla::launch_combine_parts<__nv_bfloat16>(batch, heads, dc, dv, num_parts, part_ml, part_o, ml_stride,
@@ -752,6 +760,37 @@ mla_status_t mla_combine_partials_put(const mla_config_t* cfg, mla_dtype_t dtype
     const mla::PeerRows rows{dst, dst_offset, dst_pitch, world, sig};
     return combine_impl(cfg, dtype, batch, num_parts, heads, packed, packed + 4, row, row, W_UV, scratch,
                         reinterpret_cast<cudaStream_t>(stream), rows);
+}
+
+mla_status_t mla_decode_partial_gather(const mla_config_t* cfg, const mla_decode_args_t* a, int world, void* const* dst,
+                                       size_t dst_offset, size_t parity_bytes, const mla_peer_signal_t* signal,
+                                       void* workspace, size_t workspace_bytes, mla_stream_t stream) {
+    mla_status_t st = validate_cfg(cfg);
+    if (st != MLA_OK) return st;
+    mla::PeerSig sig;
+    st = peer_sig(signal, &sig);
+    if (st != MLA_OK) return st;
+    if (!a) return fail(MLA_ERR_INVALID_ARGUMENT, "args is null");
+    if (!dst) return fail(MLA_ERR_INVALID_ARGUMENT, "dst is null");
+    if (world <= 0 || world > 512) return fail(MLA_ERR_INVALID_ARGUMENT, "world must be in [1, 512]");
+    if (a->batch < 1 || a->batch > 4) return fail(MLA_ERR_UNSUPPORTED, "the gathered export takes batch 1 .. 4");
+    if (dst_offset % 16 != 0 || parity_bytes % 16 != 0)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "dst_offset and parity_bytes must be multiples of 16 bytes");
+    mla::PartOut part{nullptr, nullptr, 0, dst, dst_offset, world, parity_bytes};
+    return decode_impl(cfg, a, workspace, workspace_bytes, nullptr, part, reinterpret_cast<cudaStream_t>(stream), 0, sig);
+}
+
+mla_status_t mla_combine_partials_gathered(const mla_config_t* cfg, mla_dtype_t dtype, int batch, int num_parts,
+                                           const float* packed, size_t parity_bytes, const int* epoch, const void* W_UV,
+                                           float* output, mla_stream_t stream) {
+    mla_status_t st = validate_cfg(cfg);
+    if (st != MLA_OK) return st;
+    if (!packed || !epoch) return fail(MLA_ERR_INVALID_ARGUMENT, "packed and epoch must be non-null");
+    if (reinterpret_cast<uintptr_t>(packed) % 16 != 0 || parity_bytes % 16 != 0)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "packed and parity_bytes must be 16-byte aligned");
+    const int row = cfg->kv_lora_rank + 4;
+    return combine_impl(cfg, dtype, batch, num_parts, cfg->num_heads, packed, packed + 4, row, row, W_UV, output,
+                        reinterpret_cast<cudaStream_t>(stream), mla::PeerRows{}, epoch, parity_bytes / sizeof(float));
 }
 
 mla_status_t mla_ipc_alloc(size_t bytes, void** ptr, void* handle) {

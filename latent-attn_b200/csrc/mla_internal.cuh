@@ -251,6 +251,8 @@ struct PeerSig {
 // - slices > 0: one packed row [m, l, 0, 0, o] of dc + 4 floats, rows grouped by head slice
 //   (H / slices heads a slice): at o + ((q B + b) hs + h % hs) (dc + 4) for q = h / hs, or, with
 //   peer != nullptr, in slice q's receiver: peer[q] + peer_offset bytes + (b hs + h % hs) rows.
+// - gather > 0 (GEMV export only): every rank q < gather receives every row, at peer[q] +
+//   peer_offset + half * parity_bytes bytes + (b H + h) rows, half = (step's flag value) & 1.
 // m is in natural-log units (-inf with l = 0 for an empty partial).
 struct PartOut {
     float* ml;
@@ -258,7 +260,9 @@ struct PartOut {
     int slices;
     void* const* peer;
     size_t peer_offset;
-    __host__ __device__ bool to_peers() const { return peer != nullptr; }
+    int gather;
+    size_t parity_bytes;
+    __host__ __device__ bool to_peers() const { return peer != nullptr; }   // slices > 0 with peer
     __device__ float* row(int b, int h, int B, int H, int dc) const {
         if (!slices) return nullptr;
         const int hs = H / slices, q = h / hs;
@@ -307,13 +311,16 @@ bool project_parts_sm100_supported(int H, int dc, int dv, int parts);
 // With rows.world > 0 the merged, projected rows also go to every rank (PeerRows); with
 // B <= gemv_max_tokens() the GEMV kernel stores them itself, otherwise `out` is staged and a put
 // kernel follows.
+// With parity_epoch the sets are read at part_ml / part_o + (*parity_epoch & 1) * parity_elems
+// (a double-buffered receive area; B <= 4, the GEMV kernel).
 template <typename T>
 cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, const float* part_ml,
                                        const float* part_o, int ml_stride, int o_stride, const T* W_UV, float* out,
-                                       const PeerRows& rows, cudaStream_t s);
+                                       const PeerRows& rows, cudaStream_t s, const int* parity_epoch = nullptr,
+                                       size_t parity_elems = 0);
 // Partial export of a decode's records (one merged partial per (b, h), see PartOut) by the
 // GEMV merge, for B <= gemv_max_tokens(); with part.peer, slice q's receiver is signalled.
-bool export_gemv_supported(const DecodePlan& P);
+bool export_gemv_supported(const DecodePlan& P, bool gather = false);
 template <typename T>
 cudaError_t launch_export_gemv(const DecodePlan& P, const float* rec_ml, const T* rec_o, const PartOut& part,
                                const PeerSig& sig, bool pdl, cudaStream_t s);

@@ -500,6 +500,58 @@ def mla_combine_partials_put(packed: torch.Tensor, W_UV_slice: torch.Tensor, d_m
         C.c_void_p(_stream(packed.device))))
 
 
+def mla_decode_partial_gather(kv_cache, q_rope, W_UV, rope_cos, rope_sin, d_model, kv_lora_rank, qk_nope_head_dim,
+                              qk_rope_head_dim, num_heads, v_head_dim, *, dst_ptrs: torch.Tensor, dst_offset: int,
+                              parity_bytes: int, signal: "PeerSignal", q_absorbed=None, q_nope=None, W_UK=None,
+                              kv_pos_offset: int = 0, softmax_scale: float = 0.0, workspace=None, kernel: int = 0,
+                              timer=None, rope_theta: float = 0.0) -> None:
+    """The gathered export (batch 1 .. 4): this rank's (B, H) packed partial rows land in every
+    rank's buffer at ``dst_ptrs[q] + dst_offset + ((epoch + 1) & 1) * parity_bytes``, written by
+    the export kernel itself; every rank is signalled."""
+    _check_half(kv_cache, "kv_cache")
+    _check_tables(rope_cos, rope_sin)
+    if dst_ptrs.dtype != torch.int64 or not dst_ptrs.is_cuda or dst_ptrs.dim() != 1:
+        raise RuntimeError("dst_ptrs must be a CUDA int64 vector of pointers")
+    if dst_ptrs.numel() != signal.world:
+        raise RuntimeError("dst_ptrs and the signal's flag pointers must have one entry per rank")
+    cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    B = q_rope.size(0)
+    L = kv_cache.size(0) // B
+    args = _decode_args(kv_cache.dtype, B, False, kv_cache, L, q_rope, W_UV, rope_cos, rope_sin, None,
+                        q_absorbed=q_absorbed, q_nope=None if q_absorbed is not None else q_nope,
+                        W_UK=None if q_absorbed is not None else W_UK, kv_pos_offset=kv_pos_offset,
+                        softmax_scale=softmax_scale, kernel=kernel, timer=timer, rope_theta=rope_theta)
+    ws = _workspace(cfg, args, kv_cache.device, workspace)
+    _lib.check(_lib.load().mla_decode_partial_gather(
+        C.byref(cfg), C.byref(args), int(dst_ptrs.numel()), C.c_void_p(dst_ptrs.data_ptr()), C.c_size_t(dst_offset),
+        C.c_size_t(parity_bytes), C.byref(signal.struct), C.c_void_p(ws.data_ptr()), C.c_size_t(ws.numel()),
+        C.c_void_p(_stream(kv_cache.device))))
+
+
+def mla_combine_partials_gathered(packed: torch.Tensor, parity_bytes: int, epoch: torch.Tensor, W_UV: torch.Tensor,
+                                  d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim,
+                                  *, parts: int, batch: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Merge the gathered sets (parts, batch, H, d_c + 4) at ``packed`` + ``(epoch & 1) *
+    parity_bytes`` and project with W_UV -> (batch, H, dv) fp32."""
+    _check_f32(packed, "packed")
+    _check_half(W_UV, "W_UV")
+    if epoch.dtype != torch.int32 or not epoch.is_cuda:
+        raise RuntimeError("epoch must be a CUDA int32 tensor")
+    need = (parity_bytes + parts * batch * num_heads * (kv_lora_rank + 4) * 4) // 4
+    if packed.numel() < need:
+        raise RuntimeError("packed is smaller than two halves of the gathered sets")
+    cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    if out is None:
+        out = torch.empty(batch, num_heads, v_head_dim, dtype=torch.float32, device=packed.device)
+    elif tuple(out.shape) != (batch, num_heads, v_head_dim) or out.dtype != torch.float32 or not out.is_contiguous():
+        raise RuntimeError(f"out must be a contiguous float32 tensor of shape ({batch}, {num_heads}, {v_head_dim})")
+    _lib.check(_lib.load().mla_combine_partials_gathered(
+        C.byref(cfg), _DT[W_UV.dtype], int(batch), int(parts), C.c_void_p(packed.data_ptr()), C.c_size_t(parity_bytes),
+        C.c_void_p(epoch.data_ptr()), C.c_void_p(W_UV.data_ptr()), C.c_void_p(out.data_ptr()),
+        C.c_void_p(_stream(packed.device))))
+    return out
+
+
 def mla_combine_partials(part_ml: torch.Tensor, part_o: torch.Tensor, W_UV: torch.Tensor, d_model,
                          kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim,
                          out: Optional[torch.Tensor] = None) -> torch.Tensor:

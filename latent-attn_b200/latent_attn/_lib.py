@@ -107,6 +107,11 @@ SIGNATURES = {
     "mla_combine_partials_put": (C.c_int, [C.POINTER(MlaConfig), C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                            C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_size_t,
                                            C.POINTER(MlaPeerSignal), C.c_void_p, C.c_void_p]),
+    "mla_decode_partial_gather": (C.c_int, [C.POINTER(MlaConfig), C.POINTER(MlaDecodeArgs), C.c_int, C.c_void_p,
+                                            C.c_size_t, C.c_size_t, C.POINTER(MlaPeerSignal), C.c_void_p, C.c_size_t,
+                                            C.c_void_p]),
+    "mla_combine_partials_gathered": (C.c_int, [C.POINTER(MlaConfig), C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                                C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "mla_peer_wait": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "mla_timer_create": (C.c_int, [C.POINTER(C.c_void_p)]),
     "mla_timer_destroy": (C.c_int, [C.c_void_p]),

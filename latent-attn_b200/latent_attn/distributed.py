@@ -25,15 +25,22 @@ rank (about 0.25 MiB for one DeepSeek-V2 token), the output all-gather
 the heads. With a head count the ranks do not divide, the partials are
 all-gathered instead and every rank merges all of them (``gather_partials``).
 
-The two exchanges run either through NCCL (``exchange="nccl"``) or inside the
+The exchanges run either through NCCL (``exchange="nccl"``) or inside the
 library's own kernels (``exchange="p2p"``, the default): every rank maps the
-others' buffers (CUDA IPC, ``PeerExchange``); the kernel that exports the
-partials stores each head slice straight into its owner's receive area over
-NVLink (``mla_decode_partial_put``) and flags it, a bounded wait kernel on the
-receiver orders the merge after the flags, and the merge kernel stores its
-128-wide outputs into every rank's output area the same way
-(``mla_combine_partials_put``). Flags carry a device-resident step counter, so
-the exchange can be captured in a CUDA graph and replayed.
+others' buffers (CUDA IPC, ``PeerExchange``) and the kernels store into them
+over NVLink, flag their receivers, and a bounded wait kernel orders the next
+kernel after the flags. Flags carry a device-resident step counter, so the
+exchange can be captured in a CUDA graph and replayed.
+
+* Batches up to ``GATHER_MAX_BATCH`` (the long-sequence case) take one exchange:
+  the export kernel stores this rank's partials of every head into every rank's
+  receive area (``mla_decode_partial_gather``, double-buffered by the step
+  counter) and every rank merges and projects all heads itself
+  (``mla_combine_partials_gathered``). The merge of a token costs the same for
+  64 or 128 heads (one block per head), so the output all-gather is saved.
+* Larger batches keep the head-sliced pair: ``mla_decode_partial_put`` stores
+  each head slice into its owner's receive area, and ``mla_combine_partials_put``
+  stores the merged rows into every rank's output area.
 """
 
 from __future__ import annotations
@@ -138,31 +145,38 @@ def gather_head_slices(o_slice: torch.Tensor, group=None, out: Optional[torch.Te
     return out
 
 
+# Largest batch the gathered exchange takes (the GEMV merge kernels' limit).
+GATHER_MAX_BATCH = 4
+
+
 def _blocks_for(nbytes: int) -> int:
     """Thread blocks a put kernel gives one destination: one per 16 KiB, 1 to 32."""
     return max(1, min(32, -(-nbytes // 16384)))
 
 
 class PeerExchange:
-    """Peer-memory buffers of a head-sliced exchange on the ranks of one node.
+    """Peer-memory buffers of the KV-range exchange on the ranks of one node.
 
     Every rank allocates one IPC buffer holding the flag words of the two exchanges (one word per
-    sender for each), the receive area of the partials (world blocks of ``slice_bytes``) and the
-    output area (``out_bytes``); the handles are all-gathered once and every rank maps every
-    peer's buffer. ``sig_partials`` / ``sig_outputs`` describe how this rank's kernels signal
-    the receivers of each exchange (flag word ``rank`` or ``world + rank``); the matching waits
-    are ``wait_partials`` and ``wait_outputs`` (the latter ends the step). ``close()`` is a
-    collective (unmap everywhere, barrier, free)."""
+    sender for each), the receive area of the partials (``halves`` copies of world blocks of
+    ``slice_bytes``; two halves double-buffer it by the step's flag value) and the output area
+    (``out_bytes``); the handles are all-gathered once and every rank maps every peer's buffer.
+    ``sig_partials`` / ``sig_outputs`` describe how this rank's kernels signal the receivers of
+    each exchange (flag word ``rank`` or ``world + rank``); the matching waits are
+    ``wait_partials`` and ``wait_outputs``, and the step's last wait advances the step counter.
+    ``close()`` is a collective (unmap everywhere, barrier, free)."""
 
-    def __init__(self, slice_bytes: int, out_bytes: int, device: torch.device, group=None):
+    def __init__(self, slice_bytes: int, out_bytes: int, device: torch.device, group=None, halves: int = 1):
         from latent_attn import _C
         self.group, self.device = group, device
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.slice_bytes, self.out_bytes = slice_bytes, out_bytes
+        self.parity_bytes = -(-self.world * slice_bytes // 256) * 256   # one half of the receive area
+        self.halves = halves
         self.flag_bytes = -(-2 * self.world * 4 // 256) * 256
         self.recv_off = self.flag_bytes
-        self.out_off = self.recv_off + -(-self.world * slice_bytes // 256) * 256
+        self.out_off = self.recv_off + halves * self.parity_bytes
         total = self.out_off + -(-out_bytes // 256) * 256
         self.buf = _C.IpcBuffer(total, device)
         handles = [None] * self.world
@@ -194,15 +208,17 @@ class PeerExchange:
                                          self.counters[self.world:])
 
     def recv(self, dtype=torch.float32) -> torch.Tensor:
-        return self.buf.view(dtype, self.world * self.slice_bytes // 4, self.recv_off)
+        """The receive area: every half (``halves * parity_bytes`` bytes) as one flat tensor."""
+        return self.buf.view(dtype, self.halves * self.parity_bytes // 4, self.recv_off)
 
     def out(self, dtype=torch.float32) -> torch.Tensor:
         return self.buf.view(dtype, self.out_bytes // 4, self.out_off)
 
-    def wait_partials(self) -> None:
-        """Orders the stream after every rank's partials for this rank have landed."""
+    def wait_partials(self, advance: bool = False) -> None:
+        """Orders the stream after every rank's partials for this rank have landed; with
+        ``advance`` it ends the step (the gathered exchange has no second half)."""
         from latent_attn import _C
-        _C.peer_wait(self.flags[:self.world], self.epoch, False, self.status)
+        _C.peer_wait(self.flags[:self.world], self.epoch, advance, self.status)
 
     def wait_outputs(self) -> None:
         """Orders the stream after every rank's outputs have landed; ends the exchange step."""
@@ -278,14 +294,17 @@ class KVRangeDecoder:
             self._buf[name] = t
         return t
 
-    def _peers(self, B, hs, world, device) -> PeerExchange:
+    def _peers(self, B, hs, world, device, gather) -> PeerExchange:
         c = self.cfg
-        key = (B, hs, world, device)
+        key = (B, hs, world, device, gather)
         if self._peer_key != key:
             if self._peer is not None:
                 self._peer.close()
             R = c.kv_lora_rank + 4
-            self._peer = PeerExchange(B * hs * R * 4, B * world * hs * c.v_head_dim * 4, device, self.group)
+            if gather:   # every rank's (B, H) rows, double-buffered; no output area
+                self._peer = PeerExchange(B * c.num_heads * R * 4, 0, device, self.group, halves=2)
+            else:
+                self._peer = PeerExchange(B * hs * R * 4, B * world * hs * c.v_head_dim * 4, device, self.group)
             self._peer_key = key
         return self._peer
 
@@ -309,19 +328,32 @@ class KVRangeDecoder:
         world = dist.get_world_size(self.group)
         rank = dist.get_rank(self.group)
         B, H, dc, dv = q_rope.size(0), c.num_heads, c.kv_lora_rank, c.v_head_dim
+        if self.exchange == "p2p" and B <= GATHER_MAX_BATCH:
+            # one exchange: the export kernel stores this rank's partials of every head into every
+            # rank's receive area (NVLink stores), and every rank merges and projects all heads
+            px = self._peers(B, H, world, q_rope.device, True)
+            _C.mla_decode_partial_gather(kv_local, q_rope, W_UV, rope_cos, rope_sin, *dims, dst_ptrs=px.recv_ptrs,
+                                         dst_offset=rank * px.slice_bytes, parity_bytes=px.parity_bytes,
+                                         signal=px.sig_partials, q_absorbed=q_absorbed, q_nope=q_nope, W_UK=W_UK,
+                                         kv_pos_offset=pos_offset, workspace=workspace, timer=timer)
+            px.wait_partials(advance=True)
+            if out is None:
+                out = self._get("full", (B, H, dv), q_rope)
+            return _C.mla_combine_partials_gathered(px.recv(), px.parity_bytes, px.epoch, W_UV, *dims, parts=world,
+                                                    batch=B, out=out)
         if H % world == 0:
             hs = H // world
             W_slice = W_UV[rank * hs * dv:(rank + 1) * hs * dv]
             if self.exchange == "p2p":
                 # the export kernel stores each head slice into its owner's receive area, the merge
                 # kernel stores the merged rows into every rank's output area (NVLink stores)
-                px = self._peers(B, hs, world, q_rope.device)
+                px = self._peers(B, hs, world, q_rope.device, False)
                 _C.mla_decode_partial_put(kv_local, q_rope, W_UV, rope_cos, rope_sin, *dims, dst_ptrs=px.recv_ptrs,
                                           dst_offset=rank * px.slice_bytes, signal=px.sig_partials,
                                           q_absorbed=q_absorbed, q_nope=q_nope, W_UK=W_UK, kv_pos_offset=pos_offset,
                                           workspace=workspace, timer=timer)
                 px.wait_partials()
-                recv = px.recv().view(world, B, hs, dc + 4)
+                recv = px.recv()[:world * B * hs * (dc + 4)].view(world, B, hs, dc + 4)
                 _C.mla_combine_partials_put(recv, W_slice, *dims, dst_ptrs=px.out_ptrs, dst_offset=rank * hs * dv * 4,
                                             dst_pitch=H * dv * 4, signal=px.sig_outputs,
                                             scratch=self._get("slice", (B, hs, dv), q_rope))
@@ -347,4 +379,4 @@ class KVRangeDecoder:
 
 
 __all__ = ["lpt_shard", "kv_range", "gather_partials", "packed_row", "exchange_head_slices", "gather_head_slices",
-           "PeerExchange", "KVRangeDecoder"]
+           "GATHER_MAX_BATCH", "PeerExchange", "KVRangeDecoder"]

@@ -229,6 +229,77 @@ def test_fused_exchange_kernels_two_emulated_ranks_on_one_gpu(B):
             b.free()
 
 
+@pytest.mark.parametrize("B", [1, 3])
+def test_gathered_exchange_two_emulated_ranks_on_one_gpu(B):
+    """The gathered exchange (batch <= 4) with two emulated ranks on one GPU, three steps: the export
+    (mla_decode_partial_gather) must put exactly the rows mla_decode_partial_packed gives (one
+    slice) into block r of every receiver, in the half of the receive area the step's flag value
+    selects (the other half, zeroed before the step, stays zero); the merge of all heads
+    (mla_combine_partials_gathered) reads that half and must be bit-identical on both receivers and
+    to mla_combine_partials_packed over the same sets, and within the decode tolerance of the
+    oracle."""
+    from latent_attn import _C
+    world, L, H, dc, dv = 2, 2501, 128, 512, 128
+    cfg = MLAConfig.deepseek_v2()
+    dims = (cfg.d_model, 512, 128, 64, 128, 128)
+    dev = torch.device("cuda", 0)
+    inp = synthetic.baseline_inputs(num_heads=H, seq_lens=[L] * B, seed=13)
+    W_UV = inp.W_UV.to(dev)
+    qn, qr, WK = inp.q_nope.float().to(dev), inp.q_rope.float().to(dev), inp.W_UK.to(dev)
+    shards = []
+    for r in range(world):
+        lo, hi = kv_range(L, world, r)
+        shards.append((lo, torch.cat([inp.kv_cache[b * L + lo:b * L + hi] for b in range(B)]).contiguous().to(dev)))
+    # on-the-fly RoPE (no tables), as the benchmark runs it
+    sets = torch.cat([_C.mla_decode_partial_packed(kv, qr, W_UV, None, None, *dims, num_slices=1, q_nope=qn, W_UK=WK,
+                                                   kv_pos_offset=lo) for lo, kv in shards])   # (world, B, H, dc + 4)
+    want = _C.mla_combine_partials_packed(sets, W_UV, *dims)
+    set_bytes = B * H * (dc + 4) * 4
+    parity = world * set_bytes
+    recv_off = 256
+    bufs = [_C.IpcBuffer(recv_off + 2 * parity, dev) for _ in range(world)]
+    try:
+        flag_ptrs = _ptrs([b.ptr for b in bufs])
+        epochs = [torch.zeros(1, dtype=torch.int32, device=dev) for _ in range(world)]
+        counters = [torch.zeros(2 * world, dtype=torch.int32, device=dev) for _ in range(world)]
+        sigs = [_signals(flag_ptrs, world, r, epochs[r], counters[r]) for r in range(world)]
+        flags = [b.view(torch.int32, 2 * world) for b in bufs]
+        recvs = [b.view(torch.float32, 2 * parity // 4, recv_off) for b in bufs]
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        for step in range(3):
+            for q in range(world):
+                recvs[q].zero_()
+            for r, (lo, kv) in enumerate(shards):
+                _C.mla_decode_partial_gather(kv, qr, W_UV, None, None, *dims, dst_ptrs=flag_ptrs + recv_off,
+                                             dst_offset=r * set_bytes, parity_bytes=parity, signal=sigs[r][0],
+                                             q_nope=qn, W_UK=WK, kv_pos_offset=lo)
+            for q in range(world):
+                _C.peer_wait(flags[q][:world], epochs[q], True, status)
+            outs = [_C.mla_combine_partials_gathered(recvs[q], parity, epochs[q], W_UV, *dims, parts=world, batch=B)
+                    for q in range(world)]
+            torch.cuda.synchronize()
+            assert int(status.item()) == 0
+            half = (step + 1) & 1
+            for q in range(world):
+                assert int(epochs[q].item()) == step + 1 and torch.all(flags[q][:world] == step + 1)
+                assert torch.all(counters[q] == 0)
+                halves = recvs[q].view(2, world, B, H, dc + 4)
+                assert torch.equal(halves[half], sets), (step, q)
+                assert not torch.any(halves[1 - half] != 0), (step, q)
+                assert torch.equal(outs[q], want), (step, q)
+        cos, sin = O.rope_tables_otf(L, 64)
+        ref = []
+        for b in range(B):
+            q_abs = O.absorb_query(inp.q_nope[b].float().numpy(), inp.W_UK.float().numpy(), 128, 512)
+            ref.append(O.absorbed_decode(inp.kv_cache[b * L:(b + 1) * L].float().numpy(), q_abs,
+                                         inp.q_rope[b].float().numpy(), inp.W_UV.float().numpy(), cos, sin,
+                                         128, 512, 128, 64, 128))
+        _close(want.cpu().numpy(), np.stack(ref), f"gathered exchange B={B}")
+    finally:
+        for b in bufs:
+            b.free()
+
+
 def test_peer_wait_gives_up_and_reports():
     """A flag that nothing sets: the wait ends after its bound (2 s), stores 1 to the status word,
     does not advance the counter, and the context stays usable."""
@@ -264,7 +335,7 @@ def _two_rank_worker(rank, world, port, L, seed, B, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("L,B", [(20011, 1), (3001, 3)])
+@pytest.mark.parametrize("L,B", [(20011, 1), (3001, 3), (1501, 5)])
 def test_kv_range_decoder_two_ranks(L, B):
     seed = 4                                    # odd lengths: the ranks' row counts differ by one
     with socket.socket() as s:
