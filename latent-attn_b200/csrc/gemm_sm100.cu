@@ -627,6 +627,7 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
         for (int j = 0; j < nk; ++j) tma_load_2d(smem_u32(wsm) + j * dv * 128, &tmap_w, w_full, 64 * j, h * dv);
     }
     if (parity_epoch) {   // gathered partial sets: the half of the receive area the last step filled
+        pdl_wait();       // the wait kernel before this one sets the step counter
         const size_t off = static_cast<size_t>(*parity_epoch & 1) * parity_elems;
         rec_ml += off;
         rec_o += off;
@@ -902,8 +903,10 @@ cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, 
     P.B = B;
     P.head_blocks = ceil_div(H, kGroupRows);
     P.status = status;
-    return launch_project_impl<T, float>(P, part_ml, part_o, W_UV, out, false, parts, ml_stride, o_stride, rows, s,
-                                         parity_epoch, parity_elems);
+    // gathered sets follow the exchange's wait kernel, which lets this kernel start (and stream its
+    // W_UV rows) while it waits
+    return launch_project_impl<T, float>(P, part_ml, part_o, W_UV, out, parity_epoch != nullptr, parts, ml_stride,
+                                         o_stride, rows, s, parity_epoch, parity_elems);
 }
 
 bool export_gemv_supported(const DecodePlan& P, bool gather) {

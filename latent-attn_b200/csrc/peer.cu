@@ -48,7 +48,12 @@ __global__ void __launch_bounds__(256) peer_put_kernel(const unsigned char* src,
 
 constexpr unsigned long long kPeerWaitNs = 2000000000ull;   // 2 s
 
+// Launched with programmatic dependent launch: it lets the next kernel start at once (that
+// kernel's own griddepcontrol.wait holds it until this one ends, so it can prefetch its weights
+// meanwhile), and waits for the previous kernel before advancing the step counter, which that
+// kernel may still read.
 __global__ void peer_wait_kernel(const int* flags, int count, int* epoch, int advance, int* status) {
+    sm100::pdl_launch_dependents();
     const int target = *epoch + 1;
     bool ok = true;
     for (int i = threadIdx.x; i < count; i += blockDim.x) {
@@ -61,8 +66,9 @@ __global__ void peer_wait_kernel(const int* flags, int count, int* epoch, int ad
         }
     }
     if (!ok && status) atomicExch(status, 1);
-    __syncthreads();   // every thread read *epoch before it advances
-    if (advance && threadIdx.x == 0) *epoch = target;
+    sm100::pdl_wait();
+    ok = __syncthreads_and(ok);   // also: every thread read *epoch before it advances
+    if (advance && ok && threadIdx.x == 0) *epoch = target;
 }
 
 }  // namespace
@@ -98,9 +104,18 @@ cudaError_t launch_peer_put(const void* src, size_t rows, size_t row_bytes, size
 }
 
 cudaError_t launch_peer_wait(const int* flags, int count, int* epoch, int advance, int* status, cudaStream_t s) {
-    peer_wait_kernel<<<1, 32, 0, s>>>(flags, count, epoch, advance, status);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, peer_wait_kernel, flags, count, epoch, advance, status);
     count_launches(1);
-    return cudaGetLastError();
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace mla

@@ -4,9 +4,10 @@
 // A sender's kernel stores its rows into receiver q's buffer with plain stores (NVLink when q is
 // another GPU), and once every block bound for q has stored its part, the last of them sets
 // receiver q's flag word `flag_index` to *epoch + 1 with a system-scope release store. Blocks
-// count themselves per receiver in `counters` (this GPU's memory, zero between steps): each block
-// fences at system scope after its stores, then one thread adds 1; the block that completes the
-// count resets it, fences again and releases the flag. The receiver's wait kernel spins (bounded)
+// count themselves per receiver in `counters` (this GPU's memory, zero between steps): after a
+// block barrier, one thread per receiver issues a system-scope acq_rel fence (cumulative over the
+// block's stores through the barrier) and adds 1; the block that completes the count resets it,
+// fences again and releases the flag (one fence per block and receiver, not one per thread). The receiver's wait kernel spins (bounded)
 // on ld.acquire.sys until every sender's word reaches *epoch + 1; its last wait of a step
 // advances *epoch, so a replayed CUDA graph carries a new value each time.
 #pragma once
@@ -26,12 +27,17 @@ __device__ __forceinline__ void peer_st_release(int* p, int v) {
     asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// One thread's count for receiver q; the block that completes it releases q's flag.
+__device__ __forceinline__ void peer_fence() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// One thread's count for receiver q, after a block barrier that orders the block's stores before
+// it: the fence makes the count a release of those stores; the block that completes the count
+// fences again (acquiring the other blocks' counts) and releases q's flag.
 __device__ __forceinline__ void peer_count(const PeerSig& s, int q, unsigned int expected) {
+    peer_fence();
     const unsigned int prev = atomicAdd(s.counters + q, 1u);
     if (prev + 1u == expected) {
         s.counters[q] = 0u;   // the next step's kernel starts after this one ends
-        __threadfence_system();
+        peer_fence();
         peer_st_release(s.flags[q] + s.flag_index, *s.epoch + 1);
     }
 }
@@ -39,14 +45,12 @@ __device__ __forceinline__ void peer_count(const PeerSig& s, int q, unsigned int
 // Called by every thread of a block once its stores bound for receiver q are issued; `expected`
 // blocks of the kernel send to q.
 __device__ __forceinline__ void peer_block_done(const PeerSig& s, int q, unsigned int expected) {
-    __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) peer_count(s, q, expected);
 }
 
 // As peer_block_done for a block that stored into every receiver q < world (world <= blockDim.x).
 __device__ __forceinline__ void peer_block_done_all(const PeerSig& s, int world, unsigned int expected) {
-    __threadfence_system();
     __syncthreads();
     if (static_cast<int>(threadIdx.x) < world) peer_count(s, threadIdx.x, expected);
 }
