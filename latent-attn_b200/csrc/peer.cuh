@@ -5,9 +5,8 @@
 // another GPU), and once every block bound for q has stored its part, the last of them sets
 // receiver q's flag word `flag_index` to *epoch + 1 with a system-scope release store. Blocks
 // count themselves per receiver in `counters` (this GPU's memory, zero between steps): after a
-// block barrier, one thread per receiver issues a system-scope acq_rel fence (cumulative over the
-// block's stores through the barrier) and adds 1; the block that completes the count resets it,
-// fences again and releases the flag (one fence per block and receiver, not one per thread). The receiver's wait kernel spins (bounded)
+// block barrier, one thread per receiver fences at GPU scope and adds 1; the block that completes
+// the count resets it, fences at system scope and releases the flag (see peer_count). The receiver's wait kernel spins (bounded)
 // on ld.acquire.sys until every sender's word reaches *epoch + 1; its last wait of a step
 // advances *epoch, so a replayed CUDA graph carries a new value each time.
 #pragma once
@@ -27,17 +26,22 @@ __device__ __forceinline__ void peer_st_release(int* p, int v) {
     asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-__device__ __forceinline__ void peer_fence() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void peer_fence_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void peer_fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 // One thread's count for receiver q, after a block barrier that orders the block's stores before
-// it: the fence makes the count a release of those stores; the block that completes the count
-// fences again (acquiring the other blocks' counts) and releases q's flag.
+// it. The GPU-scope fence makes the count a release of those stores to the other blocks of this
+// GPU (the barrier makes it cumulative over the whole block); the block that completes the count
+// acquires every other block's release through the counter, and its system-scope fence and
+// release store carry all of them (causality order is transitive across the two scopes) to the
+// receiver's acquire. One system-scope fence per receiver per kernel: a system fence in every
+// block stalled the export kernel on membar for several microseconds.
 __device__ __forceinline__ void peer_count(const PeerSig& s, int q, unsigned int expected) {
-    peer_fence();
+    peer_fence_gpu();
     const unsigned int prev = atomicAdd(s.counters + q, 1u);
     if (prev + 1u == expected) {
         s.counters[q] = 0u;   // the next step's kernel starts after this one ends
-        peer_fence();
+        peer_fence_sys();
         peer_st_release(s.flags[q] + s.flag_index, *s.epoch + 1);
     }
 }
