@@ -318,7 +318,7 @@ def test_peer_wait_gives_up_and_reports():
         buf.free()
 
 
-def _two_rank_worker(rank, world, port, L, seed, B, q):
+def _rank_worker(rank, world, port, L, seed, B, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     from datetime import timedelta
@@ -334,20 +334,19 @@ def _two_rank_worker(rank, world, port, L, seed, B, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("L,B", [(20011, 1), (3001, 3), (1501, 5)])
-def test_kv_range_decoder_two_ranks(L, B):
-    seed = 4                                    # odd lengths: the ranks' row counts differ by one
+def _run_ranks(world, L, B, seed=4):
+    """``world`` processes, one per GPU; returns every rank's output of the p2p decoder (each rank has
+    checked it bit-identical to the NCCL exchange)."""
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = mp.start_processes(_two_rank_worker, args=(2, port, L, seed, B, q), nprocs=2, join=False,
+    procs = mp.start_processes(_rank_worker, args=(world, port, L, seed, B, q), nprocs=world, join=False,
                                start_method="spawn")
     got = {}
     try:
-        for _ in range(2):                       # read before joining: a full pipe would block the writers
+        for _ in range(world):                   # read before joining: a full pipe would block the writers
             r, o = q.get(timeout=300)
             got[r] = o
     finally:
@@ -358,8 +357,29 @@ def test_kv_range_decoder_two_ranks(L, B):
                 for p in procs.processes:
                     p.kill()
                 pytest.fail("ranks did not finish")
-    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[L] * B, seed=seed)
+    return got
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("L,B", [(20011, 1), (3001, 3), (1501, 5)])
+def test_kv_range_decoder_two_ranks(L, B):
+    got = _run_ranks(2, L, B)                   # odd lengths: the ranks' row counts differ by one
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[L] * B, seed=4)
     ref = _oracle_batch(inp, L, B)
     for r in range(2):
         _close(got[r], ref, f"rank {r}")
     np.testing.assert_array_equal(got[0], got[1])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 3, reason="needs three or more GPUs")
+@pytest.mark.parametrize("L,B", [(40003, 1), (2003, 5)])
+def test_kv_range_decoder_all_gpus(L, B):
+    """Every GPU of the box a rank (the gathered exchange at B = 1, head-sliced at B = 5 when the
+    ranks divide the heads, else the NCCL all-gather of whole partial sets)."""
+    world = torch.cuda.device_count()
+    got = _run_ranks(world, L, B)
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[L] * B, seed=4)
+    ref = _oracle_batch(inp, L, B)
+    for r in range(world):
+        _close(got[r], ref, f"rank {r} of {world}")
+        np.testing.assert_array_equal(got[0], got[r])
