@@ -46,6 +46,17 @@ def _check_f32(t: torch.Tensor, name: str) -> None:
         raise RuntimeError(f"{name} must be on CUDA")
 
 
+def _check_f32_io(t: torch.Tensor, name: str) -> None:
+    """A float32 query or output tensor: on the GPU, or in pinned host memory, which the kernels
+    read or write directly (CUDA maps pinned allocations into the device address space)."""
+    if t.dtype != torch.float32:
+        raise RuntimeError(f"{name} must be float32, got {t.dtype}")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    if not (t.is_cuda or t.is_pinned()):
+        raise RuntimeError(f"{name} must be on CUDA or in pinned host memory")
+
+
 def _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim):
     key = (int(d_model), int(kv_lora_rank), int(qk_nope_head_dim), int(qk_rope_head_dim), int(num_heads),
            int(v_head_dim))
@@ -299,7 +310,9 @@ def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
     """General decode: (B, H, dv) fp32 for B sequences (or B tokens over one shared cache).
 
     Give ``q_absorbed`` (B, H, d_c) fp32, or ``q_nope`` (B, H, dn) fp32 with ``W_UK``
-    (H*dn, d_c) for in-op absorption. ``seq_lens`` (B,) int32 and ``kv_offsets`` (B,)
+    (H*dn, d_c) for in-op absorption. The queries and ``out`` may be pinned host tensors: the
+    kernels then read the queries and store the output over the host link themselves, with no
+    copy launches (for small batches, where a copy's fixed latency exceeds the transfer). ``seq_lens`` (B,) int32 and ``kv_offsets`` (B,)
     int64 (device) describe a variable-length batch packed in ``kv_cache``; without
     them every sequence has ``max_seq_len`` rows at ``b * max_seq_len``. With ``page_table``
     (B, max_pages) int32 (device) the cache is paged: position p of sequence b is row
@@ -314,17 +327,17 @@ def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
     else:
         _check_half(kv_cache, "kv_cache")
     _check_half(W_UV, "W_UV")
-    _check_f32(q_rope, "q_rope")
+    _check_f32_io(q_rope, "q_rope")
     _check_tables(rope_cos, rope_sin)
     cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
     if q_absorbed is not None:
-        _check_f32(q_absorbed, "q_absorbed")
+        _check_f32_io(q_absorbed, "q_absorbed")
         q_nope = None
         W_UK = None
     else:
         if q_nope is None or W_UK is None:
             raise RuntimeError("give q_absorbed, or q_nope together with W_UK")
-        _check_f32(q_nope, "q_nope")
+        _check_f32_io(q_nope, "q_nope")
         _check_half(W_UK, "W_UK")
         if W_UK.dtype != kv_cache.dtype:
             raise RuntimeError("W_UK dtype must match kv_cache dtype")
@@ -353,6 +366,10 @@ def mla_decode(kv_cache: torch.Tensor, q_rope: torch.Tensor, W_UV: torch.Tensor,
         host_arr = (C.c_int * B)(*[int(x) for x in seq_lens_host])
     if out is None:
         out = torch.empty(B, num_heads, v_head_dim, dtype=torch.float32, device=kv_cache.device)
+    else:
+        _check_f32_io(out, "out")
+        if out.numel() != B * num_heads * v_head_dim:
+            raise RuntimeError(f"out must hold ({B}, {num_heads}, {v_head_dim}) floats")
     _run_decode(cfg, kv_cache.dtype, B, shared_cache, kv_cache, max_seq_len, q_rope, W_UV, rope_cos,
                 rope_sin, out, workspace=workspace, q_absorbed=q_absorbed, q_nope=q_nope, W_UK=W_UK,
                 seq_lens=seq_lens, kv_offsets=kv_offsets, seq_lens_host=host_arr,

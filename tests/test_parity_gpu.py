@@ -539,3 +539,21 @@ def test_small_batches_gemv_and_tensor_core_gemms(B, dtype):
                          max_seq_len=Lmax, kernel=kern).cpu().numpy()
         for b in range(B):
             assert_close(out[b], refs[b], f"B={B} {dtype} seq {b} (L={lens[b]}) kernel={kern}")
+
+
+@pytest.mark.parametrize("B", [1, 3])
+def test_pinned_host_queries_and_output(B):
+    """mla_decode given pinned host q_nope / q_rope and a pinned host output (the kernels read and
+    write them over the host link) returns exactly what it returns for device tensors."""
+    cfg = MLAConfig.deepseek_v2()
+    inp = synthetic.baseline_inputs(num_heads=128, seq_lens=[3000] * B, seed=21)
+    dev = torch.device("cuda", 0)
+    kv, W_UK, W_UV = inp.kv_cache.to(dev), inp.W_UK.to(dev), inp.W_UV.to(dev)
+    qn_d, qr_d = inp.q_nope.float().to(dev), inp.q_rope.float().to(dev)
+    want = mla_decode(kv, qr_d, W_UV, None, None, cfg, q_nope=qn_d, W_UK=W_UK)
+    qn_h, qr_h = inp.q_nope.float().pin_memory(), inp.q_rope.float().pin_memory()
+    out_h = torch.full((B, 128, 128), float("nan")).pin_memory()
+    got = mla_decode(kv, qr_h, W_UV, None, None, cfg, q_nope=qn_h, W_UK=W_UK, out=out_h)
+    torch.cuda.synchronize()
+    assert got is out_h
+    assert torch.equal(out_h, want.cpu())
