@@ -229,9 +229,9 @@ def test_fused_exchange_kernels_two_emulated_ranks_on_one_gpu(B):
             b.free()
 
 
-@pytest.mark.parametrize("B", [1, 3])
-def test_gathered_exchange_two_emulated_ranks_on_one_gpu(B):
-    """The gathered exchange (batch <= 4) with two emulated ranks on one GPU, three steps: the export
+@pytest.mark.parametrize("world,B", [(2, 1), (2, 3), (8, 1)])
+def test_gathered_exchange_emulated_ranks_on_one_gpu(world, B):
+    """The gathered exchange (batch <= 4) with 2 or 8 emulated ranks on one GPU, three steps: the export
     (mla_decode_partial_gather) must put exactly the rows mla_decode_partial_packed gives (one
     slice) into block r of every receiver, in the half of the receive area the step's flag value
     selects (the other half, zeroed before the step, stays zero); the merge of all heads
@@ -239,7 +239,7 @@ def test_gathered_exchange_two_emulated_ranks_on_one_gpu(B):
     to mla_combine_partials_packed over the same sets, and within the decode tolerance of the
     oracle."""
     from latent_attn import _C
-    world, L, H, dc, dv = 2, 2501, 128, 512, 128
+    L, H, dc, dv = 2501, 128, 512, 128
     cfg = MLAConfig.deepseek_v2()
     dims = (cfg.d_model, 512, 128, 64, 128, 128)
     dev = torch.device("cuda", 0)
