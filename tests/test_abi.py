@@ -117,6 +117,44 @@ def test_validation_without_gpu():
     assert lib.mla_version().startswith(b"latent-attn-b200")
 
 
+def test_peer_exchange_validation_without_gpu():
+    """The peer-memory entry points reject bad arguments before any device work."""
+    lib = _lib.load()
+    ok = _lib.MlaConfig(5120, 512, 128, 64, 128, 128)
+    fake = C.c_void_p(256)
+    sig = _lib.MlaPeerSignal(256, 0, 256, 256)
+    no_counters = _lib.MlaPeerSignal(256, 0, 256, None)
+    bad_index = _lib.MlaPeerSignal(256, -1, 256, 256)
+    put = lambda s, world=2, blocks=1, row=64, off=0: lib.mla_peer_put(fake, 1, row, row, row, fake, row, off, world,
+                                                                       blocks, C.byref(s) if s else None, None)
+    assert put(None) == _lib.MLA_ERR_INVALID_ARGUMENT and b"signal" in lib.mla_last_error()
+    assert put(no_counters) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert put(bad_index) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert put(sig, world=0) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert put(sig, blocks=0) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert put(sig, row=24) == _lib.MLA_ERR_INVALID_ARGUMENT and b"16 bytes" in lib.mla_last_error()
+    assert put(sig, off=8) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert lib.mla_peer_wait(None, 1, fake, 0, None, None) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert lib.mla_peer_wait(fake, 0, fake, 0, None, None) == _lib.MLA_ERR_INVALID_ARGUMENT
+    a = _lib.MlaDecodeArgs()
+    a.dtype, a.batch, a.max_seq_len = _lib.DTYPE_BF16, 5, 16
+    gather = lambda args, world=2, off=0, parity=1024, s=sig: lib.mla_decode_partial_gather(
+        C.byref(ok), C.byref(args), world, fake, off, parity, C.byref(s), fake, 1 << 20, None)
+    assert gather(a) == _lib.MLA_ERR_UNSUPPORTED and b"batch" in lib.mla_last_error()   # batch 5 > 4
+    a.batch = 1
+    assert gather(a, world=0) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert gather(a, parity=1000) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert gather(a, s=no_counters) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert lib.mla_decode_partial_put(C.byref(ok), C.byref(a), 3, fake, 0, C.byref(sig), fake, 1 << 20,
+                                      None) == _lib.MLA_ERR_INVALID_ARGUMENT              # 3 does not divide 128
+    assert lib.mla_combine_partials_gathered(C.byref(ok), _lib.DTYPE_BF16, 1, 2, fake, 1000, fake, fake, fake,
+                                             None) == _lib.MLA_ERR_INVALID_ARGUMENT        # parity not 16-aligned
+    assert lib.mla_combine_partials_gathered(C.byref(ok), _lib.DTYPE_BF16, 1, 2, fake, 1024, None, fake, fake,
+                                             None) == _lib.MLA_ERR_INVALID_ARGUMENT        # no step counter
+    assert lib.mla_combine_partials_put(C.byref(ok), _lib.DTYPE_BF16, 1, 2, 64, fake, fake, 2, fake, 0, 64,
+                                        C.byref(sig), fake, None) == _lib.MLA_ERR_INVALID_ARGUMENT  # pitch < row
+
+
 def test_cpp_drop_in_headers_compile():
     """A caller written against the reference's C++ API (tests/test_correctness.cu:186-198 style)
     compiles unchanged against include/latent_attn_b200/*.cuh."""
