@@ -315,6 +315,24 @@ MLA_API mla_status_t mla_combine_partials_gathered(const mla_config_t* cfg, mla_
                                                    int num_parts, const float* packed, size_t parity_bytes,
                                                    const int* epoch, const void* W_UV, float* output,
                                                    mla_stream_t stream);
+/* One rank's whole KV-range decode step for batch 1 .. 4, with the exchange inside one kernel:
+ * absorption, the decode of this rank's rows (args as for mla_decode, kv_pos_offset = the rows'
+ * first position, output (batch, H, v_head_dim) fp32 on this rank), then a kernel whose block h
+ * merges the rank's split-KV records of head h, stores the packed partial into every other rank's
+ * receive area (NVLink stores), reads every other rank's partial of head h from its own area, merges
+ * the world partials in rank order and projects them with W_UV. Each 16-byte store carries two
+ * values and the step number (*epoch + 1) beside each, so a reader waits (bounded, 2 s) on the data
+ * itself: no flag, no fence, no separate wait kernel.
+ * - recv: DEVICE array of world pointers to every rank's receive area (this rank's included),
+ *   2 x half_bytes each, zeroed once at setup; half_bytes >= world * batch * H * (kv_lora_rank + 4)
+ *   * 8, a multiple of 16. The two halves alternate by step, so a rank one step ahead never
+ *   overwrites rows a slower peer is still reading.
+ * - epoch, counter, status: device ints of this rank, zeroed at setup. The kernel advances *epoch
+ *   once per call; every rank must make the same sequence of calls. A wait that gives up sets
+ *   *status to 1 and that head's output to NaN. */
+MLA_API mla_status_t mla_decode_kv_range(const mla_config_t* cfg, const mla_decode_args_t* args, int world, int rank,
+                                         void* const* recv, size_t half_bytes, int* epoch, unsigned int* counter,
+                                         int* status, void* workspace, size_t workspace_bytes, mla_stream_t stream);
 /* Waits on the device (one small kernel, bounded: 2 s) until flags[i] >= *epoch + 1 for i < count,
  * with system-scope acquire ordering, so the kernels after it on the stream see the data the
  * peers stored before their flags; with advance != 0 it then increments *epoch (the last wait of

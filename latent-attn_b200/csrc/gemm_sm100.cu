@@ -598,6 +598,46 @@ __device__ __forceinline__ int gemv_merge(const DecodePlan& P, const float* __re
     return status0;
 }
 
+// Step 3 of the GEMV projection, shared by the projection kernels: thread (q, j) (4 quarters x dv
+// rows, 512 threads) dots W_UV row j (128-byte-swizzled boxes in shared memory) with quarter q of
+// every token's merged latent row olat[t], into qsum[q][t][j]; the caller sums the quarters in order.
+template <typename T>
+__device__ __forceinline__ void gemv_w_uv(const unsigned char* wsm, const float* olat, float* qsum, int B, int dc,
+                                          int dv, bool ok) {
+    const int q = threadIdx.x / dv, j = threadIdx.x % dv;   // 4 quarters x 128 rows
+    const int kq = dc / 4;                                   // elements per quarter, a multiple of 16
+    float acc[kGemvMaxTok] = {0.f, 0.f, 0.f, 0.f};
+    if (ok) {
+        for (int c = 0; c < kq / 8; ++c) {
+            const int k = q * kq + 8 * c;
+            // 128-byte-swizzled box row: 16-byte chunk ((k % 64) / 8) ^ (j % 8)
+            const uint4 wv = *reinterpret_cast<const uint4*>(wsm + (k >> 6) * (dv * 128) + j * 128 +
+                                                             ((((k & 63) >> 3) ^ (j & 7)) << 4));
+            using T2 = typename ElemTraits<T>::T2;
+            const float2 w01 = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv.x));
+            const float2 w23 = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv.y));
+            const float2 w45 = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv.z));
+            const float2 w67 = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv.w));
+#pragma unroll
+            for (int tt = 0; tt < kGemvMaxTok; ++tt) {
+                if (tt < B) {
+                    const float4 o0 = *reinterpret_cast<const float4*>(olat + tt * dc + k);
+                    const float4 o1 = *reinterpret_cast<const float4*>(olat + tt * dc + k + 4);
+                    float a = acc[tt];
+                    a = fmaf(w01.x, o0.x, a); a = fmaf(w01.y, o0.y, a);
+                    a = fmaf(w23.x, o0.z, a); a = fmaf(w23.y, o0.w, a);
+                    a = fmaf(w45.x, o1.x, a); a = fmaf(w45.y, o1.y, a);
+                    a = fmaf(w67.x, o1.z, a); a = fmaf(w67.y, o1.w, a);
+                    acc[tt] = a;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int tt = 0; tt < kGemvMaxTok; ++tt)
+        if (tt < B) qsum[(q * kGemvMaxTok + tt) * dv + j] = acc[tt];
+}
+
 template <typename T, typename R>
 __global__ void __launch_bounds__(32 * kGemvWarps, 1)
 project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
@@ -657,40 +697,7 @@ project_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan
     ok = __syncthreads_and(ok);
     const bool failed = (parts == 0 && status0 != kStatusOk) || !ok;
     // ---- 3. thread (q, j): W_UV row j . latent quarter q, for every token
-    {
-        const int q = threadIdx.x / dv, j = threadIdx.x % dv;   // 4 quarters x 128 rows
-        const int kq = dc / 4;                                   // elements per quarter, a multiple of 16
-        float acc[kGemvMaxTok] = {0.f, 0.f, 0.f, 0.f};
-        if (ok) {
-            for (int c = 0; c < kq / 8; ++c) {
-                const int k = q * kq + 8 * c;
-                // 128-byte-swizzled box row: 16-byte chunk ((k % 64) / 8) ^ (j % 8)
-                const uint4 wv = *reinterpret_cast<const uint4*>(wsm + (k >> 6) * (dv * 128) + j * 128 +
-                                                                 ((((k & 63) >> 3) ^ (j & 7)) << 4));
-                using T2 = typename ElemTraits<T>::T2;
-                const float2 w01 = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv.x));
-                const float2 w23 = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv.y));
-                const float2 w45 = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv.z));
-                const float2 w67 = ElemTraits<T>::to_f2(*reinterpret_cast<const T2*>(&wv.w));
-#pragma unroll
-                for (int tt = 0; tt < kGemvMaxTok; ++tt) {
-                    if (tt < B) {
-                        const float4 o0 = *reinterpret_cast<const float4*>(olat + tt * dc + k);
-                        const float4 o1 = *reinterpret_cast<const float4*>(olat + tt * dc + k + 4);
-                        float a = acc[tt];
-                        a = fmaf(w01.x, o0.x, a); a = fmaf(w01.y, o0.y, a);
-                        a = fmaf(w23.x, o0.z, a); a = fmaf(w23.y, o0.w, a);
-                        a = fmaf(w45.x, o1.x, a); a = fmaf(w45.y, o1.y, a);
-                        a = fmaf(w67.x, o1.z, a); a = fmaf(w67.y, o1.w, a);
-                        acc[tt] = a;
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int tt = 0; tt < kGemvMaxTok; ++tt)
-            if (tt < B) qsum[(q * kGemvMaxTok + tt) * dv + j] = acc[tt];
-    }
+    gemv_w_uv<T>(wsm, olat, qsum, B, dc, dv, ok);
     __syncthreads();
     for (int i = threadIdx.x; i < B * dv; i += blockDim.x) {
         const int tt = i / dv, j = i % dv;
@@ -764,6 +771,212 @@ export_gemv_kernel(const DecodePlan P, const float* __restrict__ rec_ml, const T
         const int hs = P.H / part.slices;
         peer_block_done(sig, h / hs, static_cast<unsigned int>(hs));
     }
+}
+
+// ------------------------------------------------------------------------------------------
+// One-kernel KV-range exchange (gathered form, B <= kGemvMaxTok)
+// ------------------------------------------------------------------------------------------
+constexpr int kLLMaxWorld = 64;
+constexpr unsigned long long kLLWaitNs = 2000000000ull;   // 2 s
+
+__device__ __forceinline__ void st_ll(unsigned char* p, float v0, float v1, int flag) {
+    asm volatile("st.volatile.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(__float_as_uint(v0)), "r"(flag),
+                 "r"(__float_as_uint(v1)), "r"(flag)
+                 : "memory");
+}
+// Spins (bounded) until both flags of the 16-byte unit at p equal `flag`; false when it gives up.
+__device__ __forceinline__ bool ld_ll(const unsigned char* p, int flag, float& v0, float& v1) {
+    const unsigned long long t0 = globaltimer_ns();
+    while (true) {
+        uint32_t a, f0, b, f1;
+        asm volatile("ld.volatile.global.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(a), "=r"(f0), "=r"(b), "=r"(f1)
+                     : "l"(p) : "memory");
+        if (static_cast<int>(f0) == flag && static_cast<int>(f1) == flag) {
+            v0 = __uint_as_float(a);
+            v1 = __uint_as_float(b);
+            return true;
+        }
+        if (globaltimer_ns() - t0 > kLLWaitNs) return false;
+    }
+}
+
+// Block h of every rank: (1) merges the rank's decode records of head h (gemv_merge) into the packed
+// partial [m (natural log), l, 0, 0, o] of each token, (2) stores it into every other rank's ring
+// (NVLink stores) and keeps its own values in registers, (3) reads every other rank's partial of
+// head h from its own ring (a bounded spin per 16-byte unit on the step's flag value), (4) merges the
+// world partials in rank order and (5) projects with W_UV[h] (resident in shared memory, loaded at the
+// start) into out. The last block advances the step counter. One kernel replaces the partial export,
+// the wait and the merge of the gathered exchange; no fence is needed, since every value travels with
+// its step. Every rank merges in rank order with the same code, so all ranks' outputs are equal bit
+// for bit; against the NCCL path (the projection kernel's merge of partial sets) they differ in the
+// last bits, where that merge rounds the log2 conversion differently.
+template <typename T>
+__global__ void __launch_bounds__(32 * kGemvWarps, 1)
+exchange_merge_kernel(const __grid_constant__ CUtensorMap tmap_w, const DecodePlan P, const float* __restrict__ rec_ml,
+                      const T* __restrict__ rec_o, float* __restrict__ out, const LLRing ring) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int dc = P.dc, dv = P.dv, B = P.B, H = P.H;   // dv == 128, dc % 64 == 0, dc <= 512, B <= kGemvMaxTok
+    const int nk = dc / 64, units = (dc + 4) / 2;        // 16-byte units of a ring row
+    unsigned char* wsm = smem;                                                    // nk x (dv rows x 128 B)
+    float* red = reinterpret_cast<float*>(smem + nk * dv * 128);                  // [warp][dc]
+    float2* wml = reinterpret_cast<float2*>(red + kGemvWarps * dc);               // [warp]
+    float* olat = reinterpret_cast<float*>(wml + kGemvWarps);                     // [token][dc]
+    float* qsum = olat + kGemvMaxTok * dc;                                        // [quarter][token][dv]
+    float2* mlp = reinterpret_cast<float2*>(qsum + 4 * kGemvMaxTok * dv);         // [rank][token] (m, l)
+    float* wts = reinterpret_cast<float*>(mlp + kLLMaxWorld * kGemvMaxTok);      // [rank][token] weights
+    float* ltot = wts + kLLMaxWorld * kGemvMaxTok;                                // [token]
+    int* okw = reinterpret_cast<int*>(ltot + kGemvMaxTok);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(okw + 4);
+    const uint32_t w_full = smem_u32(bar);
+    const int h = blockIdx.x;
+    const int wpt = kGemvWarps / B;
+    const int world = ring.world, rank = ring.rank;
+    volatile int* err = P.status;
+
+    if (threadIdx.x == 0) {
+        mbar_init(w_full, 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tmap_w);
+        mbar_arrive_expect_tx(w_full, static_cast<uint32_t>(nk * dv * 128));
+        for (int j = 0; j < nk; ++j) tma_load_2d(smem_u32(wsm) + j * dv * 128, &tmap_w, w_full, 64 * j, h * dv);
+        okw[0] = 1;
+    }
+    const int e = *ring.epoch;   // written last by the previous step's kernel, which has ended
+    const int flag = e + 1;
+    const size_t half = static_cast<size_t>(flag & 1) * ring.half_bytes;
+    // ---- 1. merge of this rank's records
+    const int status0 = gemv_merge<T>(P, rec_ml, rec_o, 0, 2, dc, h, red, wml);
+    __syncthreads();
+    const bool failed = status0 != kStatusOk;
+    // ---- 2. packed partials, unit u = columns 2u, 2u + 1, to every other rank; own values kept
+    constexpr int kOwn = (kGemvMaxTok * 258 + 32 * kGemvWarps - 1) / (32 * kGemvWarps);
+    float own[kOwn][2];
+    {
+        int k = 0;
+        for (int i = threadIdx.x; i < B * units; i += blockDim.x, ++k) {
+            const int tt = i / units, u = i % units;
+            float M = -INFINITY;
+            for (int w = tt * wpt; w < (tt + 1) * wpt; ++w) M = fmaxf(M, wml[w].x);
+            float L = 0.f, o0 = 0.f, o1 = 0.f;
+            const int c = 2 * u - 4;   // latent columns c, c + 1 (u >= 2)
+            if (M != -INFINITY) {
+                for (int w = tt * wpt; w < (tt + 1) * wpt; ++w) {
+                    const float a = wml[w].x == -INFINITY ? 0.f : exp2f(wml[w].x - M);
+                    L = fmaf(a, wml[w].y, L);
+                    if (c >= 0) {
+                        o0 = fmaf(a, red[w * dc + c], o0);
+                        o1 = fmaf(a, red[w * dc + c + 1], o1);
+                    }
+                }
+            }
+            float v0 = o0, v1 = o1;
+            if (u == 0) {
+                const float nan = __int_as_float(0x7fc00000);
+                v0 = failed ? nan : (L > 0.f ? M * kLn2 : -INFINITY);
+                v1 = failed ? nan : L;
+                mlp[rank * kGemvMaxTok + tt] = make_float2(v0, v1);
+            } else if (u == 1) {
+                v0 = v1 = 0.f;
+            }
+            if (k < kOwn) {
+                own[k][0] = v0;
+                own[k][1] = v1;
+            }
+            const size_t off = half + ((static_cast<size_t>(rank) * B + tt) * H + h) * units * 16 + u * 16;
+            for (int q = 0; q < world; ++q)
+                if (q != rank) st_ll(static_cast<unsigned char*>(ring.recv[q]) + off, v0, v1, flag);
+        }
+    }
+    // ---- 3. (m, l) of every other rank's partials: thread p B + t reads unit 0 of row (p, t)
+    const unsigned char* mine = static_cast<const unsigned char*>(ring.recv[rank]) + half;
+    bool ok = true;
+    for (int i = threadIdx.x; i < world * B; i += blockDim.x) {
+        const int p = i / B, tt = i % B;
+        if (p == rank) continue;
+        float m = 0.f, l = 0.f;
+        // after one wait gave up, the thread waits no more (a lost peer costs one bound, not many)
+        if (ok && !ld_ll(mine + ((static_cast<size_t>(p) * B + tt) * H + h) * units * 16, flag, m, l)) ok = false;
+        mlp[p * kGemvMaxTok + tt] = make_float2(m, l);
+    }
+    if (!ok) okw[0] = 0;
+    __syncthreads();
+    ok = okw[0] != 0;
+    // ---- 4. per token: weights of the world partials (rank order), then the merged latent columns
+    if (static_cast<int>(threadIdx.x) < B) {
+        const int tt = threadIdx.x;
+        // m in log2 units, rounded before the subtraction (no contraction into an FMA), so that every
+        // rank weighs the partials alike
+        float Mx = -INFINITY;
+        for (int p = 0; p < world; ++p) {
+            const float2 v = mlp[p * kGemvMaxTok + tt];
+            if (v.y > 0.f) Mx = fmaxf(Mx, __fmul_rn(v.x, 1.4426950408889634f));
+        }
+        float L = 0.f;
+        for (int p = 0; p < world; ++p) {
+            const float2 v = mlp[p * kGemvMaxTok + tt];
+            const float a =
+                (v.y > 0.f && Mx != -INFINITY) ? exp2f(__fmul_rn(v.x, 1.4426950408889634f) - Mx) : 0.f;
+            wts[p * kGemvMaxTok + tt] = a;
+            L = fmaf(a, v.y, L);
+        }
+        ltot[tt] = L;
+    }
+    __syncthreads();
+    {
+        int k = 0;
+        for (int i = threadIdx.x; i < B * units; i += blockDim.x, ++k) {
+            const int tt = i / units, u = i % units;
+            if (u < 2) continue;
+            float o0 = 0.f, o1 = 0.f;
+            for (int p = 0; p < world; ++p) {
+                float v0 = 0.f, v1 = 0.f;
+                if (p == rank) {
+                    if (k < kOwn) {
+                        v0 = own[k][0];
+                        v1 = own[k][1];
+                    }
+                } else if (ok && !ld_ll(mine + ((static_cast<size_t>(p) * B + tt) * H + h) * units * 16 + u * 16, flag,
+                                        v0, v1)) {
+                    ok = false;
+                }
+                const float a = wts[p * kGemvMaxTok + tt];
+                o0 = fmaf(a, v0, o0);
+                o1 = fmaf(a, v1, o1);
+            }
+            const float L = ltot[tt];
+            olat[tt * dc + 2 * u - 4] = L > 0.f ? o0 / L : 0.f;
+            olat[tt * dc + 2 * u - 3] = L > 0.f ? o1 / L : 0.f;
+        }
+    }
+    if (!ok) okw[0] = 0;
+    // W_UV[h] must have landed (thread 0 waits; the block-wide AND carries the result)
+    bool wok = true;
+    if (threadIdx.x == 0) wok = mbar_wait_impl<false, false>(w_full, 0, err, gcode(kSiteProjA), kDefaultWaitNs);
+    wok = __syncthreads_and(wok);
+    const bool ring_ok = okw[0] != 0;
+    if (!ring_ok && threadIdx.x == 0) atomicExch(ring.status, 1);
+    // ---- 5. W_UV projection
+    gemv_w_uv<T>(wsm, olat, qsum, B, dc, dv, wok);
+    __syncthreads();
+    for (int i = threadIdx.x; i < B * dv; i += blockDim.x) {
+        const int tt = i / dv, j = i % dv;
+        float y = __int_as_float(0x7fc00000);   // a failed decode, exchange or wait shows in the output
+        if (wok && ring_ok)
+            y = ((qsum[(0 * kGemvMaxTok + tt) * dv + j] + qsum[(1 * kGemvMaxTok + tt) * dv + j]) +
+                 qsum[(2 * kGemvMaxTok + tt) * dv + j]) + qsum[(3 * kGemvMaxTok + tt) * dv + j];
+        out[(static_cast<long long>(tt) * H + h) * dv + j] = y;
+    }
+    // the step counter moves once every block has read it
+    if (threadIdx.x == 0) {
+        const unsigned int prev = atomicAdd(ring.done, 1u);
+        if (prev + 1u == gridDim.x) {
+            *ring.done = 0u;
+            *ring.epoch = flag;
+        }
+    }
+    // shared memory is not released under a TMA write: if the wait gave up, wait (bounded) again
+    if (threadIdx.x == 0 && !wok) mbar_wait_impl<false, false>(w_full, 0, err, gcode(kSiteProjA), 100000000ull);
 }
 
 bool absorb_sm100_supported(const DecodePlan& P) {
@@ -925,6 +1138,30 @@ cudaError_t launch_export_gemv(const DecodePlan& P, const float* rec_ml, const T
     return e != cudaSuccess ? e : cudaGetLastError();
 }
 
+size_t exchange_merge_smem_bytes(int dc, int dv) {
+    return 1024 + gemv_smem_bytes(dc, dv) + static_cast<size_t>(kLLMaxWorld) * kGemvMaxTok * (sizeof(float2) + 4) +
+           kGemvMaxTok * 4 + 16 + 16;
+}
+
+template <typename T>
+cudaError_t launch_exchange_merge(const DecodePlan& P, const float* rec_ml, const T* rec_o, const T* W_UV,
+                                  float* out, const LLRing& ring, cudaStream_t s) {
+    if (P.B < 1 || P.B > kGemvMaxTok || P.dv != 128 || P.dc % 64 != 0 || P.dc > 512 || ring.world < 1 ||
+        ring.world > kLLMaxWorld || ring.rank < 0 || ring.rank >= ring.world)
+        return cudaErrorInvalidValue;
+    CUtensorMap tmap;
+    if (!make_tmap_2d_16b(&tmap, W_UV, static_cast<uint64_t>(P.H) * P.dv, static_cast<uint64_t>(P.dc),
+                          static_cast<uint64_t>(P.dc), static_cast<uint32_t>(P.dv), 64))
+        return cudaErrorInvalidValue;
+    const size_t smem = exchange_merge_smem_bytes(P.dc, P.dv);
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(exchange_merge_kernel<T>), static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    e = launch_ex(exchange_merge_kernel<T>, dim3(P.H), dim3(32 * kGemvWarps), smem, s, true, tmap, P, rec_ml, rec_o,
+                  out, ring);
+    count_launches(1);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 #define MLA_INST(T)                                                                                              \
     template cudaError_t launch_absorb_sm100<T>(const DecodePlan&, const float*, const T*, const float*, float, T*, \
                                                 int*, cudaStream_t);                                             \
@@ -934,7 +1171,9 @@ cudaError_t launch_export_gemv(const DecodePlan& P, const float* rec_ml, const T
                                                        const T*, float*, const PeerRows&, cudaStream_t,           \
                                                        const int*, size_t);                                         \
     template cudaError_t launch_export_gemv<T>(const DecodePlan&, const float*, const T*, const PartOut&,         \
-                                               const PeerSig&, bool, cudaStream_t);
+                                               const PeerSig&, bool, cudaStream_t);                           \
+    template cudaError_t launch_exchange_merge<T>(const DecodePlan&, const float*, const T*, const T*, float*,    \
+                                                  const LLRing&, cudaStream_t);
 MLA_INST(__half)
 MLA_INST(__nv_bfloat16)
 #undef MLA_INST

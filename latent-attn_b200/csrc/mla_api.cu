@@ -286,7 +286,8 @@ cudaError_t timer_record(cudaEvent_t ev, cudaStream_t s) {
 
 template <typename T>
 mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned char* ws, float* out,
-                        const mla::PartOut& part, const mla::PeerSig& sig, cudaStream_t s) {
+                        const mla::PartOut& part, const mla::PeerSig& sig, cudaStream_t s,
+                        const mla::LLRing* ring = nullptr) {
     mla::DecodePlan d = pl.dp;
     int* prefix = reinterpret_cast<int*>(ws + pl.off_prefix);
     d.tile_prefix = d.uniform_len > 0 ? nullptr : prefix;
@@ -327,7 +328,11 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
         if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(timer)");
         a->timer->recorded = true;
     }
-    if (out && pl.use_gemm_project)
+    if (ring) {
+        if (!pl.use_gemm_project)
+            return fail(MLA_ERR_UNSUPPORTED, "the KV-range exchange needs the tensor-core path (sm_100)");
+        e = mla::launch_exchange_merge<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, *ring, s);
+    } else if (out && pl.use_gemm_project)
         e = mla::launch_project_sm100<T>(d, rec_ml, rec_o, reinterpret_cast<const T*>(a->W_UV), out, true, s);
     else if (!out && pl.use_gemm_project && mla::export_gemv_supported(d, part.gather > 0))
         e = mla::launch_export_gemv<T>(d, rec_ml, rec_o, part, sig, true, s);
@@ -341,7 +346,8 @@ mla_status_t run_decode(const Plan& pl, const mla_decode_args_t* a, unsigned cha
 
 mla_status_t decode_impl(const mla_config_t* cfg, const mla_decode_args_t* a, void* workspace,
                          size_t ws_bytes, float* out, const mla::PartOut& part, cudaStream_t s,
-                         int max_workers = 0, const mla::PeerSig& sig = mla::PeerSig{}) {
+                         int max_workers = 0, const mla::PeerSig& sig = mla::PeerSig{},
+                         const mla::LLRing* ring = nullptr) {
     Plan pl;
     mla_status_t st = make_plan(cfg, a, &pl, max_workers);
     if (st != MLA_OK) return st;
@@ -351,8 +357,8 @@ mla_status_t decode_impl(const mla_config_t* cfg, const mla_decode_args_t* a, vo
     if (ws_bytes < pl.total)
         return fail(MLA_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", ws_bytes, pl.total);
     unsigned char* ws = static_cast<unsigned char*>(workspace);
-    if (a->dtype == MLA_DTYPE_BF16) return run_decode<__nv_bfloat16>(pl, a, ws, out, part, sig, s);
-    return run_decode<__half>(pl, a, ws, out, part, sig, s);
+    if (a->dtype == MLA_DTYPE_BF16) return run_decode<__nv_bfloat16>(pl, a, ws, out, part, sig, s, ring);
+    return run_decode<__half>(pl, a, ws, out, part, sig, s, ring);
 }
 
 // Scratch for the reference-shaped launchers, whose signatures carry no workspace.
@@ -791,6 +797,29 @@ mla_status_t mla_combine_partials_gathered(const mla_config_t* cfg, mla_dtype_t 
     const int row = cfg->kv_lora_rank + 4;
     return combine_impl(cfg, dtype, batch, num_parts, cfg->num_heads, packed, packed + 4, row, row, W_UV, output,
                         reinterpret_cast<cudaStream_t>(stream), mla::PeerRows{}, epoch, parity_bytes / sizeof(float));
+}
+
+mla_status_t mla_decode_kv_range(const mla_config_t* cfg, const mla_decode_args_t* a, int world, int rank,
+                                 void* const* recv, size_t half_bytes, int* epoch, unsigned int* counter, int* status,
+                                 void* workspace, size_t workspace_bytes, mla_stream_t stream) {
+    mla_status_t st = validate_cfg(cfg);
+    if (st != MLA_OK) return st;
+    if (!a) return fail(MLA_ERR_INVALID_ARGUMENT, "args is null");
+    if (!a->output) return fail(MLA_ERR_INVALID_ARGUMENT, "output is null");
+    if (!recv || !epoch || !counter || !status)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "recv, epoch, counter and status must be non-null");
+    if (world < 1 || world > 64 || rank < 0 || rank >= world)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "world must be in [1, 64] and rank in [0, world)");
+    if (a->batch < 1 || a->batch > 4) return fail(MLA_ERR_UNSUPPORTED, "the KV-range exchange takes batch 1 .. 4");
+    if (cfg->v_head_dim != 128 || cfg->kv_lora_rank % 64 != 0 || cfg->kv_lora_rank > 512)
+        return fail(MLA_ERR_UNSUPPORTED, "the KV-range exchange needs v_head_dim 128 and kv_lora_rank a multiple of 64 "
+                                         "up to 512");
+    const size_t need = static_cast<size_t>(world) * a->batch * cfg->num_heads * (cfg->kv_lora_rank + 4) * 8;
+    if (half_bytes % 16 != 0 || half_bytes < need)
+        return fail(MLA_ERR_INVALID_ARGUMENT, "half_bytes must be a multiple of 16 and at least %zu", need);
+    const mla::LLRing ring{recv, half_bytes, world, rank, epoch, counter, status};
+    return decode_impl(cfg, a, workspace, workspace_bytes, a->output, mla::PartOut{},
+                       reinterpret_cast<cudaStream_t>(stream), 0, mla::PeerSig{}, &ring);
 }
 
 mla_status_t mla_ipc_alloc(size_t bytes, void** ptr, void* handle) {

@@ -288,6 +288,20 @@ struct PeerRows {
     PeerSig sig;
 };
 
+// The one-kernel KV-range exchange (B <= 4): every rank's receive area holds two halves (selected
+// by the parity of the step's flag value *epoch + 1), each of world x B x H rows of dc + 4 packed
+// values [m, l, 0, 0, o], stored as 16-byte units {v0, flag, v1, flag} so that a reader sees a value
+// together with the step it belongs to (8-byte halves are written atomically) and needs no separate
+// flag or fence. Sender p's row of token b, head h sits at unit ((p B + b) H + h) (dc + 4) / 2.
+struct LLRing {
+    void* const* recv;   // world pointers: each rank's receive area (two halves of half_bytes)
+    size_t half_bytes;
+    int world, rank;
+    int* epoch;          // this rank's step counter, advanced by the kernel's last block
+    unsigned int* done;  // zeroed block counter of this GPU
+    int* status;         // set to 1 when a wait for a peer's row gives up
+};
+
 // ---- kernel launchers (defined in the .cu files; return cudaGetLastError()) ----
 // pack.cu
 template <typename T>
@@ -321,6 +335,12 @@ cudaError_t launch_project_parts_sm100(int B, int H, int dc, int dv, int parts, 
 // Partial export of a decode's records (one merged partial per (b, h), see PartOut) by the
 // GEMV merge, for B <= gemv_max_tokens(); with part.peer, slice q's receiver is signalled.
 bool export_gemv_supported(const DecodePlan& P, bool gather = false);
+// The one-kernel KV-range exchange after the decode kernel (B <= kGemvMaxTok): merge this rank's
+// records per head, store the packed partials into every rank's LLRing area, wait for every rank's
+// partials of the same head, merge them and project with W_UV into `out` (B, H, dv).
+template <typename T>
+cudaError_t launch_exchange_merge(const DecodePlan& P, const float* rec_ml, const T* rec_o, const T* W_UV,
+                                  float* out, const LLRing& ring, cudaStream_t s);
 template <typename T>
 cudaError_t launch_export_gemv(const DecodePlan& P, const float* rec_ml, const T* rec_o, const PartOut& part,
                                const PeerSig& sig, bool pdl, cudaStream_t s);

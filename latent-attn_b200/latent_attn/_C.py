@@ -517,6 +517,38 @@ def mla_combine_partials_put(packed: torch.Tensor, W_UV_slice: torch.Tensor, d_m
         C.c_void_p(_stream(packed.device))))
 
 
+def mla_decode_kv_range(kv_cache, q_rope, W_UV, rope_cos, rope_sin, d_model, kv_lora_rank, qk_nope_head_dim,
+                        qk_rope_head_dim, num_heads, v_head_dim, *, world: int, rank: int, recv_ptrs: torch.Tensor,
+                        half_bytes: int, epoch: torch.Tensor, counter: torch.Tensor, status: torch.Tensor,
+                        out: torch.Tensor, q_absorbed=None, q_nope=None, W_UK=None, kv_pos_offset: int = 0,
+                        softmax_scale: float = 0.0, workspace=None, kernel: int = 0, timer=None,
+                        rope_theta: float = 0.0) -> torch.Tensor:
+    """``mla_decode_kv_range``: this rank's KV-range step for batch 1 .. 4 with the exchange of per-head
+    partials inside one kernel (stores into every rank's receive area ``recv_ptrs[q]``, two halves of
+    ``half_bytes``), every rank merging and projecting all heads into ``out`` (B, H, dv)."""
+    _check_half(kv_cache, "kv_cache")
+    _check_tables(rope_cos, rope_sin)
+    _check_f32(out, "out")
+    if recv_ptrs.dtype != torch.int64 or not recv_ptrs.is_cuda or recv_ptrs.numel() != world:
+        raise RuntimeError("recv_ptrs must be a CUDA int64 vector of world pointers")
+    for t, name in ((epoch, "epoch"), (counter, "counter"), (status, "status")):
+        if t.dtype != torch.int32 or not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA int32 tensor")
+    cfg = _cfg(d_model, kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, num_heads, v_head_dim)
+    B = q_rope.size(0)
+    L = kv_cache.size(0) // B
+    args = _decode_args(kv_cache.dtype, B, False, kv_cache, L, q_rope, W_UV, rope_cos, rope_sin, out,
+                        q_absorbed=q_absorbed, q_nope=None if q_absorbed is not None else q_nope,
+                        W_UK=None if q_absorbed is not None else W_UK, kv_pos_offset=kv_pos_offset,
+                        softmax_scale=softmax_scale, kernel=kernel, timer=timer, rope_theta=rope_theta)
+    ws = _workspace(cfg, args, kv_cache.device, workspace)
+    _lib.check(_lib.load().mla_decode_kv_range(
+        C.byref(cfg), C.byref(args), int(world), int(rank), C.c_void_p(recv_ptrs.data_ptr()), C.c_size_t(half_bytes),
+        C.c_void_p(epoch.data_ptr()), C.c_void_p(counter.data_ptr()), C.c_void_p(status.data_ptr()),
+        C.c_void_p(ws.data_ptr()), C.c_size_t(ws.numel()), C.c_void_p(_stream(kv_cache.device))))
+    return out
+
+
 def mla_decode_partial_gather(kv_cache, q_rope, W_UV, rope_cos, rope_sin, d_model, kv_lora_rank, qk_nope_head_dim,
                               qk_rope_head_dim, num_heads, v_head_dim, *, dst_ptrs: torch.Tensor, dst_offset: int,
                               parity_bytes: int, signal: "PeerSignal", q_absorbed=None, q_nope=None, W_UK=None,

@@ -112,6 +112,9 @@ SIGNATURES = {
                                             C.c_void_p]),
     "mla_combine_partials_gathered": (C.c_int, [C.POINTER(MlaConfig), C.c_int, C.c_int, C.c_int, C.c_void_p,
                                                 C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "mla_decode_kv_range": (C.c_int, [C.POINTER(MlaConfig), C.POINTER(MlaDecodeArgs), C.c_int, C.c_int, C.c_void_p,
+                                      C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                      C.c_void_p]),
     "mla_peer_wait": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "mla_timer_create": (C.c_int, [C.POINTER(C.c_void_p)]),
     "mla_timer_destroy": (C.c_int, [C.c_void_p]),

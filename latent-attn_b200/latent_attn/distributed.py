@@ -32,12 +32,16 @@ over NVLink, flag their receivers, and a bounded wait kernel orders the next
 kernel after the flags. Flags carry a device-resident step counter, so the
 exchange can be captured in a CUDA graph and replayed.
 
-* Batches up to ``GATHER_MAX_BATCH`` (the long-sequence case) take one exchange:
-  the export kernel stores this rank's partials of every head into every rank's
-  receive area (``mla_decode_partial_gather``, double-buffered by the step
-  counter) and every rank merges and projects all heads itself
-  (``mla_combine_partials_gathered``). The merge of a token costs the same for
-  64 or 128 heads (one block per head), so the output all-gather is saved.
+* Batches up to ``GATHER_MAX_BATCH`` (the long-sequence case) take one exchange
+  inside one kernel (``mla_decode_kv_range``): block h merges this rank's
+  records of head h, stores the partial into every rank's receive area as
+  16-byte units that carry the step number beside each value, reads the other
+  ranks' partials of head h from its own area (a bounded spin on the data
+  itself: no flag, no fence), merges them and projects. Every rank merges all
+  heads: one block per head costs the same for 64 or 128 heads, so the output
+  all-gather is saved. The receive area is double-buffered by step parity.
+  (``mla_decode_partial_gather`` + ``mla_peer_wait`` +
+  ``mla_combine_partials_gathered`` are the same exchange as three kernels.)
 * Larger batches keep the head-sliced pair: ``mla_decode_partial_put`` stores
   each head slice into its owner's receive area, and ``mla_combine_partials_put``
   stores the merged rows into every rank's output area.
@@ -203,6 +207,7 @@ class PeerExchange:
         self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
         self.counters = torch.zeros(2 * self.world, dtype=torch.int32, device=device)
+        self.done = torch.zeros(1, dtype=torch.int32, device=device)   # block counter of the one-kernel exchange
         self.sig_partials = _C.PeerSignal(self.flag_ptrs, self.rank, self.epoch, self.counters[:self.world])
         self.sig_outputs = _C.PeerSignal(self.flag_ptrs, self.world + self.rank, self.epoch,
                                          self.counters[self.world:])
@@ -301,8 +306,8 @@ class KVRangeDecoder:
             if self._peer is not None:
                 self._peer.close()
             R = c.kv_lora_rank + 4
-            if gather:   # every rank's (B, H) rows, double-buffered; no output area
-                self._peer = PeerExchange(B * c.num_heads * R * 4, 0, device, self.group, halves=2)
+            if gather:   # every rank's (B, H) rows as 16-byte {value, step, value, step} units, double-buffered
+                self._peer = PeerExchange(B * c.num_heads * R * 8, 0, device, self.group, halves=2)
             else:
                 self._peer = PeerExchange(B * hs * R * 4, B * world * hs * c.v_head_dim * 4, device, self.group)
             self._peer_key = key
@@ -329,18 +334,17 @@ class KVRangeDecoder:
         rank = dist.get_rank(self.group)
         B, H, dc, dv = q_rope.size(0), c.num_heads, c.kv_lora_rank, c.v_head_dim
         if self.exchange == "p2p" and B <= GATHER_MAX_BATCH:
-            # one exchange: the export kernel stores this rank's partials of every head into every
-            # rank's receive area (NVLink stores), and every rank merges and projects all heads
+            # one exchange inside one kernel: block h stores this rank's partial of head h into every
+            # rank's receive area (NVLink stores carrying the step number), reads the others' partials
+            # of head h from its own area, merges them and projects all heads
             px = self._peers(B, H, world, q_rope.device, True)
-            _C.mla_decode_partial_gather(kv_local, q_rope, W_UV, rope_cos, rope_sin, *dims, dst_ptrs=px.recv_ptrs,
-                                         dst_offset=rank * px.slice_bytes, parity_bytes=px.parity_bytes,
-                                         signal=px.sig_partials, q_absorbed=q_absorbed, q_nope=q_nope, W_UK=W_UK,
-                                         kv_pos_offset=pos_offset, workspace=workspace, timer=timer)
-            px.wait_partials(advance=True)
             if out is None:
                 out = self._get("full", (B, H, dv), q_rope)
-            return _C.mla_combine_partials_gathered(px.recv(), px.parity_bytes, px.epoch, W_UV, *dims, parts=world,
-                                                    batch=B, out=out)
+            return _C.mla_decode_kv_range(kv_local, q_rope, W_UV, rope_cos, rope_sin, *dims, world=world, rank=rank,
+                                          recv_ptrs=px.recv_ptrs, half_bytes=px.parity_bytes, epoch=px.epoch,
+                                          counter=px.done, status=px.status, out=out, q_absorbed=q_absorbed,
+                                          q_nope=q_nope, W_UK=W_UK, kv_pos_offset=pos_offset, workspace=workspace,
+                                          timer=timer)
         if H % world == 0:
             hs = H // world
             W_slice = W_UV[rank * hs * dv:(rank + 1) * hs * dv]

@@ -5,8 +5,13 @@ The put / wait kernels are checked on one GPU (every "rank" a local buffer, the 
 ordered before the waits, so nothing waits on a kernel that runs beside it), including a wait that
 runs out because nothing sets its flag. A one-rank process group checks the decode glue on any GPU
 box; the two-rank cases run when the box has two GPUs, one process per GPU, and compare every
-rank's output with the fp64 oracle of the whole sequence and the two exchanges with each other
-(bit-identical: same kernels, same merge order), eagerly and replayed from a CUDA graph.
+rank's output with the fp64 oracle of the whole sequence and the two exchanges with each other,
+eagerly and replayed from a CUDA graph: bit-identical for the head-sliced form (the same export and
+merge kernels), within 1e-6 for the one-kernel exchange of batches up to 4 (its own merge); every
+rank's output, and every call's, bit-identical.
+
+The one-kernel exchange (mla_decode_kv_range) waits on peers inside the kernel, so it runs only with
+one rank per GPU (or a single rank), never with emulated ranks on one GPU.
 """
 
 import os
@@ -20,7 +25,7 @@ import torch.multiprocessing as mp
 
 from oracle import mla_oracle as O
 from latent_attn import MLAConfig, synthetic
-from latent_attn.distributed import KVRangeDecoder, kv_range
+from latent_attn.distributed import GATHER_MAX_BATCH, KVRangeDecoder, kv_range
 
 pytestmark = pytest.mark.gpu
 
@@ -327,8 +332,12 @@ def _rank_worker(rank, world, port, L, seed, B, q):
     try:
         _, ref = _decode_rank(rank, world, L, seed, "nccl", B)
         _, outs = _decode_rank(rank, world, L, seed, "p2p", B, graph=True)
-        for o in outs:              # same kernels and merge order: the exchanges agree bit for bit
-            np.testing.assert_array_equal(o, ref[-1])
+        for o in outs:
+            if B > GATHER_MAX_BATCH:   # head-sliced: the same export and merge kernels as the NCCL path
+                np.testing.assert_array_equal(o, ref[-1])
+            else:                      # the one-kernel exchange: its own merge, equal to the last bits
+                np.testing.assert_allclose(o, ref[-1], rtol=1e-5, atol=1e-6)
+            np.testing.assert_array_equal(o, outs[0])   # eager calls and graph replays agree bit for bit
         q.put((rank, outs[-1]))
     finally:
         dist.destroy_process_group()
@@ -336,7 +345,7 @@ def _rank_worker(rank, world, port, L, seed, B, q):
 
 def _run_ranks(world, L, B, seed=4):
     """``world`` processes, one per GPU; returns every rank's output of the p2p decoder (each rank has
-    checked it bit-identical to the NCCL exchange)."""
+    checked it against the NCCL exchange)."""
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
