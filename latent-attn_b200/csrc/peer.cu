@@ -1,6 +1,6 @@
 // Peer memory for the multi-GPU exchange: CUDA IPC allocations that the other processes of the
 // node map, and the put / wait kernels that move per-head partials and outputs over NVLink with
-// plain stores (no TMA, no multicast). The flag protocol (per-receiver block counts, a
+// plain stores (no TMA). The flag protocol (per-receiver block counts, a
 // system-scope release store of the step counter, a bounded acquire spin) is in peer.cuh.
 #include <cstdint>
 #include <cstring>
