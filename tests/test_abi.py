@@ -153,6 +153,21 @@ def test_peer_exchange_validation_without_gpu():
                                              None) == _lib.MLA_ERR_INVALID_ARGUMENT        # no step counter
     assert lib.mla_combine_partials_put(C.byref(ok), _lib.DTYPE_BF16, 1, 2, 64, fake, fake, 2, fake, 0, 64,
                                         C.byref(sig), fake, None) == _lib.MLA_ERR_INVALID_ARGUMENT  # pitch < row
+    # the one-kernel KV-range step
+    a.output = 256
+    need = 2 * 1 * 128 * (512 + 4) * 8
+    kvr = lambda args, world=2, rank=0, half=need, recv=fake: lib.mla_decode_kv_range(
+        C.byref(ok), C.byref(args), world, rank, recv, half, fake, fake, fake, fake, 1 << 20, None)
+    assert kvr(a, world=0) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert kvr(a, world=65) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert kvr(a, rank=2) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert kvr(a, recv=None) == _lib.MLA_ERR_INVALID_ARGUMENT
+    assert kvr(a, half=need - 16) == _lib.MLA_ERR_INVALID_ARGUMENT and b"half_bytes" in lib.mla_last_error()
+    assert kvr(a, half=need + 8) == _lib.MLA_ERR_INVALID_ARGUMENT              # not a multiple of 16
+    a.batch = 5
+    assert kvr(a) == _lib.MLA_ERR_UNSUPPORTED and b"batch" in lib.mla_last_error()
+    a.batch, a.output = 1, None
+    assert kvr(a) == _lib.MLA_ERR_INVALID_ARGUMENT
 
 
 def test_cpp_drop_in_headers_compile():
